@@ -1,0 +1,63 @@
+// Shared device helpers and host-side error plumbing for the OpenAttention B200 kernels.
+//
+// Layout conventions used by every kernel in this library (all row-major, contiguous unless a
+// stride argument says otherwise):
+//   D   = 128 (head dimension), G = 4 query heads per KV head, RQ = 32 (QGS rank), RC = 16 (QGC rank)
+//   row r        = b * 32 + h          (one query head of one request)
+//   kv row       = b * 8 + h / 4       (the KV head that query head reads)
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <math.h>
+
+namespace oa {
+
+constexpr int kD = 128;
+constexpr int kG = 4;
+constexpr int kRQ = 32;
+constexpr int kRC = 16;
+constexpr int kHQ = 32;
+constexpr int kHKV = 8;
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ float bf_lo(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf_hi(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Round-to-nearest-even fp32 -> bf16 bits (no NaN inputs occur on these paths; +-inf preserved).
+__device__ __forceinline__ uint16_t f2bf_bits(float x) {
+  return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+}
+__device__ __forceinline__ float bf_round(float x) {
+  return __bfloat162float(__float2bfloat16_rn(x));
+}
+
+// 16-byte read-only streaming load (K/V rows are touched once per row).
+__device__ __forceinline__ uint4 ldg_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+
+}  // namespace oa
+
+// ---------------------------------------------------------------- host error plumbing
+enum {
+  OA_OK = 0,
+  OA_ERR_INVALID = 1,
+  OA_ERR_UNSUPPORTED = 2,
+  OA_ERR_CUDA = 3,
+};
+
+int oa_fail(int code, const char* fmt, ...);
+int oa_check_launch(const char* what);
+
+#define OA_REQUIRE(cond, ...)                      \
+  do {                                             \
+    if (!(cond)) return oa_fail(OA_ERR_INVALID, __VA_ARGS__); \
+  } while (0)
+
+static inline bool oa_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }

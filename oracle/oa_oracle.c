@@ -1,0 +1,772 @@
+/* CPU ORACLE for the OpenAttention decode path -- TEST INFRASTRUCTURE, NOT PRODUCT CODE.
+ *
+ * Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline / reference arm may load this
+ * library, and only as the checker (or as the timed CPU restatement of the reference).  The product
+ * (openattention_b200/) never calls it.
+ *
+ * A plain-C restatement of the reference's per-step algorithm (inference/methods_eager.py
+ * Ours.decode :583-654, with the fused-kernel tie rules of inference/ours_fused.py and
+ * inference/graph_runner.py) and of the per-request build (methods_eager.py Ours.build :505-555,
+ * inference/ours_fastbuild.py :253-304).  Every floating-point operation that feeds an index
+ * decision (QGS scores, codes, centroid distances, ErrorGate scores, water-filling) is written as
+ * one fixed sequence of IEEE operations; the CUDA kernels perform the identical sequence, so
+ * selected / expanded index sets, quotas, codes and cluster assignments must agree bit for bit.
+ * Compile with -ffp-contract=off (no FMA contraction other than the explicit fmaf calls).
+ *
+ * Transcendentals (ln, exp, erf) are this file's own double-precision series (not libm), rounded
+ * to fp32 once, so the GPU side can reproduce them exactly:
+ *   ln(x)  = e*ln2 + 2*atanh(s), s = (m-1)/(m+1), m in [sqrt(1/2), sqrt(2)), 13-term odd series
+ *   exp(x) = 2^k * exp(r), r = x - k*ln2 (Cody-Waite split), 17-term Taylor series
+ *   erf(x) = 2/sqrt(pi) * exp(-x^2) * sum_n (2x^2)^n x / (1*3*...*(2n+1))   (all-positive series,
+ *            Abramowitz & Stegun 7.1.6), 1 for x >= 6.
+ *
+ * Layouts (contiguous): row r = b*32 + h, kv row = b*8 + h/4, D = 128.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define D 128
+#define HQ 32
+#define HKV 8
+#define G 4
+#define RQ 32
+#define RC 16
+
+/* ------------------------------------------------------------------ bf16 helpers */
+static inline float bf2f(uint16_t b) {
+  uint32_t u = (uint32_t)b << 16;
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+static inline uint16_t f2bf(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0;
+  u += 0x7fffu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+static inline float bfr(float f) { return bf2f(f2bf(f)); }
+
+/* ------------------------------------------------------------------ own transcendental functions */
+static const double LN2_D = 0.69314718055994530942;
+static const double LN2_HI = 6.93147180369123816490e-01; /* high part, trailing zeros */
+static const double LN2_LO = 1.90821492927058770002e-10;
+static const double LOG2E_D = 1.44269504088896338700;
+
+static double pow2i(int k) { /* exact 2^k for -1022 <= k <= 1023 */
+  uint64_t bits = (uint64_t)(k + 1023) << 52;
+  double d;
+  memcpy(&d, &bits, 8);
+  return d;
+}
+
+double oro_ln_d(double x) { /* x > 0, normal */
+  uint64_t bits;
+  memcpy(&bits, &x, 8);
+  int e = (int)((bits >> 52) & 0x7ff) - 1022;
+  bits = (bits & 0x000fffffffffffffull) | 0x3fe0000000000000ull; /* m in [0.5, 1) */
+  double m;
+  memcpy(&m, &bits, 8);
+  if (m < 0.70710678118654752440) {
+    m = m * 2.0;
+    e = e - 1;
+  }
+  double s = (m - 1.0) / (m + 1.0);
+  double s2 = s * s;
+  double term = s, sum = s;
+  for (int k = 1; k <= 13; ++k) {
+    term = term * s2;
+    sum = sum + term / (double)(2 * k + 1);
+  }
+  double a = 2.0 * sum;
+  double b = (double)e * LN2_D;
+  return a + b;
+}
+
+double oro_exp_d(double x) {
+  if (x < -745.0) return 0.0;
+  if (x > 709.0) return INFINITY;
+  double k = nearbyint(x * LOG2E_D);
+  double t1 = k * LN2_HI;
+  double t2 = k * LN2_LO;
+  double r = (x - t1) - t2;
+  double p = 1.0, term = 1.0;
+  for (int i = 1; i <= 17; ++i) {
+    term = term * r;
+    term = term / (double)i;
+    p = p + term;
+  }
+  int ki = (int)k;
+  if (ki < -1022) return 0.0;
+  return p * pow2i(ki);
+}
+
+double oro_erf_d(double x) { /* x >= 0 */
+  if (x >= 6.0) return 1.0;
+  double x2 = x * x;
+  double tx2 = 2.0 * x2;
+  double term = x, sum = x;
+  for (int n = 1; n < 400; ++n) {
+    term = term * tx2;
+    term = term / (double)(2 * n + 1);
+    sum = sum + term;
+    if (term < sum * 1e-17) break;
+  }
+  double c = 1.1283791670955126 * oro_exp_d(-x2);
+  return c * sum;
+}
+
+float oro_logf(float x) { return (float)oro_ln_d((double)x); }
+float oro_expf(float x) {
+  if (x == -INFINITY) return 0.0f;
+  return (float)oro_exp_d((double)x);
+}
+float oro_erff(float x) { return (float)oro_erf_d((double)x); }
+
+/* ------------------------------------------------------------------ decode: index update */
+/* New token at position pos of every request: QGS code (per KV head), nearest QGC centroid (per
+ * query head, ties -> lower id), n_b += 1, Sk += k, Sk2 += k*k, Sv += v, generated-token list append.
+ * Restates ours_graph._k_index_update_d2 (inference/ours_graph.py:43-90) / methods_eager.py:586-601. */
+void oro_index_update(int B, int Lmax, int C, int pos, const uint16_t* K, const uint16_t* V, int8_t* codes,
+                      const float* U, const float* scale, const uint16_t* W, const float* colmean,
+                      const float* cent, int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv,
+                      int32_t* reclist, int32_t* reccnt, int rmax) {
+  for (int kv = 0; kv < B * HKV; ++kv) {
+    const uint16_t* kr = K + ((int64_t)kv * Lmax + pos) * D;
+    const uint16_t* vr = V + ((int64_t)kv * Lmax + pos) * D;
+    float kf[D], vf[D];
+    for (int d = 0; d < D; ++d) {
+      kf[d] = bf2f(kr[d]);
+      vf[d] = bf2f(vr[d]);
+    }
+    const float* Uk = U + (int64_t)kv * D * RQ;
+    for (int j = 0; j < RQ; ++j) {
+      float acc = 0.0f;
+      for (int d = 0; d < D; ++d) acc = fmaf(kf[d], Uk[d * RQ + j], acc);
+      float c = rintf(acc / scale[kv * RQ + j]);
+      c = fminf(fmaxf(c, -127.0f), 127.0f);
+      codes[((int64_t)kv * Lmax + pos) * RQ + j] = (int8_t)c;
+    }
+    for (int g = 0; g < G; ++g) {
+      const int r = kv * G + g;
+      const uint16_t* Wr = W + (int64_t)r * D * RC;
+      float zp[RC];
+      for (int c = 0; c < RC; ++c) {
+        float acc = 0.0f;
+        for (int d = 0; d < D; ++d) acc = fmaf(kf[d], bf2f(Wr[d * RC + c]), acc);
+        zp[c] = bfr(acc) - colmean[r * RC + c];
+      }
+      const float* ce = cent + (int64_t)r * C * RC;
+      int best = 0;
+      float bestv = -INFINITY;
+      for (int i = 0; i < C; ++i) {
+        float dot = 0.0f, nrm = 0.0f;
+        for (int c = 0; c < RC; ++c) {
+          dot = fmaf(zp[c], ce[i * RC + c], dot);
+          nrm = fmaf(ce[i * RC + c], ce[i * RC + c], nrm);
+        }
+        float dist = dot - 0.5f * nrm;
+        if (dist > bestv) {
+          bestv = dist;
+          best = i;
+        }
+      }
+      asg[(int64_t)r * Lmax + pos] = best;
+      nb[r * C + best] += 1.0f;
+      float* sk = Sk + ((int64_t)r * C + best) * D;
+      float* sk2 = Sk2 + ((int64_t)r * C + best) * D;
+      float* sv = Sv + ((int64_t)r * C + best) * D;
+      for (int d = 0; d < D; ++d) {
+        sk[d] = sk[d] + kf[d];
+        float kk = kf[d] * kf[d];
+        sk2[d] = sk2[d] + kk;
+        sv[d] = sv[d] + vf[d];
+      }
+      if (reclist) {
+        int cnt = reccnt[r * C + best];
+        if (cnt < rmax) reclist[((int64_t)r * C + best) * rmax + cnt] = pos;
+        reccnt[r * C + best] = cnt + 1;
+      }
+    }
+  }
+}
+
+/* zq[r, j] = bf16((q_r . U[:, j]) * scale_j), U of the row's KV head (methods_eager.py:603). */
+void oro_zq(int B, const uint16_t* q, const float* U, const float* scale, uint16_t* zq) {
+  for (int r = 0; r < B * HQ; ++r) {
+    const int kv = r / G;
+    float qf[D];
+    for (int d = 0; d < D; ++d) qf[d] = bf2f(q[(int64_t)r * D + d]);
+    for (int j = 0; j < RQ; ++j) {
+      float acc = 0.0f;
+      for (int d = 0; d < D; ++d) acc = fmaf(qf[d], U[((int64_t)kv * D + d) * RQ + j], acc);
+      float z = acc * scale[kv * RQ + j];
+      zq[r * RQ + j] = f2bf(z);
+    }
+  }
+}
+
+/* QGS scores s[r, t] = bf16(sum_j code[t, j] * zq[r, j]) (j ascending), -inf for t < ns and
+ * t >= n - nl.  Restates _k_qgs_scan_tm (inference/graph_runner.py:100-120). s: (R, sw) bf16 bits. */
+void oro_scan(int B, int Lmax, int n, int ns, int nl, const int8_t* codes, const uint16_t* zq, uint16_t* s,
+              int64_t sw) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < B * HQ; ++r) {
+    const int kv = r / G;
+    float z[RQ];
+    for (int j = 0; j < RQ; ++j) z[j] = bf2f(zq[r * RQ + j]);
+    const int8_t* cr = codes + (int64_t)kv * Lmax * RQ;
+    uint16_t* sr = s + (int64_t)r * sw;
+    for (int t = 0; t < n; ++t) {
+      float acc = 0.0f;
+      const int8_t* c = cr + (int64_t)t * RQ;
+      for (int j = 0; j < RQ; ++j) acc = fmaf((float)c[j], z[j], acc);
+      uint16_t v = f2bf(acc);
+      if (t < ns || t >= n - nl) v = 0xff80; /* -inf */
+      sr[t] = v;
+    }
+  }
+}
+
+/* orderable 16-bit key of a bf16 score: larger score -> larger key */
+static inline uint32_t ukey16(uint16_t b) { return (b & 0x8000u) ? (uint32_t)(~b & 0xffffu) : (uint32_t)(b | 0x8000u); }
+
+/* Row top-k by (score desc, position asc); sel = [0..ns-1, n-nl..n-1, top (in rank order)]; the
+ * selected scores are then set to -inf.  Restates _k_select (inference/graph_runner.py:123-159). */
+void oro_select(int R, int n, int ns, int nl, int k_top, uint16_t* s, int64_t sw, int32_t* sel) {
+  const int NS = ns + nl + k_top;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < R; ++r) {
+    uint16_t* sr = s + (int64_t)r * sw;
+    int32_t* o = sel + (int64_t)r * NS;
+    for (int i = 0; i < ns; ++i) o[i] = i;
+    for (int i = 0; i < nl; ++i) o[ns + i] = n - nl + i;
+    /* insertion into a sorted top list (k_top is small) */
+    int32_t* top = o + ns + nl;
+    uint32_t tk[4096];
+    if (k_top > 4096) k_top = 4096;
+    int cnt = 0;
+    for (int t = 0; t < n; ++t) {
+      uint32_t key = ukey16(sr[t]);
+      if (cnt == k_top && key <= tk[cnt - 1]) continue; /* ties keep the lower position */
+      int p = cnt < k_top ? cnt : k_top - 1;
+      while (p > 0 && tk[p - 1] < key) {
+        tk[p] = tk[p - 1];
+        top[p] = top[p - 1];
+        --p;
+      }
+      tk[p] = key;
+      top[p] = t;
+      if (cnt < k_top) ++cnt;
+    }
+    for (int i = 0; i < k_top; ++i) sr[top[i]] = 0xff80;
+  }
+}
+
+/* ErrorGate wl1 (inference/ours_fused.py:122-154, methods_eager.py:613-627).  Per row: tail sums
+ * (pooled sums minus the selected tokens, in sel order), then per cluster
+ *   kbar = Skt*inv, var = max(Sk2t*inv - kbar*kbar, 0), inv = 1/max(nt,1)
+ *   zbar = SC * sum_d q_d kbar_d,  s2 = SC^2 * sum_d (q_d q_d) var_d   (d ascending, fmaf)
+ *   score = ((zbar + ln max(nt,1)) + 0.5 s2) + ln max(erf(sqrt(s2)*0.70710677), 1e-30). */
+void oro_errorgate(int B, int Lmax, int C, int NS, const uint16_t* q, const uint16_t* K, const int32_t* asg,
+                   const int32_t* sel, const float* Sk, const float* Sk2, const float* nb, float* score, float* nt) {
+  const float SCf = 0.08838834764831845f;
+  const float SC2f = 0.0078125f;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < B * HQ; ++r) {
+    const int kv = r / G;
+    float* skt = (float*)malloc(sizeof(float) * C * D);
+    float* sk2t = (float*)malloc(sizeof(float) * C * D);
+    memcpy(skt, Sk + (int64_t)r * C * D, sizeof(float) * C * D);
+    memcpy(sk2t, Sk2 + (int64_t)r * C * D, sizeof(float) * C * D);
+    float* ntr = nt + (int64_t)r * C;
+    for (int c = 0; c < C; ++c) ntr[c] = nb[(int64_t)r * C + c];
+    for (int j = 0; j < NS; ++j) {
+      const int t = sel[(int64_t)r * NS + j];
+      const int c = asg[(int64_t)r * Lmax + t];
+      const uint16_t* kr = K + ((int64_t)kv * Lmax + t) * D;
+      for (int d = 0; d < D; ++d) {
+        float kf = bf2f(kr[d]);
+        skt[c * D + d] = skt[c * D + d] - kf;
+        float kk = kf * kf;
+        sk2t[c * D + d] = sk2t[c * D + d] - kk;
+      }
+      ntr[c] = ntr[c] - 1.0f;
+    }
+    float qf[D], q2[D];
+    for (int d = 0; d < D; ++d) {
+      qf[d] = bf2f(q[(int64_t)r * D + d]);
+      q2[d] = qf[d] * qf[d];
+    }
+    for (int c = 0; c < C; ++c) {
+      const float inv = 1.0f / fmaxf(ntr[c], 1.0f);
+      float zd = 0.0f, sd = 0.0f;
+      for (int d = 0; d < D; ++d) {
+        float kb = skt[c * D + d] * inv;
+        float p1 = sk2t[c * D + d] * inv;
+        float p2 = kb * kb;
+        float var = fmaxf(p1 - p2, 0.0f);
+        zd = fmaf(qf[d], kb, zd);
+        sd = fmaf(q2[d], var, sd);
+      }
+      float zbar = SCf * zd;
+      float s2 = SC2f * sd;
+      float lg = oro_logf(fmaxf(ntr[c], 1.0f));
+      float er = oro_erff(sqrtf(s2) * 0.70710677f);
+      float le = oro_logf(fmaxf(er, 1e-30f));
+      float hs = 0.5f * s2;
+      float sc = zbar + lg;
+      sc = sc + hs;
+      sc = sc + le;
+      score[(int64_t)r * C + c] = sc;
+    }
+    free(skt);
+    free(sk2t);
+  }
+}
+
+/* Hierarchical water-filling (inference/ours_fused.py:158-216 = methods_eager.py Ours.hier_quota
+ * :558-581).  Sorts by (ratio asc, cluster asc) and (score desc, cluster asc); suffix sums of the
+ * weights accumulate in double from the end (as torch's CPU cumsum does for fp32). */
+void oro_waterfill(int R, int C, float E, const float* score, const float* nt, float* quota) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < R; ++r) {
+    const float* sc = score + (int64_t)r * C;
+    const float* n_t = nt + (int64_t)r * C;
+    float* qo = quota + (int64_t)r * C;
+    float s[256], w[256], cap[256], ratio[256], qb[256];
+    int o[256], o2[256];
+    float smax = -INFINITY;
+    int any = 0;
+    for (int c = 0; c < C; ++c) {
+      int live = n_t[c] > 1.0f;
+      s[c] = live ? sc[c] : -INFINITY;
+      if (live) any = 1;
+      if (s[c] > smax) smax = s[c];
+    }
+    float tot = 0.0f;
+    for (int c = 0; c < C; ++c) {
+      int live = n_t[c] > 1.0f;
+      w[c] = live ? oro_expf(s[c] - smax) : 0.0f;
+      cap[c] = live ? n_t[c] : 0.0f;
+      tot = tot + cap[c];
+      ratio[c] = w[c] > 0.0f ? cap[c] / fmaxf(w[c], 1e-30f) : INFINITY;
+    }
+    (void)any;
+    /* stable insertion sort by ratio asc (index order kept among equal ratios) */
+    for (int c = 0; c < C; ++c) {
+      int p = c;
+      while (p > 0 && ratio[o[p - 1]] > ratio[c]) {
+        o[p] = o[p - 1];
+        --p;
+      }
+      o[p] = c;
+    }
+    float c_ex[256], w_suf[256];
+    float run = 0.0f;
+    for (int j = 0; j < C; ++j) {
+      c_ex[j] = run;
+      run = run + cap[o[j]];
+    }
+    double acc = 0.0;
+    for (int j = C - 1; j >= 0; --j) {
+      acc = acc + (double)w[o[j]];
+      w_suf[j] = (float)acc;
+    }
+    int jj = -1;
+    for (int j = 0; j < C; ++j) {
+      float f;
+      if (w_suf[j] > 0.0f) {
+        float prod = ratio[o[j]] * w_suf[j];
+        f = c_ex[j] + prod;
+      } else {
+        f = INFINITY;
+      }
+      if (f >= E) {
+        jj = j;
+        break;
+      }
+    }
+    if (jj < 0) jj = 0;
+    const float lam = (E - c_ex[jj]) / fmaxf(w_suf[jj], 1e-30f);
+    float sumq = 0.0f;
+    for (int c = 0; c < C; ++c) {
+      float lw = lam * w[c];
+      qb[c] = fminf(cap[c], floorf(lw));
+      if (tot <= E) qb[c] = cap[c];
+      sumq = sumq + qb[c];
+    }
+    float rem = fmaxf(fminf(tot, E) - sumq, 0.0f);
+    /* leftover: score desc, cluster asc */
+    for (int c = 0; c < C; ++c) {
+      int p = c;
+      while (p > 0 && s[o2[p - 1]] < s[c]) {
+        o2[p] = o2[p - 1];
+        --p;
+      }
+      o2[p] = c;
+    }
+    int given = 0;
+    for (int i = 0; i < C; ++i) {
+      const int c = o2[i];
+      float add = 0.0f;
+      if (qb[c] < cap[c]) {
+        if ((float)given < rem) add = 1.0f;
+        ++given;
+      }
+      qo[c] = qb[c] + add;
+    }
+  }
+}
+
+/* Within-cluster top-q (inference/ours_graph.py:93-166, ours_fused.py:220-363): for each cluster c
+ * with quota q > 0, its members (prefix tokens t < n0 and generated tokens n0 <= t < n with
+ * asg == c) ranked by (score desc, position asc); the first q are written to
+ * exp[r, base_c : base_c + q] in ascending position, base_c = sum of the quotas of clusters < c.
+ * Unused slots are -1. */
+void oro_topq(int R, int Lmax, int C, int E, int n, const uint16_t* s, int64_t sw, const int32_t* asg,
+              const float* quota, int32_t* exp_idx) {
+#pragma omp parallel for schedule(dynamic, 4)
+  for (int r = 0; r < R; ++r) {
+    const uint16_t* sr = s + (int64_t)r * sw;
+    const int32_t* ar = asg + (int64_t)r * Lmax;
+    const float* qr = quota + (int64_t)r * C;
+    int32_t* er = exp_idx + (int64_t)r * E;
+    for (int i = 0; i < E; ++i) er[i] = -1;
+    /* bucket the row's tokens by cluster, each bucket in ascending position */
+    int32_t* start = (int32_t*)calloc((size_t)C + 1, sizeof(int32_t));
+    int32_t* fill = (int32_t*)calloc((size_t)C, sizeof(int32_t));
+    int32_t* tok = (int32_t*)malloc(sizeof(int32_t) * (size_t)(n > 0 ? n : 1));
+    for (int t = 0; t < n; ++t) start[ar[t] + 1]++;
+    for (int c = 0; c < C; ++c) start[c + 1] += start[c];
+    for (int t = 0; t < n; ++t) {
+      const int c = ar[t];
+      tok[start[c] + fill[c]++] = t;
+    }
+    int base = 0;
+    for (int c = 0; c < C; ++c) {
+      const int q = (int)qr[c];
+      if (q <= 0) continue;
+      const int32_t* mt = tok + start[c];
+      const int m = start[c + 1] - start[c];
+      /* two 8-bit radix passes find the threshold key T (the q-th largest) */
+      int hist[256];
+      memset(hist, 0, sizeof(hist));
+      for (int i = 0; i < m; ++i) hist[ukey16(sr[mt[i]]) >> 8]++;
+      int above = 0, hi = 0;
+      for (int b = 255; b >= 0; --b) {
+        if (above + hist[b] >= q) {
+          hi = b;
+          break;
+        }
+        above += hist[b];
+      }
+      memset(hist, 0, sizeof(hist));
+      for (int i = 0; i < m; ++i) {
+        const uint32_t k = ukey16(sr[mt[i]]);
+        if ((int)(k >> 8) == hi) hist[k & 255]++;
+      }
+      int lo = 0;
+      for (int b = 255; b >= 0; --b) {
+        if (above + hist[b] >= q) {
+          lo = b;
+          break;
+        }
+        above += hist[b];
+      }
+      const uint32_t T = ((uint32_t)hi << 8) | (uint32_t)lo;
+      int need = q - above, w = 0;
+      for (int i = 0; i < m && w < q; ++i) {
+        const uint32_t k = ukey16(sr[mt[i]]);
+        if (k > T || (k == T && need > 0)) {
+          if (k == T) --need;
+          if (base + w < E) er[base + w] = mt[i];
+          ++w;
+        }
+      }
+      base += q;
+    }
+    free(start);
+    free(fill);
+    free(tok);
+  }
+}
+
+/* Residual proxies (inference/ours_fused.py:367-407, methods_eager.py:641-652): pooled sums minus
+ * every token read (sel in order, then exp slots in order; -1 slots skipped), n' = nt - quota,
+ * kbar' = bf16(Skr/max(n',1)), vbar' = bf16(Svr/max(n',1)), log n' = ln max(n',1) if n' > 0.5 else -inf. */
+void oro_residual(int B, int Lmax, int C, int NS, int E, const uint16_t* K, const uint16_t* V, const int32_t* asg,
+                  const int32_t* sel, const int32_t* exp_idx, const float* Sk, const float* Sv, const float* nt,
+                  const float* quota, uint16_t* kbar, uint16_t* vbar, float* logn) {
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < B * HQ; ++r) {
+    const int kv = r / G;
+    float* skr = (float*)malloc(sizeof(float) * C * D);
+    float* svr = (float*)malloc(sizeof(float) * C * D);
+    memcpy(skr, Sk + (int64_t)r * C * D, sizeof(float) * C * D);
+    memcpy(svr, Sv + (int64_t)r * C * D, sizeof(float) * C * D);
+    for (int j = 0; j < NS + E; ++j) {
+      const int t = j < NS ? sel[(int64_t)r * NS + j] : exp_idx[(int64_t)r * E + (j - NS)];
+      if (t < 0) continue;
+      const int c = asg[(int64_t)r * Lmax + t];
+      const uint16_t* kr = K + ((int64_t)kv * Lmax + t) * D;
+      const uint16_t* vr = V + ((int64_t)kv * Lmax + t) * D;
+      for (int d = 0; d < D; ++d) {
+        skr[c * D + d] = skr[c * D + d] - bf2f(kr[d]);
+        svr[c * D + d] = svr[c * D + d] - bf2f(vr[d]);
+      }
+    }
+    for (int c = 0; c < C; ++c) {
+      const float nr = nt[(int64_t)r * C + c] - quota[(int64_t)r * C + c];
+      const float inv = 1.0f / fmaxf(nr, 1.0f);
+      for (int d = 0; d < D; ++d) {
+        kbar[((int64_t)r * C + c) * D + d] = f2bf(skr[c * D + d] * inv);
+        vbar[((int64_t)r * C + c) * D + d] = f2bf(svr[c * D + d] * inv);
+      }
+      logn[(int64_t)r * C + c] = nr > 0.5f ? oro_logf(fmaxf(nr, 1.0f)) : -INFINITY;
+    }
+    free(skr);
+    free(svr);
+  }
+}
+
+/* OpenAttention.flash in double precision (the fp32 estimator of methods_eager.selftest :708-719):
+ * softmax over valid tokens (q.k*sm) and proxies (q.kbar*sm + ln n) against their values.
+ * prow_div = 1: proxies per query row; = G (BQ/BH): per KV head.  out: (BQ, D) double. */
+void oro_flash(int BQ, int BH, int64_t Kdim, int n_sel, int n_exp, int NB, int prow_div, const uint16_t* q,
+               const uint16_t* k, const uint16_t* v, const int32_t* sel, const int32_t* exp_idx,
+               const uint16_t* kbar, const uint16_t* vbar, const float* logn, double sm_scale, double* out) {
+  const int Gq = BQ / BH;
+#pragma omp parallel for schedule(static)
+  for (int r = 0; r < BQ; ++r) {
+    const int kvh = r / Gq;
+    const int prow = r / prow_div;
+    double qd[D];
+    for (int d = 0; d < D; ++d) qd[d] = bf2f(q[(int64_t)r * D + d]);
+    const int tot = n_sel + n_exp + NB;
+    double* z = (double*)malloc(sizeof(double) * (tot > 0 ? tot : 1));
+    double m = -INFINITY;
+    for (int j = 0; j < tot; ++j) {
+      z[j] = -INFINITY;
+      if (j < n_sel + n_exp) {
+        int t = j < n_sel ? sel[(int64_t)r * n_sel + j] : exp_idx[(int64_t)r * n_exp + j - n_sel];
+        if (t < 0 || t >= Kdim) continue;
+        const uint16_t* kr = k + ((int64_t)kvh * Kdim + t) * D;
+        double dot = 0;
+        for (int d = 0; d < D; ++d) dot += qd[d] * (double)bf2f(kr[d]);
+        z[j] = dot * sm_scale;
+      } else {
+        int b = j - n_sel - n_exp;
+        double ln = logn[(int64_t)r * NB + b];
+        if (ln == -INFINITY) continue;
+        const uint16_t* kr = kbar + ((int64_t)prow * NB + b) * D;
+        double dot = 0;
+        for (int d = 0; d < D; ++d) dot += qd[d] * (double)bf2f(kr[d]);
+        z[j] = dot * sm_scale + ln;
+      }
+      if (z[j] > m) m = z[j];
+    }
+    double l = 0, acc[D];
+    for (int d = 0; d < D; ++d) acc[d] = 0;
+    if (m > -INFINITY) {
+      for (int j = 0; j < tot; ++j) {
+        if (z[j] == -INFINITY) continue;
+        double p = exp(z[j] - m);
+        l += p;
+        const uint16_t* vr;
+        if (j < n_sel + n_exp) {
+          int t = j < n_sel ? sel[(int64_t)r * n_sel + j] : exp_idx[(int64_t)r * n_exp + j - n_sel];
+          vr = v + ((int64_t)kvh * Kdim + t) * D;
+        } else {
+          vr = vbar + ((int64_t)prow * NB + (j - n_sel - n_exp)) * D;
+        }
+        for (int d = 0; d < D; ++d) acc[d] += p * (double)bf2f(vr[d]);
+      }
+    }
+    for (int d = 0; d < D; ++d) out[(int64_t)r * D + d] = l > 0 ? acc[d] / l : 0.0;
+    free(z);
+  }
+}
+
+/* ------------------------------------------------------------------ per-request build */
+/* QGS codes of one request: z[h,t,j] = sum_d k.U (d ascending, fmaf), scale_j = max(amax_t |z| / 127,
+ * 1e-12), code = clamp(rint(z / scale), +-127).  (methods_eager.py:520-524, ours_fastbuild.py:257-260)
+ * K: (8, Lmax, D) bf16 of the request, U: (8, D, 32), scale: (8, 32), codes: (8, Lmax, 32). */
+void oro_build_codes(int T, int Lmax, const uint16_t* K, const float* U, float* scale, int8_t* codes) {
+#pragma omp parallel for schedule(static)
+  for (int h = 0; h < HKV; ++h) {
+    float* z = (float*)malloc(sizeof(float) * (size_t)T * RQ);
+    const float* Uh = U + (int64_t)h * D * RQ;
+    float amax[RQ];
+    for (int j = 0; j < RQ; ++j) amax[j] = 0.0f;
+    for (int t = 0; t < T; ++t) {
+      const uint16_t* kr = K + ((int64_t)h * Lmax + t) * D;
+      float kf[D];
+      for (int d = 0; d < D; ++d) kf[d] = bf2f(kr[d]);
+      for (int j = 0; j < RQ; ++j) {
+        float acc = 0.0f;
+        for (int d = 0; d < D; ++d) acc = fmaf(kf[d], Uh[d * RQ + j], acc);
+        z[(int64_t)t * RQ + j] = acc;
+        float a = fabsf(acc);
+        if (a > amax[j]) amax[j] = a;
+      }
+    }
+    for (int j = 0; j < RQ; ++j) scale[h * RQ + j] = fmaxf(amax[j] / 127.0f, 1e-12f);
+    for (int t = 0; t < T; ++t)
+      for (int j = 0; j < RQ; ++j) {
+        float c = rintf(z[(int64_t)t * RQ + j] / scale[h * RQ + j]);
+        c = fminf(fmaxf(c, -127.0f), 127.0f);
+        codes[((int64_t)h * Lmax + t) * RQ + j] = (int8_t)c;
+      }
+    free(z);
+  }
+}
+
+/* QGC projection of one request: zp[h,t,c] = bf16(sum_d k.W (d ascending, fmaf)) per query head h
+ * (K row h/4), colmean = (float)(sum_t zp / T) with the sum in double, sequential over tiles of 256
+ * tokens; zP = zp - colmean.  (methods_eager.py:529-532)  W: (32, D, 16) bf16, zP: (32, T, 16). */
+void oro_project(int T, int Lmax, const uint16_t* K, const uint16_t* W, float* zP, float* colmean) {
+#pragma omp parallel for schedule(static)
+  for (int h = 0; h < HQ; ++h) {
+    const uint16_t* Wh = W + (int64_t)h * D * RC;
+    float wf[D * RC];
+    for (int i = 0; i < D * RC; ++i) wf[i] = bf2f(Wh[i]);
+    double sum[RC];
+    for (int c = 0; c < RC; ++c) sum[c] = 0.0;
+    for (int t0 = 0; t0 < T; t0 += 256) {
+      double part[RC];
+      for (int c = 0; c < RC; ++c) part[c] = 0.0;
+      for (int t = t0; t < T && t < t0 + 256; ++t) {
+        const uint16_t* kr = K + ((int64_t)(h / G) * Lmax + t) * D;
+        float kf[D];
+        for (int d = 0; d < D; ++d) kf[d] = bf2f(kr[d]);
+        for (int c = 0; c < RC; ++c) {
+          float acc = 0.0f;
+          for (int d = 0; d < D; ++d) acc = fmaf(kf[d], wf[d * RC + c], acc);
+          float zb = bfr(acc);
+          zP[((int64_t)h * T + t) * RC + c] = zb;
+          part[c] = part[c] + (double)zb;
+        }
+      }
+      for (int c = 0; c < RC; ++c) sum[c] = sum[c] + part[c];
+    }
+    for (int c = 0; c < RC; ++c) colmean[h * RC + c] = (float)(sum[c] / (double)T);
+    for (int t = 0; t < T; ++t)
+      for (int c = 0; c < RC; ++c) {
+        float* p = &zP[((int64_t)h * T + t) * RC + c];
+        *p = *p - colmean[h * RC + c];
+      }
+  }
+}
+
+/* One Lloyd assignment for all 32 query heads of a request: dist = bf16(bf16(zb.cb) - half),
+ * zb = bf16(zP), cb = bf16(cent), half = bf16(0.5 * sum_c cent_c^2); argmax, ties -> lower id.
+ * (methods_eager.py:538-542, ours_fastbuild.py:52-82) */
+void oro_kmeans_assign(int T, int C, const float* zP, const float* cent, int32_t* asg, int64_t asg_stride) {
+#pragma omp parallel for schedule(static)
+  for (int h = 0; h < HQ; ++h) {
+    float* cb = (float*)malloc(sizeof(float) * C * RC);
+    float* half = (float*)malloc(sizeof(float) * C);
+    for (int i = 0; i < C; ++i) {
+      float nrm = 0.0f;
+      for (int c = 0; c < RC; ++c) {
+        const float x = cent[((int64_t)h * C + i) * RC + c];
+        cb[i * RC + c] = bfr(x);
+        float xx = x * x;
+        nrm = nrm + xx;
+      }
+      half[i] = bfr(0.5f * nrm);
+    }
+    for (int t = 0; t < T; ++t) {
+      float zb[RC];
+      for (int c = 0; c < RC; ++c) zb[c] = bfr(zP[((int64_t)h * T + t) * RC + c]);
+      int best = 0;
+      float bestv = -INFINITY;
+      for (int i = 0; i < C; ++i) {
+        float acc = 0.0f;
+        for (int c = 0; c < RC; ++c) acc = fmaf(zb[c], cb[i * RC + c], acc);
+        float dd = bfr(bfr(acc) - half[i]);
+        if (dd > bestv) {
+          bestv = dd;
+          best = i;
+        }
+      }
+      asg[(int64_t)h * asg_stride + t] = best;
+    }
+    free(cb);
+    free(half);
+  }
+}
+
+/* Lloyd update: cent_i = (sum of member zP in token order, fp32) / count; an empty cluster takes its
+ * seed point zP[init_i].  nb = member counts.  (methods_eager.py:543-545) */
+void oro_kmeans_update(int T, int C, const float* zP, const int32_t* asg, int64_t asg_stride, const int64_t* init,
+                       float* cent, float* nb) {
+#pragma omp parallel for schedule(static)
+  for (int h = 0; h < HQ; ++h) {
+    float* acc = (float*)calloc((size_t)C * RC, sizeof(float));
+    float* cnt = (float*)calloc((size_t)C, sizeof(float));
+    for (int t = 0; t < T; ++t) {
+      const int a = asg[(int64_t)h * asg_stride + t];
+      for (int c = 0; c < RC; ++c) acc[a * RC + c] = acc[a * RC + c] + zP[((int64_t)h * T + t) * RC + c];
+      cnt[a] = cnt[a] + 1.0f;
+    }
+    for (int i = 0; i < C; ++i) {
+      for (int c = 0; c < RC; ++c) {
+        float v = cnt[i] > 0.0f ? acc[i * RC + c] / fmaxf(cnt[i], 1.0f) : zP[((int64_t)h * T + init[i]) * RC + c];
+        cent[((int64_t)h * C + i) * RC + c] = v;
+      }
+      nb[(int64_t)h * C + i] = cnt[i];
+    }
+    free(acc);
+    free(cnt);
+  }
+}
+
+/* CSR member lists (stable by position) and per-cluster sums of k, k*k, v in member order, fp32
+ * (ours_fused.py:436-445 + ours_fastbuild.py:111-139; = the scatter_add sums of methods_eager.py:549-555).
+ * mem: (32, Lmax) first T used; cstart, clen: (32, C); Sk, Sk2, Sv: (32, C, D). */
+void oro_csr_sums(int T, int Lmax, int C, const uint16_t* K, const uint16_t* V, const int32_t* asg,
+                  int64_t asg_stride, int32_t* mem, int32_t* cstart, int32_t* clen, float* Sk, float* Sk2,
+                  float* Sv) {
+#pragma omp parallel for schedule(static)
+  for (int h = 0; h < HQ; ++h) {
+    int32_t* cnt = (int32_t*)calloc((size_t)C, sizeof(int32_t));
+    const int32_t* ar = asg + (int64_t)h * asg_stride;
+    for (int t = 0; t < T; ++t) cnt[ar[t]]++;
+    int run = 0;
+    for (int i = 0; i < C; ++i) {
+      cstart[h * C + i] = run;
+      clen[h * C + i] = cnt[i];
+      run += cnt[i];
+      cnt[i] = 0;
+    }
+    for (int t = 0; t < T; ++t) {
+      const int a = ar[t];
+      mem[(int64_t)h * Lmax + cstart[h * C + a] + cnt[a]] = t;
+      cnt[a]++;
+    }
+    for (int i = 0; i < C; ++i) {
+      float* sk = Sk + ((int64_t)h * C + i) * D;
+      float* sk2 = Sk2 + ((int64_t)h * C + i) * D;
+      float* sv = Sv + ((int64_t)h * C + i) * D;
+      for (int d = 0; d < D; ++d) sk[d] = sk2[d] = sv[d] = 0.0f;
+      for (int j = 0; j < clen[h * C + i]; ++j) {
+        const int t = mem[(int64_t)h * Lmax + cstart[h * C + i] + j];
+        const uint16_t* kr = K + ((int64_t)(h / G) * Lmax + t) * D;
+        const uint16_t* vr = V + ((int64_t)(h / G) * Lmax + t) * D;
+        for (int d = 0; d < D; ++d) {
+          float kf = bf2f(kr[d]);
+          sk[d] = sk[d] + kf;
+          float kk = kf * kf;
+          sk2[d] = sk2[d] + kk;
+          sv[d] = sv[d] + bf2f(vr[d]);
+        }
+      }
+    }
+    free(cnt);
+  }
+}
