@@ -1,0 +1,451 @@
+#!/usr/bin/env python3
+"""Decode-attention-stage benchmark of the OpenAttention deployed path on B200 (BASELINE config c2).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload per GPU: B=32 requests, 32K-token bf16 KV caches (seeded synthetic, see
+openattention_b200/synth.py), 1% read (C=64, E=216), ONE layer's decode step: index update + QGS
+scan + top-k, ErrorGate + water-filling, within-cluster top-q, residual proxies, OpenAttention.flash.
+Each step appends a token (n grows by one per step).  The step is one CUDA graph replay (the
+reference's deployed graph mode); the timed region replays K steps, inputs resident in HBM
+(`value`), and again with per-step host->device input copies and a device->host output copy through
+the same public API (`e2e`).  Inputs (int8 codes 268 MB + bf16 K/V 4.3 GB per GPU) exceed the
+126 MB L2, so no flush is needed between iterations.
+
+Multi-GPU (torchrun): requests are sharded, every rank runs its own B=32 (weak scaling), no
+collective on the data path; the step time is the max over ranks and `value` = that time / N
+(µs per bs32 layer-step for the whole job).
+
+--impl reference: the reference's CPU implementation of the path (this repository's C restatement
+of it, oracle/oa_oracle.c -- the reference itself is Python and cannot run without a checkout), on
+all host cores, on a bounded sample of the same workload, scaled to the same unit.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+import types
+
+import numpy as np
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode-attn-stage µs/step @32K ctx, bs32, 1% read; % HBM roofline; ms/token e2e"
+UNIT = "µs/step"
+B_PER_GPU, N_CTX, RHO = 32, 32768, 0.01
+SCAN_BYTES_PER_TOKEN = 32  # int8 codes per token per KV head (the scan's algorithmic bytes)
+LAUNCHES_PER_STEP = 7      # index_update, qgs_scan, qgs_select, errorgate_waterfill, topq, residual, flash
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)), int(os.environ.get("LOCAL_RANK", 0))
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_from_profiles():
+    """DRAM bytes per scan launch from the committed ncu summary (None when not captured yet)."""
+    p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
+    if os.path.exists(p):
+        try:
+            return json.load(open(p)).get("qgs_scan_per_launch_bytes")
+        except (ValueError, OSError):
+            return None
+    return None
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (SM clock, max clock, throttle reasons)."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, dev):
+        try:
+            self.index = torch.cuda.get_device_properties(dev).pci_bus_id
+        except AttributeError:
+            self.index = str(dev.index)
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "20"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------------ our arm
+def build_workload(dev, seed, steps_total):
+    from openattention_b200 import method as Mth
+    from openattention_b200 import synth
+    from openattention_b200.geometry import HQ
+    B, n0 = B_PER_GPU, N_CTX
+    Lmax = n0 + steps_total + 16
+    K, V, mus = synth.kv_torch(seed, B, n0, Lmax, dev)
+    Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40] * B
+    m = Mth.OursB200(types.SimpleNamespace(rho=RHO), B, Lmax, dev, layers=1)
+    g = torch.Generator(device=dev)
+    qpre = torch.empty(1, HQ, n0, 128, dtype=torch.bfloat16, device=dev)
+    for b in range(B):
+        g.manual_seed(seed + 5000 + b)
+        qpre[:, :, n0 - 64:] = torch.randn(1, HQ, 64, 128, generator=g, device=dev).to(torch.bfloat16)
+        m.build(0, b, qpre, n0)
+    del qpre
+    # per-step inputs: decode queries and the new K/V rows
+    g.manual_seed(seed + 9000)
+    qs = torch.randn(steps_total, B, HQ, 1, 128, generator=g, device=dev).to(torch.bfloat16)
+    nks, nvs = [], []
+    for s in range(steps_total):
+        nk, nv = synth.new_tokens_torch(seed + 20000 + s, mus, n0 + s)
+        nks.append(nk)
+        nvs.append(nv)
+    torch.cuda.synchronize()
+    return m, Mth, qs, torch.stack(nks), torch.stack(nvs), n0, Lmax
+
+
+class GraphStep:
+    """One decode step as a CUDA graph: write the new token at kv_idx, n_dev and kv_idx advance, decode."""
+
+    def __init__(self, m, Mth, n0, dev):
+        from openattention_b200.geometry import HQ
+        B = m.B
+        self.m, self.Mth = m, Mth
+        self.q_in = torch.zeros(B, HQ, 1, 128, dtype=torch.bfloat16, device=dev)
+        self.k_in = torch.zeros(B, 8, 128, dtype=torch.bfloat16, device=dev)
+        self.v_in = torch.zeros(B, 8, 128, dtype=torch.bfloat16, device=dev)
+        Mth.C.n_dev = torch.full((1,), n0, dtype=torch.int32, device=dev)      # n before the step
+        Mth.C.kv_idx = torch.full((1,), n0 - 1, dtype=torch.int64, device=dev)
+        Mth.C.n0_dev = torch.full((1,), n0, dtype=torch.int32, device=dev)
+        self.n_host = n0 + 1  # ns/nl/k_top are constant over the benchmark window
+        snap = {k: v.clone() for k, v in m.st[0].items()}
+        n_snap, kv_snap = Mth.C.n_dev.clone(), Mth.C.kv_idx.clone()
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(s):
+            for _ in range(2):  # warm-up outside capture
+                self._body()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for k, v in snap.items():
+            m.st[0][k].copy_(v)
+        Mth.C.n_dev.copy_(n_snap)
+        Mth.C.kv_idx.copy_(kv_snap)
+        torch.cuda.synchronize()
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.out = self._body()
+        torch.cuda.synchronize()
+
+    def _body(self):
+        C = self.Mth.C
+        C.n_dev.add_(1)
+        C.kv_idx.add_(1)
+        C.K[0].index_copy_(2, C.kv_idx, self.k_in.unsqueeze(2))
+        C.V[0].index_copy_(2, C.kv_idx, self.v_in.unsqueeze(2))
+        return self.m.decode(0, self.q_in, self.n_host)
+
+    def replay(self):
+        self.graph.replay()
+
+
+def time_scan(m, Mth, dev, iters):
+    """Average duration of the QGS scan kernel alone (CUDA events on its launch stream)."""
+    from openattention_b200 import selection as S
+    from openattention_b200.geometry import step_split
+    n = int(Mth.C.n_dev.item())
+    ns, nl, _ = step_split(n, RHO, m.C, m.E)
+    st = m.st[0]
+    for _ in range(3):
+        S.qgs_scan(st["codes"], m.zq, Mth.C.n_dev, ns, nl, m.scores, m.tmax)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        S.qgs_scan(st["codes"], m.zq, Mth.C.n_dev, ns, nl, m.scores, m.tmax)
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / iters, n
+
+
+def cpu_baseline_sample(m, Mth, qs, nks, nvs, budget_s=12.0):
+    """The oracle (C restatement of the reference's per-step algorithm) on the host cores: decode
+    steps of ONE request (request 0's state copied from the GPU), repeated until ~budget_s of CPU
+    work; reported per bs32 layer-step (x32)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    st_gpu = m.st[0]
+    st = {}
+    for k, v in st_gpu.items():
+        t = v[0:1].detach()
+        st[k] = O.bits(t).copy() if t.dtype == torch.bfloat16 else t.cpu().numpy().copy()
+    K = O.bits(Mth.C.K[0][0:1]).copy()
+    V = O.bits(Mth.C.V[0][0:1]).copy()
+    n = int(Mth.C.n_dev.item())
+    C, E = m.C, m.E
+    times, steps = [], 0
+    t_end = time.perf_counter() + budget_s
+    while time.perf_counter() < t_end and steps < 64:
+        s = steps % qs.shape[0]
+        n += 1
+        if n > K.shape[2]:
+            break
+        K[:, :, n - 1] = O.bits(nks[s][0:1])
+        V[:, :, n - 1] = O.bits(nvs[s][0:1])
+        q = O.bits(qs[s][0:1].reshape(32, 128))
+        t0 = time.perf_counter()
+        O.decode_step(st, q, K, V, n, RHO, C, E)
+        times.append(time.perf_counter() - t0)
+        steps += 1
+    per_req = statistics.median(times)
+    return {"value": per_req * 1e6 * B_PER_GPU, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"{steps} decode steps of 1 request (n~{N_CTX}, 1% read), median x {B_PER_GPU} requests; "
+                      f"oracle/oa_oracle.c with OpenMP on {os.cpu_count()} threads"}
+
+
+def run_ours(a):
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+        pg = dist
+    steps_total = a.warmup + 2 * a.steps + 8
+    m, Mth, qs, nks, nvs, n0, Lmax = build_workload(dev, seed=1000 * rank + 17, steps_total=steps_total)
+    gs = GraphStep(m, Mth, n0, dev)
+    snap = {k: v.clone() for k, v in m.st[0].items()}
+    n_snap, kv_snap = Mth.C.n_dev.clone(), Mth.C.kv_idx.clone()
+    Kc, Vc = Mth.C.K[0].clone(), Mth.C.V[0].clone()
+
+    def reset():
+        for k, v in snap.items():
+            m.st[0][k].copy_(v)
+        Mth.C.n_dev.copy_(n_snap)
+        Mth.C.kv_idx.copy_(kv_snap)
+        Mth.C.K[0].copy_(Kc)
+        Mth.C.V[0].copy_(Vc)
+        torch.cuda.synchronize()
+
+    def barrier():
+        if pg is not None:
+            pg.barrier()
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x):
+        if pg is None:
+            return x
+        t = torch.tensor([x], device=dev, dtype=torch.float64)
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- value: device-resident inputs (clocks sampled over warm-up and the timed region)
+    clk = Clocks(dev).__enter__()
+    for s in range(a.warmup):
+        gs.q_in.copy_(qs[s])
+        gs.k_in.copy_(nks[s])
+        gs.v_in.copy_(nvs[s])
+        gs.replay()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if True:
+        e0.record()
+        for s in range(a.steps):
+            i = a.warmup + s
+            gs.q_in.copy_(qs[i])
+            gs.k_in.copy_(nks[i])
+            gs.v_in.copy_(nvs[i])
+            gs.replay()
+        e1.record()
+        torch.cuda.synchronize()
+    clk.__exit__(None, None, None)
+    barrier()
+    ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
+    # ---- e2e: host buffers, copies inside the timed region
+    reset()
+    from openattention_b200.geometry import HQ
+    hq = qs.cpu().pin_memory()
+    hk = nks.cpu().pin_memory()
+    hv = nvs.cpu().pin_memory()
+    hout = torch.empty(a.steps, B_PER_GPU, HQ, 1, 128, dtype=torch.bfloat16).pin_memory()
+    for s in range(a.warmup):
+        gs.q_in.copy_(hq[s], non_blocking=True)
+        gs.k_in.copy_(hk[s], non_blocking=True)
+        gs.v_in.copy_(hv[s], non_blocking=True)
+        gs.replay()
+        hout[0].copy_(gs.out, non_blocking=True)
+    barrier()
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record()
+    for s in range(a.steps):
+        i = a.warmup + s
+        gs.q_in.copy_(hq[i], non_blocking=True)
+        gs.k_in.copy_(hk[i], non_blocking=True)
+        gs.v_in.copy_(hv[i], non_blocking=True)
+        gs.replay()
+        hout[s].copy_(gs.out, non_blocking=True)
+    f1.record()
+    torch.cuda.synchronize()
+    barrier()
+    ms_e2e = max_over_ranks(f0.elapsed_time(f1) / a.steps)
+    h2d = (qs[0].numel() + nks[0].numel() + nvs[0].numel()) * 2
+    d2h = gs.out.numel() * 2
+    # ---- roofline of the dominant kernel (QGS scan), timed alone
+    scan_ms, n_now = time_scan(m, Mth, dev, max(10, a.steps))
+    scan_ms = max_over_ranks(scan_ms)
+    alg_bytes = B_PER_GPU * 8 * n_now * SCAN_BYTES_PER_TOKEN
+    peak, peak_kind = peaks()
+    achieved = alg_bytes / (scan_ms * 1e-3) / 1e9
+    res = None
+    if rank == 0:
+        cpu = cpu_baseline_sample(m, Mth, qs, nks, nvs) if world == 1 else None
+        res = {
+            "metric": METRIC, "value": round(ms * 1e3 / world, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms, 5), "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded clustered RoPE keys, N(0,1) values/queries)",
+            "config": {"workload": f"c2 decode-attn-stage: B={B_PER_GPU} requests/GPU, n={N_CTX}+steps, rho=1% "
+                                   f"(C={m.C}, E={m.E}), one layer step as one CUDA graph",
+                       "global_batch": B_PER_GPU * world, "seq_len": N_CTX,
+                       "parallelism": f"request-sharded x{world} (no data-path collective)",
+                       "l2": "inputs larger than L2 (int8 codes 268 MB + bf16 K/V 4.3 GB per GPU), no flush"},
+            "e2e": {"value": round(ms_e2e * 1e3 / world, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": LAUNCHES_PER_STEP * a.steps,
+            "roofline": {"kernel": "qgs_scan_kernel", "bound": "hbm", "achieved": round(achieved, 1),
+                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic_from_profiles(), "alg_bytes_per_launch": alg_bytes,
+                         "launch_us": round(scan_ms * 1e3, 3)},
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+            "stage_us_per_step_per_gpu": round(ms * 1e3, 3),
+        }
+    if pg is not None:
+        del gs
+        pg.barrier()
+        pg.destroy_process_group()
+    return res
+
+
+# ------------------------------------------------------------------ reference arm (CPU)
+def run_reference(a):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return None
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    from openattention_b200 import synth
+    from openattention_b200.geometry import HQ, budget
+    C, E = budget(RHO)
+    B_s = 1  # requests per sample step (bounded CPU sample), scaled to bs32
+    n0 = N_CTX
+    Lmax = n0 + a.warmup + a.steps + 8
+    st = O.new_state(B_s, Lmax, C)
+    K = np.zeros((B_s, 8, Lmax, 128), np.uint16)
+    V = np.zeros_like(K)
+    mus = []
+    t_build = time.perf_counter()
+    Mpre = synth.static_metric_numpy(7, 1)[0]
+    inv = synth.llama31_inv_freq()
+    for b in range(B_s):
+        Kb, Vb, mu = synth.kv_numpy(17 + b, n0, Lmax)
+        K[b], V[b] = O.bits(Kb), O.bits(Vb)
+        mus.append(mu)
+        qpre = torch.zeros(HQ, n0, 128, dtype=torch.bfloat16)
+        qpre[:, n0 - 64:] = synth.queries_numpy(5017 + b, HQ * 64).view(HQ, 64, 128)
+        M = O.metric(Mpre, inv, 1.0, qpre, n0, 40)
+        U, W = O.basis(M)
+        O.build_from_basis(st, b, K[b], V[b], U.numpy(), O.bits(W), n0, layer=0)
+    t_build = time.perf_counter() - t_build
+    times = []
+    n = n0
+    for s in range(a.warmup + a.steps):
+        n += 1
+        for b in range(B_s):
+            nk, nv = synth.new_token_numpy(20017 + 100 * s + b, mus[b], n - 1)
+            K[b, :, n - 1], V[b, :, n - 1] = O.bits(nk), O.bits(nv)
+        q = O.bits(synth.queries_numpy(9017 + s, B_s * HQ))
+        t0 = time.perf_counter()
+        O.decode_step(st, q, K, V, n, RHO, C, E)
+        if s >= a.warmup:
+            times.append(time.perf_counter() - t0)
+    per = statistics.median(times) / B_s * B_PER_GPU * 1e6
+    cores = os.cpu_count()
+    sample = (f"{a.steps} timed decode steps of {B_s} request(s) at n={N_CTX}, 1% read (C={C}, E={E}); median "
+              f"scaled x{B_PER_GPU // B_s} to bs32; build {t_build:.1f} s untimed")
+    return {"metric": METRIC, "value": round(per, 1), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(per / 1e3, 4), "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded clustered RoPE keys)",
+            "impl": "reference",
+            "config": {"workload": f"c2 decode-attn-stage: B={B_PER_GPU} requests, n={N_CTX}, rho=1% (C={C}, E={E}), "
+                                   "one layer step", "global_batch": B_PER_GPU, "seq_len": N_CTX,
+                       "parallelism": "host CPU"},
+            "cpu_baseline": {"value": round(per, 1), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": round(per, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=500)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    a = ap.parse_args()
+    if a.warmup < 3:
+        a.warmup = 3
+    res = run_reference(a) if a.impl == "reference" else run_ours(a)
+    if res is not None:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -46,8 +46,10 @@ const char* oa_last_error_string(void);
  *   out    (BQ, D) bf16 or fp32 (out_dtype), row stride out_stride
  *   G = BQ / BH.  nsplit: 0 = automatic, 1 = one CTA per row, >1 = split the concatenated list
  *   [sel | exp | proxies] into nsplit chunks merged by a log-sum-exp combine; splitting needs
- *   `workspace` of oa_flash_workspace_bytes(BQ, nsplit) bytes, zero-filled before its first use
- *   (the kernel leaves it reusable).  Calls that share one workspace must not overlap on the GPU.
+ *   `workspace` of oa_flash_workspace_bytes(...) bytes whose first BQ*4 bytes (one ticket counter
+ *   per row) are zero before its first use; every call leaves them zero again, so a workspace can
+ *   be reused by later calls with the same BQ (any nsplit).  Calls that share one workspace must
+ *   not overlap on the GPU.
  * ----------------------------------------------------------------------------------------------*/
 int oa_flash_kvhead_proxies(const void* q, int64_t q_stride, const void* k, const void* v,
                             int64_t kv_stride_h, int64_t kv_stride_t, const int32_t* sel, int64_t n_sel,
@@ -72,6 +74,110 @@ int oa_flash_qhead_proxies(const void* q, int64_t q_stride, const void* k, const
 /* Bytes of workspace the flash entry points need for `nsplit` chunks per row (0 when nsplit <= 1;
  * nsplit = 0 is resolved the same way the entry points resolve it). */
 size_t oa_flash_workspace_bytes(int64_t BQ, int64_t n_sel, int64_t n_exp, int64_t NB, int nsplit);
+
+/* ------------------------------------------------------------------------------------------------
+ * Decode-step selection.  State layouts (all contiguous; B requests, C clusters, Lmax positions):
+ *   K, V     (B, 8, Lmax, 128) bf16 caches, new token already written at position n-1
+ *   codes    (B, 8, Lmax, 32) int8       U (B, 8, 128, 32) fp32      scale (B, 8, 32) fp32
+ *   W        (B, 32, 128, 16) bf16       colmean (B, 32, 16) fp32    cent (B, 32, C, 16) fp32
+ *   asg      (B, 32, Lmax) int32         nb (B, 32, C) fp32          Sk, Sk2, Sv (B, 32, C, 128) fp32
+ *   mem      (B, 32, Lmax) int32 CSR member lists, cstart / clen (B, 32, C) int32
+ *   reclist  (B, 32, C, rmax) int32 generated tokens per cluster, reccnt (B, 32, C) int32
+ * n_dev / n0_dev are device int32 scalars (current length incl. the new token; prefix length at
+ * build), so a captured CUDA graph replays correctly as n grows.
+ * ----------------------------------------------------------------------------------------------*/
+
+/* Index update of the new token at position n-1 plus the QGS query projection.
+ * Replaces _k_index_update_d2 (inference/ours_graph.py:43-90) and the zq matmul
+ * (inference/ours_graph.py:298, methods_eager.py:603).  Per KV head: code = clamp(rint(k.U/scale),
+ * +-127); per query head: nearest centroid of bf16(k.W) - colmean (ties -> lower id), asg, nb += 1,
+ * Sk += k, Sk2 += k*k, Sv += v, generated-token list append (reclist may be NULL).  If q is not
+ * NULL, zq (B*32, 32) bf16 = bf16((q.U) * scale) for q (B*32, 128) bf16 with row stride q_stride. */
+int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, int8_t* codes,
+                    const float* U, const float* scale, const void* W, const float* colmean, const float* cent,
+                    int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv, int32_t* reclist, int32_t* reccnt,
+                    int rmax, const void* q, int64_t q_stride, void* zq, const int32_t* n_dev, void* stream);
+
+/* QGS scan: scores (B*32, score_stride) bf16 = exact int8 dot products of codes and zq, rounded to
+ * fp32 then bf16, -inf for t < ns and t >= n - nl; tile_max (B*32, tile_max_stride) fp32 = maximum
+ * of each 256-token tile.  Replaces _k_qgs_scan_tm (inference/graph_runner.py:100-120). */
+int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64_t Lmax, const int32_t* n_dev, int ns, int nl,
+                void* scores, int64_t score_stride, float* tile_max, int64_t tile_max_stride, void* stream);
+
+/* Row top-k among the 2k tiles with the largest maxima (exact), ties -> lower position;
+ * sel (R, ns+nl+k_top) int32 = [0..ns-1, n-nl..n-1, top-k by rank]; the selected scores are set to
+ * -inf in `scores`.  Replaces _k_select (inference/graph_runner.py:123-159).  k_top <= 64. */
+int oa_qgs_select(void* scores, int64_t score_stride, const float* tile_max, int64_t tile_max_stride, int64_t R,
+                  int64_t Lmax, const int32_t* n_dev, int ns, int nl, int k_top, int32_t* sel, void* stream);
+
+/* ErrorGate (wl1) + hierarchical water-filling per row: tail statistics (pooled sums minus the
+ * selected tokens), score = zbar + ln n + s2/2 + ln erf(sqrt(s2/2)), quotas q_b = min(n_b,
+ * floor(lambda w_b)) plus leftover whole tokens to the best-scoring clusters with room.
+ * Outputs score, nt (tail counts) and quota, each (B*32, C) fp32.  Replaces _k_errorgate +
+ * _k_waterfill (inference/ours_fused.py:122-216).  C <= 256, n_sel <= 512. */
+int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64_t B, int64_t Lmax, int64_t C,
+                           const int32_t* asg, const int32_t* sel, int64_t n_sel, const float* Sk, const float* Sk2,
+                           const float* nb, float E, float* score, float* nt, float* quota, void* stream);
+
+/* Within-cluster top-q: for each cluster with quota q > 0, its q best members (CSR members, then
+ * generated tokens) by QGS score (selected tokens already -inf), ties -> lower position, written to
+ * exp_idx (R, E) int32 at the cluster's offset sum_{c'<c} q_c' in ascending position; -1 pads.
+ * reclist may be NULL (generated tokens are then found by scanning asg over [n0, n)).
+ * Replaces _k_topq_d2 (inference/ours_graph.py:93-166). */
+int oa_topq(const void* scores, int64_t score_stride, int64_t R, int64_t Lmax, int64_t C, const int32_t* mem,
+            const int32_t* cstart, const int32_t* clen, const int32_t* asg, const int32_t* reclist,
+            const int32_t* reccnt, int rmax, const float* quota, int64_t E, const int32_t* n_dev,
+            const int32_t* n0_dev, int32_t* exp_idx, void* stream);
+
+/* Residual proxies: per (row, cluster) the pooled sums minus every token read (sel in order, then
+ * the cluster's exp segment), n' = nt - quota, kbar' / vbar' = bf16(sums / max(n', 1)) (R, C, 128),
+ * log_n = ln max(n', 1) if n' > 0.5 else -inf (R, C) fp32.  Replaces _k_resid_scatter +
+ * _k_resid_norm (inference/ours_fused.py:367-407), without atomics. */
+int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, const int32_t* asg,
+                const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E, const float* Sk,
+                const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar, float* log_n,
+                void* stream);
+
+/* ------------------------------------------------------------------------------------------------
+ * Per-request build (prefill).  Each call works on ONE request: K, V (8, Lmax, 128) bf16 with the
+ * first T positions valid; state pointers address that request's slice ((8, ...) for QGS arrays,
+ * (32, ...) for QGC arrays).  Replaces methods_eager.Ours.build (inference/methods_eager.py:519-555)
+ * and the fast build (inference/ours_fastbuild.py:253-304); the eigen-decomposition and the k-means
+ * seeds stay on the host (torch), as in the reference.
+ * ----------------------------------------------------------------------------------------------*/
+
+/* QGS codes: z = k.U (8, T, 32), scale = max(amax_t |z| / 127, 1e-12) (8, 32), codes (8, Lmax, 32)
+ * = clamp(rint(z / scale), +-127).  amax_ws: 256 uint32 of scratch. */
+int oa_build_codes(const void* K, int64_t Lmax, int64_t T, const float* U, float* scale, int8_t* codes,
+                   uint32_t* amax_ws, void* stream);
+
+/* QGC projection: zP (32, T, 16) fp32 = bf16(k . W[h]) - colmean, colmean (32, 16) = column means
+ * (double accumulation per 256-token tile, then over tiles).  W (32, 128, 16) bf16. */
+size_t oa_build_project_workspace_bytes(int64_t T);
+int oa_build_project(const void* K, int64_t Lmax, int64_t T, const void* W, float* zP, float* colmean,
+                     void* workspace, size_t workspace_bytes, void* stream);
+
+/* One Lloyd assignment for the 32 query heads: asg[h, t] = argmax_c bf16(bf16(bf16(zP).bf16(cent_c))
+ * - bf16(|cent_c|^2 / 2)), ties -> lower c (inference/ours_fastbuild.py:52-82). */
+int oa_kmeans_assign(const float* zP, int64_t T, int64_t C, const float* cent, int32_t* asg, int64_t asg_stride,
+                     void* stream);
+
+/* Stable CSR member lists of an assignment: mem[h, cstart[h,c] + i] = i-th position (ascending) with
+ * asg == c; clen = counts (inference/ours_fused.py:436-445).  mem (32, mem_stride) int32. */
+size_t oa_csr_workspace_bytes(int64_t T, int64_t C);
+int oa_csr_build(const int32_t* asg, int64_t asg_stride, int64_t T, int64_t C, int32_t* mem, int64_t mem_stride,
+                 int32_t* cstart, int32_t* clen, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Lloyd update: cent_c = (sum of member zP, in position order, fp32) / count, an empty cluster takes
+ * zP[init_c]; nb = counts (inference/methods_eager.py:543-545). init: (C,) int64 seed positions. */
+int oa_kmeans_update(const float* zP, int64_t T, int64_t C, const int32_t* mem, int64_t mem_stride,
+                     const int32_t* cstart, const int32_t* clen, const int64_t* init, float* cent, float* nb,
+                     void* stream);
+
+/* Cluster sums Sk, Sk2, Sv (32, C, 128) fp32 over the members in position order
+ * (inference/ours_fastbuild.py:111-139; = the scatter_add sums of methods_eager.py:549-555). */
+int oa_cluster_sums(const void* K, const void* V, int64_t Lmax, int64_t C, const int32_t* mem, int64_t mem_stride,
+                    const int32_t* cstart, const int32_t* clen, float* Sk, float* Sk2, float* Sv, void* stream);
 
 #ifdef __cplusplus
 }

@@ -12,6 +12,8 @@
 #include <stdint.h>
 #include <math.h>
 
+#include <algorithm>
+
 namespace oa {
 
 constexpr int kD = 128;

@@ -301,13 +301,14 @@ int flash_entry(bool qhead, const void* q, int64_t q_stride, const void* k, cons
     OA_REQUIRE(workspace && ws_bytes >= need && oa_aligned16(workspace),
                "%s: split into %d chunks needs a 16-byte aligned workspace of %zu bytes (got %zu)", fn, ns,
                need, ws_bytes);
+    // ticket counters first (their place depends on BQ only), then the partial (m, l, acc) arrays
     const size_t parts = (size_t)BQ * ns;
     char* w = static_cast<char*>(workspace);
+    a.cnt = reinterpret_cast<unsigned*>(w);
+    w += align256((size_t)BQ * sizeof(unsigned));
     a.pm = reinterpret_cast<float*>(w);
     a.pl = reinterpret_cast<float*>(w + align256(parts * sizeof(float)));
     a.pacc = reinterpret_cast<float*>(w + 2 * align256(parts * sizeof(float)));
-    a.cnt = reinterpret_cast<unsigned*>(w + 2 * align256(parts * sizeof(float)) +
-                                        align256(parts * kD * sizeof(float)));
   }
   dim3 grid((unsigned)BQ, (unsigned)ns);
   cudaStream_t st = static_cast<cudaStream_t>(stream);

@@ -1,0 +1,255 @@
+"""The deployed OpenAttention method on B200: the drop-in for the reference's `Method` classes
+(inference/methods_eager.py:243-266 Method, :468-662 Ours; inference/ours_graph.py:265-347 OursG2;
+inference/ours_fastbuild.py:143-307 OursG3 "ours3").
+
+    C.K = [...]; C.V = [...]          # per layer (B, 8, Lmax, 128) bf16 caches, owned by the caller
+    m = OursB200(SimpleNamespace(rho=0.01), B, Lmax, "cuda")
+    m.build(l, b, q_prefill, T)       # prefill: per layer and batch row, after K/V[:, :, :T] are written
+    out = m.decode(l, q, n)           # decode: q (B, 32, 1, 128) bf16, new token already at n - 1
+
+Every compute step is a kernel of the C-ABI library (selection.py / flash.py / the build entry
+points); torch only allocates memory, runs the per-request eigen-decomposition of the 128x128 query
+metric (torch.linalg.eigh, as the reference) and draws the k-means seeds (CPU randperm, as the
+reference).  The step is CUDA-graph safe: it reads the current length from `C.n_dev` and the
+prefix length from `C.n0_dev` when the caller provides them (graph_runner.py:601-603), never syncs
+with the host, and all per-step buffers are preallocated in __init__.
+"""
+from __future__ import annotations
+
+import os
+
+import torch
+
+from . import _lib
+from . import flash as flash_mod
+from . import selection as S
+from .geometry import D, G, HKV, HQ, ITERS, PQ, RC, RMAX, RQ, WIN, budget, llama31_inv_freq, step_split
+
+NL = 32  # layers a method instance holds state for (methods_eager.NL)
+
+
+class Ctx:
+    """Run state shared with the attention hook (inference/methods_eager.py:176-189)."""
+    phase = "prefill"
+    brow = 0
+    n = 0
+    K = V = None        # per layer (B, HKV, Lmax, D)
+    qlen = []           # question-chunk length per batch row
+    method = None
+    n_dev = None        # device int32 (1,): current length incl. the new token (graph mode)
+    n0_dev = None       # device int32 (1,): prefix length at build (graph mode)
+    kv_idx = None       # device int64 (1,): write position of the new token (graph mode)
+
+
+C = Ctx()
+
+
+# ------------------------------------------------------------------ static query metric
+def rot_avg(Mpre: torch.Tensor, inv_freq: torch.Tensor, scaling: float, p: int, w: int) -> torch.Tensor:
+    """mean over t in [p, p+w) of R_t M R_t^T in closed form, R_t the RoPE rotation at position t
+    (StaticTopKMasker._rot_avg, static_top_k.py:102-131)."""
+    dev = Mpre.device
+    th = torch.cat([inv_freq, inv_freq]).double().to(dev)
+    a, b = th.unsqueeze(1), th.unsqueeze(0)
+
+    def mean_exp(alpha):
+        if w <= 64:
+            t = torch.arange(p, p + w, device=dev, dtype=torch.float64)
+            ph = alpha.unsqueeze(-1) * t
+            return torch.complex(ph.cos().mean(-1), ph.sin().mean(-1))
+        z = torch.polar(torch.ones_like(alpha), alpha)
+        den = 1 - z
+        small = den.abs() < 1e-9
+        s = torch.where(small, torch.full_like(z, float(w)), (1 - z ** w) / torch.where(small, torch.ones_like(den), den))
+        return s * torch.polar(torch.ones_like(alpha), alpha * p) / w
+
+    Em, Ep = mean_exp(a - b), mean_exp(a + b)
+    cc, ss = 0.5 * (Em.real + Ep.real), 0.5 * (Em.real - Ep.real)
+    cs, sc = 0.5 * (Ep.imag - Em.imag), 0.5 * (Ep.imag + Em.imag)
+    cc, ss, cs, sc = [x.float() * (scaling * scaling) for x in (cc, ss, cs, sc)]
+    h = D // 2
+    J = torch.zeros(D, D, device=dev)
+    J[:h, h:] = -torch.eye(h, device=dev)
+    J[h:, :h] = torch.eye(h, device=dev)
+    M = Mpre.float()
+    return cc * M + cs * (M @ J.T) + sc * (J @ M) + ss * (J @ M @ J.T)
+
+
+def query_metric(Mpre_l, inv_freq, scaling, q, T, Qn, win=WIN, P=PQ):
+    """M = 1/2 trnorm(static metric rotated to [T, T+win)) + 1/2 trnorm(question rows)
+    (inference/methods_eager.py:510-518).  q: (1, 32, T, D) prefill queries."""
+    def nt(x):
+        return x / torch.diagonal(x, dim1=-2, dim2=-1).sum(-1).clamp(min=1e-12)[..., None, None]
+    dev = q.device
+    Mst = rot_avg(Mpre_l, inv_freq, scaling, T, win)
+    Pn = min(P, max(Qn - 2, 1))
+    pi = torch.linspace(0, max(Qn - 3, 0), Pn, device=dev).long().unique()
+    qsel = q[0, :, T - Qn:, :].index_select(1, pi).float()
+    freqs = (Qn - pi).float().unsqueeze(-1) * inv_freq.to(dev).unsqueeze(0)
+    emb = torch.cat([freqs, freqs], -1)
+    cos, sin = emb.cos() * scaling, emb.sin() * scaling
+    h = D // 2
+    qrot = qsel * cos + torch.cat([-qsel[..., h:], qsel[..., :h]], -1) * sin
+    Mq = torch.matmul(qrot.transpose(-1, -2), qrot) / qrot.shape[1]
+    return 0.5 * nt(Mst) + 0.5 * nt(Mq)
+
+
+def basis_from_metric(M: torch.Tensor):
+    """U (8, D, 32): top-32 eigenvectors of each KV head's mean metric; W (32, D, 16) bf16 =
+    top-16 eigenvectors scaled by sqrt(max(eigenvalue, 0)) (inference/methods_eager.py:520-528)."""
+    _, Ukv = torch.linalg.eigh(M.view(HKV, G, D, D).mean(1))
+    U = Ukv[..., -RQ:].contiguous()
+    ev, Uq = torch.linalg.eigh(M)
+    W = (Uq[..., -RC:] * ev[..., -RC:].clamp(min=0).sqrt().unsqueeze(-2)).to(torch.bfloat16).contiguous()
+    return U, W
+
+
+def kmeans_seeds(T: int, Cn: int, layer: int) -> torch.Tensor:
+    g = torch.Generator(device="cpu").manual_seed(31 * (layer + 1))
+    return torch.randperm(T, generator=g)[:Cn]
+
+
+def load_static_metric(a, layers: int):
+    """The pre-RoPE query metric (L, 32, D, D): `a.static_metric` (tensor or dict), else the file named
+    by OA_STATIC_M (the reference's unpacked asset format: {"M", "inv_freq", "attention_scaling"}),
+    else the seeded stand-in of synth.static_metric_numpy."""
+    src = getattr(a, "static_metric", None)
+    if src is None and os.environ.get("OA_STATIC_M") and os.path.exists(os.environ["OA_STATIC_M"]):
+        src = torch.load(os.environ["OA_STATIC_M"], map_location="cpu", weights_only=False)
+    if src is None:
+        from .synth import static_metric_numpy
+        return static_metric_numpy(getattr(a, "metric_seed", 7), layers), llama31_inv_freq(), 1.0
+    if isinstance(src, dict):
+        return src["M"].float(), src.get("inv_freq", llama31_inv_freq()).float(), float(src.get("attention_scaling", 1.0))
+    return src.float(), llama31_inv_freq(), 1.0
+
+
+# ------------------------------------------------------------------ the method
+class OursB200:
+    """OpenAttention decode (QGS scan + top-k, ErrorGate + water-filling, within-cluster top-q,
+    residual proxies, OpenAttention.flash) with the per-request QGC/QGS build."""
+    name = "ours3"
+
+    def __init__(self, a, B, Lmax, dev, layers: int | None = None):
+        self.a, self.B, self.Lmax = a, B, Lmax
+        self.dev = torch.device(dev)
+        if self.dev.type != "cuda":
+            raise RuntimeError("OursB200 runs on CUDA devices only (no CPU fallback)")
+        _lib.load()
+        self.R = B * HQ
+        self.C, self.E = budget(a.rho)
+        self.NL = layers or getattr(a, "layers", None) or NL
+        Mpre, inv_freq, scaling = load_static_metric(a, self.NL)
+        self.Mpre = Mpre.to(self.dev)
+        self.inv_freq = inv_freq.to(self.dev)
+        self.scaling = scaling
+        self.st = [S.new_state(B, Lmax, self.C, self.dev, RMAX) for _ in range(self.NL)]
+        R, Cn, E, dev = self.R, self.C, self.E, self.dev
+        self.NT = (Lmax + 255) // 256
+        self.SW = self.NT * 256
+        self.zq = torch.zeros(R, RQ, dtype=torch.bfloat16, device=dev)
+        self.scores = torch.zeros(R, self.SW, dtype=torch.bfloat16, device=dev)
+        self.tmax = torch.zeros(R, self.NT, dtype=torch.float32, device=dev)
+        self.score = torch.zeros(R, Cn, device=dev)
+        self.nt = torch.zeros(R, Cn, device=dev)
+        self.quota = torch.zeros(R, Cn, device=dev)
+        self.exp_idx = torch.full((R, E), -1, dtype=torch.int32, device=dev)
+        self.kbar = torch.zeros(R, Cn, D, dtype=torch.bfloat16, device=dev)
+        self.vbar = torch.zeros(R, Cn, D, dtype=torch.bfloat16, device=dev)
+        self.logn = torch.zeros(R, Cn, device=dev)
+        self.out = torch.zeros(R, D, dtype=torch.bfloat16, device=dev)
+        self._sel = {}
+        self._n_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._n0_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        lib = _lib.load()
+        # the automatic split count depends on the list length (chunk rounding): size for the largest
+        nbytes = max(lib.oa_flash_workspace_bytes(R, ns, E, Cn, 0) for ns in range(1, 513))
+        self.flash_ws = torch.zeros(max(nbytes, 16), dtype=torch.uint8, device=dev) if nbytes else None
+        self._quota = self.quota
+        self.read_frac = 0.0
+
+    # ---------------------------------------------------------------- build (prefill)
+    def build(self, l, b, q, T):
+        """Index of layer l, batch row b after the prefill wrote C.K[l][b, :, :T], C.V[l][b, :, :T];
+        q: (1, 32, T, D) prefill queries (the last C.qlen[b] rows are the question)."""
+        st = self.st[l]
+        K1, V1 = C.K[l][b], C.V[l][b]
+        Qn = C.qlen[b] if C.qlen else 40
+        M = query_metric(self.Mpre[l], self.inv_freq, self.scaling, q, T, Qn)
+        U, W = basis_from_metric(M)
+        self.build_from_basis(l, b, U, W, T)
+
+    def build_from_basis(self, l, b, U, W, T):
+        """Everything of the build after the eigen-decomposition (QGS codes, QGC projection, Lloyd
+        iterations, CSR member lists, cluster sums), all on the GPU."""
+        st, dev, Cn, Lmax = self.st[l], self.dev, self.C, self.Lmax
+        K1, V1 = C.K[l][b], C.V[l][b]
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        p = _lib.ptr
+        st["U"][b].copy_(U)
+        st["W"][b].copy_(W)
+        lib = _lib.load()
+        amax = torch.empty(HKV * RQ, dtype=torch.int32, device=dev)
+        _lib.call("oa_build_codes", p(K1), Lmax, T, p(st["U"][b]), p(st["scale"][b]), p(st["codes"][b]), p(amax),
+                  stream)
+        zP = torch.empty(HQ, T, RC, device=dev)
+        ws = torch.empty(max(lib.oa_build_project_workspace_bytes(T), lib.oa_csr_workspace_bytes(T, Cn)),
+                         dtype=torch.uint8, device=dev)
+        _lib.call("oa_build_project", p(K1), Lmax, T, p(st["W"][b]), p(zP), p(st["colmean"][b]), p(ws), ws.numel(),
+                  stream)
+        init = kmeans_seeds(T, Cn, l).to(dev)
+        cent = st["cent"][b]
+        cent.copy_(zP.index_select(1, init))
+        for _ in range(ITERS):
+            _lib.call("oa_kmeans_assign", p(zP), T, Cn, p(cent), p(st["asg"][b]), Lmax, stream)
+            _lib.call("oa_csr_build", p(st["asg"][b]), Lmax, T, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]),
+                      p(st["clen"][b]), p(ws), ws.numel(), stream)
+            _lib.call("oa_kmeans_update", p(zP), T, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]), p(st["clen"][b]),
+                      p(init), p(cent), p(st["nb"][b]), stream)
+        _lib.call("oa_cluster_sums", p(K1), p(V1), Lmax, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]),
+                  p(st["clen"][b]), p(st["Sk"][b]), p(st["Sk2"][b]), p(st["Sv"][b]), stream)
+        st["reccnt"][b].zero_()
+        self._n0_dev.fill_(T)
+
+    # ---------------------------------------------------------------- decode step
+    def _sel_buf(self, NS):
+        if NS not in self._sel:
+            self._sel[NS] = torch.zeros(self.R, NS, dtype=torch.int32, device=self.dev)
+        return self._sel[NS]
+
+    def select(self, l, q, n):
+        """Stages 1-5 of the step: index update + zq, QGS scan + top-k, ErrorGate + water-filling,
+        within-cluster top-q, residual proxies.  Returns (sel, exp_idx, kbar', vbar', log n')."""
+        st, Lmax = self.st[l], self.Lmax
+        K, V = C.K[l], C.V[l]
+        n_dev = C.n_dev if C.n_dev is not None else self._n_dev.fill_(n)
+        n0_dev = C.n0_dev if C.n0_dev is not None else self._n0_dev
+        ns, nl, k_top = step_split(n, self.a.rho, self.C, self.E)
+        qr = q.reshape(self.R, D)
+        if not qr.is_contiguous():
+            qr = qr.contiguous()
+        sel = self._sel_buf(ns + nl + k_top)
+        S.index_update(K, V, st, n_dev, q=qr, zq=self.zq)
+        S.qgs_scan(st["codes"], self.zq, n_dev, ns, nl, self.scores, self.tmax)
+        S.qgs_select(self.scores, self.tmax, Lmax, n_dev, ns, nl, k_top, sel)
+        S.errorgate_waterfill(qr, K, st, sel, self.E, self.score, self.nt, self.quota)
+        S.topq(self.scores, st, self.quota, self.E, n_dev, n0_dev, self.exp_idx)
+        S.residual(K, V, st, sel, self.exp_idx, self.nt, self.quota, self.kbar, self.vbar, self.logn)
+        self._quota = self.quota
+        self.read_frac = (ns + nl + k_top + self.E + 1.5 * self.C) / n
+        return qr, sel
+
+    def decode(self, l, q, n):
+        qr, sel = self.select(l, q, n)
+        return self.attend(l, qr, sel, self.exp_idx, self.kbar, self.vbar, self.logn)
+
+    def attend(self, l, qr, sel, exp_idx, kbar_r, vbar_r, logn):
+        """OpenAttention.flash with per-query-head proxies, called through the module attribute
+        flash.ours_flash so tests can spy on it (as the reference's bl.ours_flash)."""
+        Lmax = self.Lmax
+        out = flash_mod.ours_flash(qr, C.K[l].view(-1, Lmax, D), C.V[l].view(-1, Lmax, D), sel, exp_idx, kbar_r,
+                                   vbar_r, logn, out=self.out, workspace=self.flash_ws)
+        return out.view(self.B, HQ, 1, D)
+
+
+METHODS = {"ours3": OursB200, "ours": OursB200}

@@ -1,0 +1,108 @@
+"""Torch-tensor wrappers over the C-ABI selection stages (one call = one kernel launch on the current
+stream).  Shapes follow the state layout of include/openattention_b200.h; all tensors must be CUDA,
+contiguous and of the stated dtype (checked here, so the C side only sees valid layouts)."""
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .geometry import D, HKV, HQ, RC, RQ
+
+_ptr = _lib.ptr
+
+
+def _stream(t):
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need(name, t, dtype, shape=None):
+    if t is None:
+        return
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise RuntimeError(f"{name}: need a contiguous CUDA {dtype} tensor, got {t.dtype} "
+                           f"{'cuda' if t.is_cuda else 'cpu'} contiguous={t.is_contiguous()}")
+    if shape is not None and tuple(t.shape) != tuple(shape):
+        raise RuntimeError(f"{name}: shape {tuple(t.shape)} != {tuple(shape)}")
+
+
+def index_update(K, V, st, n_dev, q=None, zq=None):
+    """New token at n-1 joins the index; with q (B*32, D) also writes zq (B*32, 32) bf16."""
+    B, _, Lmax, _ = K.shape
+    C = st["nb"].shape[-1]
+    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("V", V, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("n_dev", n_dev, torch.int32, (1,))
+    if q is not None:
+        if q.dtype != torch.bfloat16 or q.stride(-1) != 1 or q.shape != (B * HQ, D):
+            raise RuntimeError("q must be (B*32, 128) bf16 with a contiguous last dim")
+        _need("zq", zq, torch.bfloat16, (B * HQ, RQ))
+    rec = st.get("reclist")
+    _lib.call("oa_index_update", _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["codes"]), _ptr(st["U"]), _ptr(st["scale"]),
+              _ptr(st["W"]), _ptr(st["colmean"]), _ptr(st["cent"]), _ptr(st["asg"]), _ptr(st["nb"]),
+              _ptr(st["Sk"]), _ptr(st["Sk2"]), _ptr(st["Sv"]), _ptr(rec), _ptr(st.get("reccnt")),
+              0 if rec is None else rec.shape[-1], _ptr(q), 0 if q is None else q.stride(0), _ptr(zq), _ptr(n_dev),
+              _stream(K))
+
+
+def qgs_scan(codes, zq, n_dev, ns, nl, scores, tile_max):
+    B, _, Lmax, _ = codes.shape
+    _need("codes", codes, torch.int8)
+    _need("zq", zq, torch.bfloat16, (B * HQ, RQ))
+    if scores.dtype != torch.bfloat16 or tile_max.dtype != torch.float32 or scores.stride(1) != 1:
+        raise RuntimeError("scores must be bf16 (R, >= Lmax) and tile_max fp32 (R, >= NT)")
+    _lib.call("oa_qgs_scan", _ptr(codes), _ptr(zq), B, Lmax, _ptr(n_dev), int(ns), int(nl), _ptr(scores),
+              scores.stride(0), _ptr(tile_max), tile_max.stride(0), _stream(codes))
+
+
+def qgs_select(scores, tile_max, Lmax, n_dev, ns, nl, k_top, sel):
+    R = scores.shape[0]
+    _need("sel", sel, torch.int32, (R, ns + nl + k_top))
+    _lib.call("oa_qgs_select", _ptr(scores), scores.stride(0), _ptr(tile_max), tile_max.stride(0), R, Lmax,
+              _ptr(n_dev), int(ns), int(nl), int(k_top), _ptr(sel), _stream(scores))
+
+
+def errorgate_waterfill(q, K, st, sel, E, score, nt, quota):
+    B, _, Lmax, _ = K.shape
+    C = st["nb"].shape[-1]
+    R = B * HQ
+    for nm, t in (("score", score), ("nt", nt), ("quota", quota)):
+        _need(nm, t, torch.float32, (R, C))
+    _need("sel", sel, torch.int32)
+    _lib.call("oa_errorgate_waterfill", _ptr(q), q.stride(0), _ptr(K), B, Lmax, C, _ptr(st["asg"]), _ptr(sel),
+              sel.shape[1], _ptr(st["Sk"]), _ptr(st["Sk2"]), _ptr(st["nb"]), float(E), _ptr(score), _ptr(nt),
+              _ptr(quota), _stream(K))
+
+
+def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx):
+    R = scores.shape[0]
+    B, _, Lmax = st["asg"].shape
+    C = st["nb"].shape[-1]
+    _need("exp_idx", exp_idx, torch.int32, (R, E))
+    rec = st.get("reclist")
+    _lib.call("oa_topq", _ptr(scores), scores.stride(0), R, Lmax, C, _ptr(st["mem"]), _ptr(st["cstart"]),
+              _ptr(st["clen"]), _ptr(st["asg"]), _ptr(rec), _ptr(st.get("reccnt")),
+              0 if rec is None else rec.shape[-1], _ptr(quota), E, _ptr(n_dev), _ptr(n0_dev), _ptr(exp_idx),
+              _stream(scores))
+
+
+def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn):
+    B, _, Lmax, _ = K.shape
+    C = st["nb"].shape[-1]
+    R = B * HQ
+    _need("kbar", kbar, torch.bfloat16, (R, C, D))
+    _need("vbar", vbar, torch.bfloat16, (R, C, D))
+    _need("logn", logn, torch.float32, (R, C))
+    _lib.call("oa_residual", _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["asg"]), _ptr(sel), sel.shape[1], _ptr(exp_idx),
+              exp_idx.shape[1], _ptr(st["Sk"]), _ptr(st["Sv"]), _ptr(nt), _ptr(quota), _ptr(kbar), _ptr(vbar),
+              _ptr(logn), _stream(K))
+
+
+def new_state(B: int, Lmax: int, C: int, device, rmax: int = 256) -> dict:
+    """Per-layer index state (the layout contract of methods_eager.Ours / OursG2 state, int8 codes)."""
+    z = lambda *s, dt=torch.float32: torch.zeros(*s, device=device, dtype=dt)  # noqa: E731
+    return dict(codes=z(B, HKV, Lmax, RQ, dt=torch.int8), U=z(B, HKV, D, RQ), scale=z(B, HKV, RQ),
+                W=z(B, HQ, D, RC, dt=torch.bfloat16), colmean=z(B, HQ, RC), cent=z(B, HQ, C, RC),
+                asg=z(B, HQ, Lmax, dt=torch.int32), nb=z(B, HQ, C), Sk=z(B, HQ, C, D), Sk2=z(B, HQ, C, D),
+                Sv=z(B, HQ, C, D), mem=z(B, HQ, Lmax, dt=torch.int32), cstart=z(B, HQ, C, dt=torch.int32),
+                clen=z(B, HQ, C, dt=torch.int32), reclist=z(B, HQ, C, rmax, dt=torch.int32),
+                reccnt=z(B, HQ, C, dt=torch.int32))

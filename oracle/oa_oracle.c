@@ -20,6 +20,9 @@
  *   erf(x) = 2/sqrt(pi) * exp(-x^2) * sum_n (2x^2)^n x / (1*3*...*(2n+1))   (all-positive series,
  *            Abramowitz & Stegun 7.1.6), 1 for x >= 6.
  *
+ * QGS scores are exact: the int8 codes times a fixed-point image of zq summed in integers (see
+ * oro_zq_fixed), so any summation order -- the GPU uses int8 tensor-core MMAs -- gives the same value.
+ *
  * Layouts (contiguous): row r = b*32 + h, kv row = b*8 + h/4, D = 128.
  */
 #include <math.h>
@@ -209,22 +212,57 @@ void oro_zq(int B, const uint16_t* q, const float* U, const float* scale, uint16
   }
 }
 
-/* QGS scores s[r, t] = bf16(sum_j code[t, j] * zq[r, j]) (j ascending), -inf for t < ns and
- * t >= n - nl.  Restates _k_qgs_scan_tm (inference/graph_runner.py:100-120). s: (R, sw) bf16 bits. */
+/* Exact fixed-point image of one query head's zq (32 bf16 values): Z_j = trunc(z_j * 2^S) with
+ * S = 29 - e_max (e_max = binary exponent of max |z_j|), so |Z_j| < 2^30; z_j below 2^(e_max - 23)
+ * lose their fractional bits.  Returns S; all-zero (or below 2^-100) heads give S = 0, Z = 0. */
+static float pow2f_exact(int k) { /* 2^k as float, -126 <= k <= 127 */
+  uint32_t b = (uint32_t)(k + 127) << 23;
+  float f;
+  memcpy(&f, &b, 4);
+  return f;
+}
+static float scale_pow2(float x, int k) { /* x * 2^k by exact power-of-two steps */
+  while (k > 100) { x = x * pow2f_exact(100); k -= 100; }
+  while (k < -100) { x = x * pow2f_exact(-100); k += 100; }
+  return x * pow2f_exact(k);
+}
+int oro_zq_fixed(const uint16_t* zq, int32_t* Z) {
+  float amax = 0.0f;
+  for (int j = 0; j < RQ; ++j) {
+    float a = fabsf(bf2f(zq[j]));
+    if (a > amax) amax = a;
+  }
+  uint32_t ab;
+  memcpy(&ab, &amax, 4);
+  const int e_max = (int)((ab >> 23) & 0xff) - 127;
+  if (amax == 0.0f || e_max < -100) {
+    for (int j = 0; j < RQ; ++j) Z[j] = 0;
+    return 0;
+  }
+  const int S = 29 - e_max;
+  for (int j = 0; j < RQ; ++j) Z[j] = (int32_t)scale_pow2(bf2f(zq[j]), S); /* C cast truncates */
+  return S;
+}
+
+/* QGS scores s[r, t] = bf16( fp32( sum_j code[t, j] * Z[r, j] ) * 2^-S_r ): the exact integer dot
+ * product of the int8 codes with the fixed-point zq, rounded once to fp32 and once to bf16 (the
+ * value an fp32 sum without intermediate rounding would give); -inf for t < ns and t >= n - nl.
+ * Restates _k_qgs_scan_tm (inference/graph_runner.py:100-120). s: (R, sw) bf16 bits. */
 void oro_scan(int B, int Lmax, int n, int ns, int nl, const int8_t* codes, const uint16_t* zq, uint16_t* s,
               int64_t sw) {
 #pragma omp parallel for schedule(static)
   for (int r = 0; r < B * HQ; ++r) {
     const int kv = r / G;
-    float z[RQ];
-    for (int j = 0; j < RQ; ++j) z[j] = bf2f(zq[r * RQ + j]);
+    int32_t Z[RQ];
+    const int S = oro_zq_fixed(zq + (int64_t)r * RQ, Z);
     const int8_t* cr = codes + (int64_t)kv * Lmax * RQ;
     uint16_t* sr = s + (int64_t)r * sw;
     for (int t = 0; t < n; ++t) {
-      float acc = 0.0f;
+      int64_t acc = 0;
       const int8_t* c = cr + (int64_t)t * RQ;
-      for (int j = 0; j < RQ; ++j) acc = fmaf((float)c[j], z[j], acc);
-      uint16_t v = f2bf(acc);
+      for (int j = 0; j < RQ; ++j) acc += (int64_t)c[j] * (int64_t)Z[j];
+      const float f = scale_pow2((float)acc, -S);
+      uint16_t v = f2bf(f);
       if (t < ns || t >= n - nl) v = 0xff80; /* -inf */
       sr[t] = v;
     }
@@ -266,10 +304,29 @@ void oro_select(int R, int n, int ns, int nl, int k_top, uint16_t* s, int64_t sw
   }
 }
 
+/* 128-term dot product in the order one warp computes it: lane l accumulates
+ * fma(a[l+96], b[l+96], fma(a[l+64], b[l+64], fma(a[l+32], b[l+32], a[l]*b[l]))), then the 32
+ * partials are combined by an xor butterfly over offsets 16, 8, 4, 2, 1. */
+float oro_dot128_tree(const float* a, const float* b) {
+  float p[32], t[32];
+  for (int l = 0; l < 32; ++l) {
+    float v = a[l] * b[l];
+    v = fmaf(a[l + 32], b[l + 32], v);
+    v = fmaf(a[l + 64], b[l + 64], v);
+    v = fmaf(a[l + 96], b[l + 96], v);
+    p[l] = v;
+  }
+  for (int off = 16; off >= 1; off >>= 1) {
+    for (int l = 0; l < 32; ++l) t[l] = p[l] + p[l ^ off];
+    for (int l = 0; l < 32; ++l) p[l] = t[l];
+  }
+  return p[0];
+}
+
 /* ErrorGate wl1 (inference/ours_fused.py:122-154, methods_eager.py:613-627).  Per row: tail sums
  * (pooled sums minus the selected tokens, in sel order), then per cluster
  *   kbar = Skt*inv, var = max(Sk2t*inv - kbar*kbar, 0), inv = 1/max(nt,1)
- *   zbar = SC * sum_d q_d kbar_d,  s2 = SC^2 * sum_d (q_d q_d) var_d   (d ascending, fmaf)
+ *   zbar = SC * dot(q, kbar),  s2 = SC^2 * dot(q*q, var)   (oro_dot128_tree order)
  *   score = ((zbar + ln max(nt,1)) + 0.5 s2) + ln max(erf(sqrt(s2)*0.70710677), 1e-30). */
 void oro_errorgate(int B, int Lmax, int C, int NS, const uint16_t* q, const uint16_t* K, const int32_t* asg,
                    const int32_t* sel, const float* Sk, const float* Sk2, const float* nb, float* score, float* nt) {
@@ -303,15 +360,15 @@ void oro_errorgate(int B, int Lmax, int C, int NS, const uint16_t* q, const uint
     }
     for (int c = 0; c < C; ++c) {
       const float inv = 1.0f / fmaxf(ntr[c], 1.0f);
-      float zd = 0.0f, sd = 0.0f;
+      float kb[D], var[D];
       for (int d = 0; d < D; ++d) {
-        float kb = skt[c * D + d] * inv;
+        kb[d] = skt[c * D + d] * inv;
         float p1 = sk2t[c * D + d] * inv;
-        float p2 = kb * kb;
-        float var = fmaxf(p1 - p2, 0.0f);
-        zd = fmaf(qf[d], kb, zd);
-        sd = fmaf(q2[d], var, sd);
+        float p2 = kb[d] * kb[d];
+        var[d] = fmaxf(p1 - p2, 0.0f);
       }
+      float zd = oro_dot128_tree(qf, kb);
+      float sd = oro_dot128_tree(q2, var);
       float zbar = SCf * zd;
       float s2 = SC2f * sd;
       float lg = oro_logf(fmaxf(ntr[c], 1.0f));

@@ -1,0 +1,166 @@
+"""The decode step and the build on the GPU vs the CPU oracle, stage by stage.
+
+Bit-exact: new-token codes / assignments / pooled sums, zq, QGS scores, selected indices (same
+order), ErrorGate scores, tail counts, quotas, expanded indices (same order), proxies (bf16 bits),
+log n'; build: scale, codes, column means, centroids, assignments, counts, CSR lists, cluster sums.
+Tolerance (north star) on the attention output: fp32 output within 2e-3 max-abs and 1e-3 relative-L2
+of the fp64 estimator on the same indices."""
+import os
+import types
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle as O
+from helpers import state_from_fixture, to_gpu_state, to_np
+from openattention_b200 import flash as F
+from openattention_b200 import method as Mth
+from openattention_b200.geometry import HQ
+
+pytestmark = pytest.mark.gpu
+D = 128
+
+
+def _eq(name, gpu, ref):
+    g = to_np(gpu) if isinstance(gpu, torch.Tensor) else gpu
+    ref = np.asarray(ref)
+    g = g.reshape(ref.shape)
+    if not np.array_equal(g, ref):
+        bad = np.argwhere(g != ref)
+        raise AssertionError(f"{name}: {len(bad)} mismatches, first at {bad[:3].tolist()}: gpu {g[tuple(bad[0])]} "
+                             f"oracle {ref[tuple(bad[0])]}")
+
+
+def _method(B, Lmax, rho, dev="cuda"):
+    return Mth.OursB200(types.SimpleNamespace(rho=rho), B, Lmax, dev, layers=1)
+
+
+@pytest.mark.parametrize("name", list(cases.DECODE_CASES))
+def test_decode_steps_bit_exact(name, golden_dir):
+    x = cases.decode_inputs(name)
+    z = np.load(os.path.join(golden_dir, f"{name}.npz"))
+    st_np, K, V = state_from_fixture(x, z)
+    B, n0, Lmax, rho = x["B"], x["n0"], x["Lmax"], x["rho"]
+    m = _method(B, Lmax, rho)
+    C, E, R = m.C, m.E, B * HQ
+    m.st[0] = to_gpu_state(st_np)
+    Mth.C.K = [x["K"].cuda()]
+    Mth.C.V = [x["V"].cuda()]
+    Mth.C.n_dev = None
+    Mth.C.n0_dev = torch.tensor([n0], dtype=torch.int32, device="cuda")
+    for s in range(x["steps"]):
+        n = n0 + s + 1
+        Mth.C.K[0][:, :, n - 1] = x["new_k"][s].cuda()
+        Mth.C.V[0][:, :, n - 1] = x["new_v"][s].cuda()
+        K[:, :, n - 1] = O.bits(x["new_k"][s])
+        V[:, :, n - 1] = O.bits(x["new_v"][s])
+        q = x["qdec"][s]
+        qr, sel = m.select(0, q.cuda(), n)
+        torch.cuda.synchronize()
+        o = O.decode_step(st_np, O.bits(q.reshape(R, D)), K, V, n, rho, C, E)
+        g = m.st[0]
+        for k in ("codes", "asg", "nb", "Sk", "Sk2", "Sv", "reclist", "reccnt"):
+            _eq(f"step{s}.{k}", g[k], st_np[k])
+        _eq(f"step{s}.zq", m.zq, o["zq"])
+        _eq(f"step{s}.scores", m.scores[:, :n], o["s_masked"][:, :n])
+        _eq(f"step{s}.sel", sel, o["sel"])
+        _eq(f"step{s}.errorgate_score", m.score, o["score"])
+        _eq(f"step{s}.nt", m.nt, o["nt"])
+        _eq(f"step{s}.quota", m.quota, o["quota"])
+        _eq(f"step{s}.exp_idx", m.exp_idx, o["exp_idx"])
+        _eq(f"step{s}.kbar", m.kbar, o["kbar"])
+        _eq(f"step{s}.vbar", m.vbar, o["vbar"])
+        _eq(f"step{s}.logn", m.logn, o["logn"])
+        out = F.ours_flash(qr, Mth.C.K[0].view(-1, Lmax, D), Mth.C.V[0].view(-1, Lmax, D), sel, m.exp_idx, m.kbar,
+                           m.vbar, m.logn, out_dtype=torch.float32).cpu().double().numpy()
+        ref = o["out"]
+        assert np.abs(out - ref).max() <= 2e-3
+        assert np.linalg.norm(out - ref) <= 1e-3 * np.linalg.norm(ref)
+        # and the method's own bf16 output is the rounding of that
+        ob = m.attend(0, qr, sel, m.exp_idx, m.kbar, m.vbar, m.logn).float().cpu().numpy().reshape(R, D)
+        assert np.abs(ob - ref).max() <= 2e-3 + np.abs(ref).max() * 2 ** -8
+
+
+@pytest.mark.parametrize("name", list(cases.DECODE_CASES))
+def test_build_bit_exact(name, golden_dir):
+    """Build on the GPU from the reference's basis (U, W) == the oracle's build from the same basis."""
+    x = cases.decode_inputs(name)
+    z = np.load(os.path.join(golden_dir, f"{name}.npz"))
+    B, n0, Lmax, rho = x["B"], x["n0"], x["Lmax"], x["rho"]
+    m = _method(B, Lmax, rho)
+    Mth.C.K = [x["K"].cuda()]
+    Mth.C.V = [x["V"].cuda()]
+    st_np = O.new_state(B, Lmax, m.C)
+    K, V = O.bits(x["K"]), O.bits(x["V"])
+    for b in range(B):
+        U = torch.from_numpy(z["U"][b]).cuda()
+        W = O.from_bits(z["W"][b]).cuda()
+        m.build_from_basis(0, b, U, W, n0)
+        O.build_from_basis(st_np, b, K[b], V[b], z["U"][b], z["W"][b], n0, layer=0)
+    torch.cuda.synchronize()
+    g = m.st[0]
+    _eq("scale", g["scale"], st_np["scale"])
+    _eq("codes", g["codes"][:, :, :n0], st_np["codes"][:, :, :n0])
+    _eq("colmean", g["colmean"], st_np["colmean"])
+    _eq("cent", g["cent"], st_np["cent"])
+    _eq("asg", g["asg"][:, :, :n0], st_np["asg"][:, :, :n0])
+    _eq("nb", g["nb"], st_np["nb"])
+    _eq("mem", g["mem"][:, :, :n0], st_np["mem"][:, :, :n0])
+    _eq("cstart", g["cstart"], st_np["cstart"])
+    _eq("clen", g["clen"], st_np["clen"])
+    for k in ("Sk", "Sk2", "Sv"):
+        _eq(k, g[k], st_np[k])
+    # the reference's own codes and scale (same basis) are reproduced exactly
+    _eq("codes_vs_reference", g["codes"][:, :, :n0], z["codes"][:, :, :n0])
+    _eq("scale_vs_reference", g["scale"], z["scale"].reshape(B, 8, 32))
+
+
+def test_decode_graph_replay_matches_eager():
+    """One decode step captured in a CUDA graph (device-side n) replays to the same outputs as eager
+    calls, across several steps with generated tokens."""
+    from openattention_b200 import synth
+    B, n0, steps, rho = 1, 2048, 4, 0.01
+    Lmax = n0 + steps + 8
+    dev = "cuda"
+    K = torch.zeros(1, 8, Lmax, D, dtype=torch.bfloat16, device=dev)
+    V = torch.zeros_like(K)
+    Kb, Vb, mu = synth.kv_numpy(5, n0, Lmax)
+    K[0], V[0] = Kb.to(dev), Vb.to(dev)
+    qpre = synth.queries_numpy(6, HQ * n0).view(1, HQ, n0, D).to(dev)
+    outs = {}
+    for mode in ("eager", "graph"):
+        Kc, Vc = K.clone(), V.clone()
+        Mth.C.K, Mth.C.V, Mth.C.qlen = [Kc], [Vc], [40]
+        Mth.C.n_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        Mth.C.n0_dev = torch.full((1,), n0, dtype=torch.int32, device=dev)
+        m = _method(B, Lmax, rho)
+        m.build(0, 0, qpre, n0)
+        qbuf = torch.zeros(B, HQ, 1, D, dtype=torch.bfloat16, device=dev)
+        res = []
+        graph = None
+        for s in range(steps):
+            n = n0 + s + 1
+            nk, nv = synth.new_token_numpy(100 + s, mu, n - 1)
+            Kc[0, :, n - 1], Vc[0, :, n - 1] = nk.to(dev), nv.to(dev)
+            qbuf.copy_(synth.queries_numpy(200 + s, HQ).view(B, HQ, 1, D).to(dev))
+            Mth.C.n_dev.fill_(n)
+            if mode == "eager":
+                o = m.decode(0, qbuf, n)
+            else:
+                if graph is None:
+                    snap = {k: v.clone() for k, v in m.st[0].items()}
+                    m.decode(0, qbuf, n)  # warm-up outside capture, then undo its state update
+                    for k, v in snap.items():
+                        m.st[0][k].copy_(v)
+                    graph = torch.cuda.CUDAGraph()
+                    torch.cuda.synchronize()
+                    with torch.cuda.graph(graph):  # records only; replay runs the step
+                        gout = m.decode(0, qbuf, n)
+                graph.replay()
+                o = gout
+            res.append(o.clone())
+        torch.cuda.synchronize()
+        outs[mode] = torch.stack(res)
+    assert torch.equal(outs["eager"], outs["graph"])
