@@ -75,20 +75,22 @@ class Clocks:
          "clocks_event_reasons.sw_power_cap")
 
     def __init__(self, dev):
-        try:
-            self.index = torch.cuda.get_device_properties(dev).pci_bus_id
-        except AttributeError:
-            self.index = str(dev.index)
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        idx = dev.index or 0
+        self.index = ids[idx] if idx < len(ids) and ids[idx].isdigit() else str(idx)
         self.proc = None
         self.lines = []
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "20"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t_end = time.time() + 5.0
+            while not self.lines and time.time() < t_end:  # sampling has started before the timed work
+                time.sleep(0.02)
         except OSError:
             self.proc = None
         return self
@@ -108,9 +110,9 @@ class Clocks:
     def summary(self):
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
+        for ln in self.lines[1:]:  # the first sample predates the load
             f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
+            if len(f) < 9 or f[0] != self.index:
                 continue
             try:
                 sm.append(float(f[1]))
@@ -205,12 +207,12 @@ def time_scan(m, Mth, dev, iters):
     ns, nl, _ = step_split(n, RHO, m.C, m.E)
     st = m.st[0]
     for _ in range(3):
-        S.qgs_scan(st["codes"], m.zq, Mth.C.n_dev, ns, nl, m.scores, m.tmax)
+        S.qgs_scan(st["codes"], m.zq, Mth.C.n_dev, ns, nl, m.scores, m.tmax, m.status)
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(iters):
-        S.qgs_scan(st["codes"], m.zq, Mth.C.n_dev, ns, nl, m.scores, m.tmax)
+        S.qgs_scan(st["codes"], m.zq, Mth.C.n_dev, ns, nl, m.scores, m.tmax, m.status)
     e1.record()
     torch.cuda.synchronize()
     return e0.elapsed_time(e1) / iters, n

@@ -100,9 +100,12 @@ int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64
 
 /* QGS scan: scores (B*32, score_stride) bf16 = exact int8 dot products of codes and zq, rounded to
  * fp32 then bf16, -inf for t < ns and t >= n - nl; tile_max (B*32, tile_max_stride) fp32 = maximum
- * of each 256-token tile.  Replaces _k_qgs_scan_tm (inference/graph_runner.py:100-120). */
+ * of each 256-token tile.  Replaces _k_qgs_scan_tm (inference/graph_runner.py:100-120).
+ * status (may be NULL): device int32 set to 1 if a bulk copy of the codes did not complete within
+ * the kernel's bounded wait (the affected tiles are then not computed). */
 int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64_t Lmax, const int32_t* n_dev, int ns, int nl,
-                void* scores, int64_t score_stride, float* tile_max, int64_t tile_max_stride, void* stream);
+                void* scores, int64_t score_stride, float* tile_max, int64_t tile_max_stride, int32_t* status,
+                void* stream);
 
 /* Row top-k among the 2k tiles with the largest maxima (exact), ties -> lower position;
  * sel (R, ns+nl+k_top) int32 = [0..ns-1, n-nl..n-1, top-k by rank]; the selected scores are set to
@@ -114,29 +117,34 @@ int oa_qgs_select(void* scores, int64_t score_stride, const float* tile_max, int
  * selected tokens), score = zbar + ln n + s2/2 + ln erf(sqrt(s2/2)), quotas q_b = min(n_b,
  * floor(lambda w_b)) plus leftover whole tokens to the best-scoring clusters with room.
  * Outputs score, nt (tail counts) and quota, each (B*32, C) fp32.  Replaces _k_errorgate +
- * _k_waterfill (inference/ours_fused.py:122-216).  C <= 256, n_sel <= 512. */
+ * _k_waterfill (inference/ours_fused.py:122-216).  C <= 256, n_sel <= 512.  status (may be NULL):
+ * device int32 set to 2 if a bulk copy of the pooled sums did not complete in the bounded wait. */
 int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64_t B, int64_t Lmax, int64_t C,
                            const int32_t* asg, const int32_t* sel, int64_t n_sel, const float* Sk, const float* Sk2,
-                           const float* nb, float E, float* score, float* nt, float* quota, void* stream);
+                           const float* nb, float E, float* score, float* nt, float* quota, int32_t* status,
+                           void* stream);
 
-/* Within-cluster top-q: for each cluster with quota q > 0, its q best members (CSR members, then
- * generated tokens) by QGS score (selected tokens already -inf), ties -> lower position, written to
- * exp_idx (R, E) int32 at the cluster's offset sum_{c'<c} q_c' in ascending position; -1 pads.
- * reclist may be NULL (generated tokens are then found by scanning asg over [n0, n)).
+/* Within-cluster top-q: for each cluster with quota q > 0, its q best members by QGS score (the
+ * selected tokens are already -inf), ties -> lower position, written to exp_idx (R, E) int32 at the
+ * cluster's offset sum_{c'<c} q_c' in ascending position; -1 pads.  Candidates are the cluster's CSR
+ * members (positions < n0) and its generated tokens: reclist (may be NULL) while it holds them all
+ * (reccnt <= rmax), else positions in [n0, n) with asg == c.  C <= 256.  status (may be NULL): set to
+ * 4 if the bulk copy of the score row did not complete in the bounded wait.
  * Replaces _k_topq_d2 (inference/ours_graph.py:93-166). */
 int oa_topq(const void* scores, int64_t score_stride, int64_t R, int64_t Lmax, int64_t C, const int32_t* mem,
             const int32_t* cstart, const int32_t* clen, const int32_t* asg, const int32_t* reclist,
             const int32_t* reccnt, int rmax, const float* quota, int64_t E, const int32_t* n_dev,
-            const int32_t* n0_dev, int32_t* exp_idx, void* stream);
+            const int32_t* n0_dev, int32_t* exp_idx, int32_t* status, void* stream);
 
 /* Residual proxies: per (row, cluster) the pooled sums minus every token read (sel in order, then
  * the cluster's exp segment), n' = nt - quota, kbar' / vbar' = bf16(sums / max(n', 1)) (R, C, 128),
  * log_n = ln max(n', 1) if n' > 0.5 else -inf (R, C) fp32.  Replaces _k_resid_scatter +
- * _k_resid_norm (inference/ours_fused.py:367-407), without atomics. */
+ * _k_resid_norm (inference/ours_fused.py:367-407), without atomics.  status: as oa_errorgate_waterfill
+ * (value 3). */
 int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, const int32_t* asg,
                 const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E, const float* Sk,
                 const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar, float* log_n,
-                void* stream);
+                int32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * Per-request build (prefill).  Each call works on ONE request: K, V (8, Lmax, 128) bf16 with the

@@ -341,8 +341,8 @@ extern "C" int oa_kmeans_assign(const float* zP, int64_t T, int64_t C, const flo
     cudaError_t e = cudaFuncSetAttribute(kmeans_assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
   }
-  kmeans_assign_kernel<<<dim3((unsigned)((T + kBT - 1) / kBT), kHQ), kBT, smem, S(stream)>>>(zP, (int)T, (int)C, cent,
-                                                                                             asg, asg_stride);
+  kmeans_assign_kernel<<<dim3((unsigned)((T + kBT - 1) / kBT), kHQ), kBT, smem, S(stream)>>>(
+      zP, (int)T, (int)C, cent, asg, asg_stride);
   return oa_check_launch(fn);
 }
 

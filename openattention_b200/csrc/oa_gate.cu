@@ -46,7 +46,10 @@ struct GateArgs {
   float* score;
   float* nt;
   float* quota;
+  int32_t* status;
 };
+
+constexpr int kChunkC = 64;  // clusters whose pooled-sum rows are staged in shared memory at once
 
 __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const GateArgs a) {
   const int r = blockIdx.x;
@@ -72,15 +75,27 @@ __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const
     q2[i] = __fmul_rn(qv[i], qv[i]);
   }
   __syncthreads();
-  // ---- ErrorGate: warp per cluster
-  for (int c = warp; c < C; c += kGateThreads / 32) {
-    float skt[4], sk2t[4];
-    const int64_t base = ((int64_t)r * C + c) * kD;
+  // ---- ErrorGate: warp per cluster; the next cluster's pooled-sum rows are requested before the
+  //      current one is processed
+  constexpr int kStride = kGateThreads / 32;
+  float nk[4], nk2[4];
+  auto fetch = [&](int c, float (&x)[4], float (&x2)[4]) {
+    const int64_t base = ((int64_t)r * C + min(c, C - 1)) * kD;
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-      skt[i] = a.Sk[base + lane + 32 * i];
-      sk2t[i] = a.Sk2[base + lane + 32 * i];
+      x[i] = a.Sk[base + lane + 32 * i];
+      x2[i] = a.Sk2[base + lane + 32 * i];
     }
+  };
+  if (warp < C) fetch(warp, nk, nk2);
+  for (int c = warp; c < C; c += kStride) {
+    float skt[4], sk2t[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      skt[i] = nk[i];
+      sk2t[i] = nk2[i];
+    }
+    if (c + kStride < C) fetch(c + kStride, nk, nk2);
     float ntc = a.nb[(int64_t)r * C + c];
     for (int j = 0; j < a.NS; ++j) {
       if (s_selc[j] != c) continue;
@@ -105,17 +120,22 @@ __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const
     const float zd = warp_tree_dot(qv, kb);
     const float sd = warp_tree_dot(q2, var);
     if (lane == 0) {
-      const float zbar = __fmul_rn(0.08838834764831845f, zd);
-      const float s2 = __fmul_rn(0.0078125f, sd);
-      const float lg = ln_f(fmaxf(ntc, 1.f));
-      const float er = erf_f(__fmul_rn(__fsqrt_rn(s2), 0.70710677f));
-      const float le = ln_f(fmaxf(er, 1e-30f));
-      float sc = __fadd_rn(zbar, lg);
-      sc = __fadd_rn(sc, __fmul_rn(0.5f, s2));
-      sc = __fadd_rn(sc, le);
-      s_score[c] = sc;
+      s_w[c] = zd;  // staging: dots and tail counts, the scalar tail runs one thread per cluster below
+      s_cap[c] = sd;
       s_nt[c] = ntc;
     }
+  }
+  __syncthreads();
+  if (tid < C) {
+    const float zbar = __fmul_rn(0.08838834764831845f, s_w[tid]);
+    const float s2 = __fmul_rn(0.0078125f, s_cap[tid]);
+    const float lg = ln_f(fmaxf(s_nt[tid], 1.f));
+    const float er = erf_f(__fmul_rn(__fsqrt_rn(s2), 0.70710677f));
+    const float le = ln_f(fmaxf(er, 1e-30f));
+    float sc = __fadd_rn(zbar, lg);
+    sc = __fadd_rn(sc, __fmul_rn(0.5f, s2));
+    sc = __fadd_rn(sc, le);
+    s_score[tid] = sc;
   }
   __syncthreads();
   // ---- water-filling (thread c <-> cluster c)
@@ -140,9 +160,19 @@ __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const
     s_cap[c] = cap;
     s_ratio[c] = ratio;
   }
-  __syncthreads();
-  float tot = 0.f;  // integer-valued: exact in any order
-  for (int j = 0; j < C; ++j) tot = __fadd_rn(tot, s_cap[j]);
+  // integer-valued sums (< 2^24): exact in any order, so a block reduction gives the sequential value
+  auto block_sum = [&](float v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, off));
+    __syncthreads();
+    if (lane == 0) s_red[warp] = v;
+    __syncthreads();
+    float t = 0.f;
+#pragma unroll
+    for (int w = 0; w < kGateThreads / 32; ++w) t = __fadd_rn(t, s_red[w]);
+    return t;
+  };
+  const float tot = block_sum(act ? cap : 0.f);
   if (act) {
     // rank by (ratio asc, cluster asc); rank by (score desc, cluster asc)
     int r1 = 0, r2 = 0;
@@ -191,9 +221,7 @@ __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const
     if (tot <= a.E) qb = cap;
     s_qb[c] = qb;
   }
-  __syncthreads();
-  float sumq = 0.f;
-  for (int j = 0; j < C; ++j) sumq = __fadd_rn(sumq, s_qb[j]);
+  const float sumq = block_sum(act ? qb : 0.f);
   const float rem = fmaxf(__fsub_rn(fminf(tot, a.E), sumq), 0.f);
   if (act) {
     const bool room = qb < cap;
@@ -208,13 +236,23 @@ __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const
 }
 
 // ------------------------------------------------------------------------ within-cluster top-q
-constexpr int kTopqWarps = 8;
-constexpr int kCap = 1536;  // candidates held in shared memory per warp (larger clusters stream)
+// One CTA (16 warps) per row.  The row's bf16 score spill is staged in shared memory by one bulk
+// copy when it fits (else keys are read from global memory).  Warps take the clusters with q > 0:
+// the candidates are the cluster's CSR members (ascending position) followed by its generated
+// tokens (the per-cluster list, or a scan of asg over [n0, n) when the list overflowed).
+//   q <= 32 and <= 1024 candidates: packed (key, list index) words in registers, q rounds of warp
+//     max extraction (ties -> lower list index = lower position), winners sorted by position
+//   otherwise: two 8-bit radix passes for the threshold key, then an ordered collection
+constexpr int kTqThreads = 512;
+constexpr int kTqWarps = kTqThreads / 32;
+constexpr int kRegCand = 32;  // candidates per lane in the register path
+constexpr int kSmallQ = 32;
+constexpr int kU = 4;         // 32-candidate chunks whose loads are issued together (radix path)
 
 struct TopqArgs {
   const uint16_t* scores;
   int64_t sw;
-  int Lmax, C, E, rmax;
+  int Lmax, C, E, rmax, smem_keys;
   const int32_t* mem;
   const int32_t* cstart;
   const int32_t* clen;
@@ -225,180 +263,201 @@ struct TopqArgs {
   const int32_t* n_dev;
   const int32_t* n0_dev;
   int32_t* exp;
+  int32_t* status;
 };
 
 __device__ __forceinline__ uint32_t ukey16(uint32_t b) { return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u); }
 
-// Candidate i of cluster c (members in CSR order, then generated tokens in position order).
-struct CandSrc {
-  const int32_t* mem;   // member list of (r, c)
-  int nmem;
-  const int32_t* rec;   // generated-token list, or nullptr to scan [n0, n)
-  int nrec;
-  const int32_t* asg_r;
-  int n0, n, c;
-};
-
-__global__ void __launch_bounds__(kTopqWarps * 32) topq_kernel(const TopqArgs a) {
+__global__ void __launch_bounds__(kTqThreads, 1) topq_kernel(const TopqArgs a) {
+  extern __shared__ __align__(128) uint16_t s_spill[];  // the row's scores (when a.smem_keys)
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int s_base[kMaxC + 1];
+  __shared__ int s_q[kMaxC];
+  __shared__ int s_next;
+  __shared__ int s_hist[kTqWarps][256];
   const int r = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int C = a.C;
   const int n = __ldg(a.n_dev), n0 = __ldg(a.n0_dev);
-  __shared__ int s_base[kMaxC + 1];
-  __shared__ int s_next;
-  extern __shared__ __align__(16) unsigned char topq_smem[];
-  int32_t* s_tok = reinterpret_cast<int32_t*>(topq_smem);                              // [warps][kCap]
-  int* s_hist = reinterpret_cast<int*>(s_tok + kTopqWarps * kCap);                      // [warps][256]
-  uint16_t* s_key = reinterpret_cast<uint16_t*>(s_hist + kTopqWarps * 256);              // [warps][kCap]
+  const uint16_t* sr = a.scores + (int64_t)r * a.sw;
+  const uint32_t bar = smem_u32(&mbar);
+  const int nbytes = ((min(n, a.Lmax) + 7) & ~7) * 2;
+  if (tid == 0) {
+    mbar_init(bar);
+    if (a.smem_keys && nbytes > 0) bulk_load(s_spill, sr, (uint32_t)nbytes, bar);
+    s_next = 0;
+  }
+  for (int c = tid; c < C; c += kTqThreads) s_q[c] = (int)a.quota[(int64_t)r * C + c];
+  __syncthreads();
   if (tid == 0) {
     int run = 0;
     for (int c = 0; c < C; ++c) {
       s_base[c] = run;
-      run += (int)a.quota[(int64_t)r * C + c];
+      run += s_q[c];
     }
     s_base[C] = run;
-    s_next = 0;
   }
   __syncthreads();
   int32_t* out = a.exp + (int64_t)r * a.E;
-  for (int i = s_base[C] + tid; i < a.E; i += blockDim.x) out[i] = -1;
-  const uint16_t* sr = a.scores + (int64_t)r * a.sw;
+  for (int i = s_base[C] + tid; i < a.E; i += kTqThreads) out[i] = -1;
+  const bool ok = !(a.smem_keys && nbytes > 0) || mbar_wait(bar, 0);
+  if (!__syncthreads_and(ok)) {
+    if (tid == 0 && a.status != nullptr) atomicExch(a.status, 4);
+    if (!ok) mbar_wait(bar, 0);
+    return;
+  }
+  const uint16_t* keys = a.smem_keys ? s_spill : sr;
   const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
-  uint16_t* keys = s_key + warp * kCap;
-  int32_t* toks = s_tok + warp * kCap;
-  int* hist = s_hist + warp * 256;
+  int* hist = s_hist[warp];
+  const unsigned lt = (1u << lane) - 1u;
   while (true) {
     int c = 0;
-    if (lane == 0) c = atomicAdd(&s_next, 1);
+    if (lane == 0) {
+      do {
+        c = atomicAdd(&s_next, 1);
+      } while (c < C && s_q[c] <= 0);
+    }
     c = __shfl_sync(0xffffffffu, c, 0);
     if (c >= C) break;
-    const int q = s_base[c + 1] - s_base[c];
-    if (q <= 0) continue;
-    const int base = s_base[c];
+    const int q = s_q[c], base = s_base[c];
     const int64_t rc = (int64_t)r * C + c;
     const int nmem = a.clen[rc];
-    const int32_t* mem = a.mem + (int64_t)r * a.Lmax + a.cstart[rc];
+    const int32_t* mp = a.mem + (int64_t)r * a.Lmax + a.cstart[rc];
     const int cnt = a.reclist ? a.reccnt[rc] : 0x7fffffff;
     const bool use_list = a.reclist != nullptr && cnt <= a.rmax;
     const int32_t* rec = use_list ? a.reclist + rc * a.rmax : nullptr;
+    const int ngen = use_list ? cnt : 0;
+    if (use_list && q <= kSmallQ && nmem + ngen <= 32 * kRegCand) {
+      // ---- register path
+      const int m = nmem + ngen;
+      uint32_t v[kRegCand];
+#pragma unroll
+      for (int i = 0; i < kRegCand; ++i) {
+        const int idx = i * 32 + lane;
+        v[i] = idx < nmem ? (uint32_t)mp[idx] : (idx < m ? (uint32_t)rec[idx - nmem] : 0xffffffffu);
+      }
+#pragma unroll
+      for (int i = 0; i < kRegCand; ++i) {
+        const int idx = i * 32 + lane;
+        v[i] = v[i] == 0xffffffffu ? 0u : (ukey16(keys[v[i]]) << 16) | (uint32_t)(0xffff - idx);
+      }
+      int my_idx = 0x7fffffff;  // list index of the winner this lane records (lane k <-> k-th winner)
+      for (int k = 0; k < q; ++k) {
+        uint32_t lm = 0u;
+#pragma unroll
+        for (int i = 0; i < kRegCand; ++i) lm = max(lm, v[i]);
+        uint32_t wm = lm;
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) wm = max(wm, __shfl_xor_sync(0xffffffffu, wm, off));
+        if (wm == 0u) break;
+        if (lm == wm) {  // unique owner (list indices are unique)
+#pragma unroll
+          for (int i = 0; i < kRegCand; ++i)
+            if (v[i] == wm) v[i] = 0u;
+        }
+        if (lane == k) my_idx = 0xffff - (int)(wm & 0xffffu);
+      }
+      // winners in position order: rank of my_idx among the q recorded indices
+      int rank = 0;
+      for (int j = 0; j < q; ++j) {
+        const int o = __shfl_sync(0xffffffffu, my_idx, j);
+        rank += (o < my_idx) ? 1 : 0;
+      }
+      if (lane < q && my_idx != 0x7fffffff) out[base + rank] = my_idx < nmem ? mp[my_idx] : rec[my_idx - nmem];
+      continue;
+    }
+    // ---- radix path: candidates enumerated in order (members, then generated tokens)
     const int ngen_scan = max(0, n - n0);
-    // enumerate candidates in order: members, then generated tokens (list, or scan of [n0, n))
-    // chunks of 32; f(tok, key) is applied to each candidate in order
     auto for_each = [&](auto&& f) {
-      for (int i0 = 0; i0 < nmem; i0 += 32) {
-        const int i = i0 + lane;
-        const bool v = i < nmem;
-        const int t = v ? mem[i] : 0;
-        const uint32_t k = v ? ukey16(sr[t]) : 0u;
-        f(v, t, k);
+      for (int i0 = 0; i0 < nmem; i0 += 32 * kU) {
+        int t[kU];
+        bool v[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+          const int i = i0 + 32 * u + lane;
+          v[u] = i < nmem;
+          t[u] = v[u] ? mp[i] : 0;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u)
+          if (i0 + 32 * u < nmem) f(v[u], t[u], v[u] ? ukey16(keys[t[u]]) : 0u);
       }
       if (use_list) {
         for (int i0 = 0; i0 < cnt; i0 += 32) {
           const int i = i0 + lane;
           const bool v = i < cnt;
           const int t = v ? rec[i] : 0;
-          const uint32_t k = v ? ukey16(sr[t]) : 0u;
-          f(v, t, k);
+          f(v, t, v ? ukey16(keys[t]) : 0u);
         }
       } else {
         for (int i0 = 0; i0 < ngen_scan; i0 += 32) {
           const int t = n0 + i0 + lane;
           const bool v = (i0 + lane < ngen_scan) && asg_r[t] == c;
-          const uint32_t k = v ? ukey16(sr[t]) : 0u;
-          f(v, t, k);
+          f(v, t, v ? ukey16(keys[t]) : 0u);
         }
       }
     };
-    const int total = nmem + (use_list ? cnt : ngen_scan);
-    const bool in_smem = total <= kCap;
-    int m = 0;  // compacted candidate count (in smem mode)
-    if (in_smem) {
-      for_each([&](bool v, int t, uint32_t k) {
-        const unsigned bal = __ballot_sync(0xffffffffu, v);
-        const int pos = m + __popc(bal & ((1u << lane) - 1u));
-        if (v) {
-          keys[pos] = (uint16_t)k;
-          toks[pos] = t;
-        }
-        m += __popc(bal);
-      });
-      __syncwarp();
-    }
-    // two 8-bit radix passes: threshold key T = the q-th largest key
     int above = 0, hi = 0, lo = 0;
-    for (int pass = 0; pass < 2; ++pass) {
+    bool all = false;
+    for (int pass = 0; pass < 2 && !all; ++pass) {
       for (int b = lane; b < 256; b += 32) hist[b] = 0;
       __syncwarp();
-      auto add = [&](bool v, int t, uint32_t k) {
+      for_each([&](bool v, int t, uint32_t k) {
         if (v && (pass == 0 || (int)(k >> 8) == hi)) atomicAdd(&hist[pass == 0 ? (k >> 8) : (k & 255)], 1);
-      };
-      if (in_smem) {
-        for (int i = lane; i < m; i += 32) add(true, 0, keys[i]);
-      } else {
-        for_each(add);
-      }
+      });
       __syncwarp();
-      // find the bin (from the top) where the running count reaches q: lane l owns bins 255-8l..248-8l
-      int cnt8[8], s = 0;
+      int cnt8[8], sum = 0;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         cnt8[i] = hist[255 - 8 * lane - i];
-        s += cnt8[i];
+        sum += cnt8[i];
       }
-      int incl = s;
+      int incl = sum;
 #pragma unroll
       for (int off = 1; off < 32; off <<= 1) {
         const int o = __shfl_up_sync(0xffffffffu, incl, off);
         if (lane >= off) incl += o;
       }
-      const int excl = incl - s;
+      const int excl = incl - sum;
       const int need = q - above;
-      int found_bin = -1, found_above = 0;
+      int fb = -1, fa = 0;
       if (excl < need && incl >= need) {
         int run = excl;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          if (found_bin < 0 && run + cnt8[i] >= need) {
-            found_bin = 255 - 8 * lane - i;
-            found_above = run;
+          if (fb < 0 && run + cnt8[i] >= need) {
+            fb = 255 - 8 * lane - i;
+            fa = run;
           }
           run += cnt8[i];
         }
       }
-      const unsigned who = __ballot_sync(0xffffffffu, found_bin >= 0);
-      const int src = who ? (__ffs(who) - 1) : 0;
-      const int fb = __shfl_sync(0xffffffffu, found_bin, src);
-      const int fa = __shfl_sync(0xffffffffu, found_above, src);
-      if (pass == 0) hi = fb < 0 ? 0 : fb;
-      else lo = fb < 0 ? 0 : fb;
-      above += fa;
+      const unsigned who = __ballot_sync(0xffffffffu, fb >= 0);
+      if (who == 0u) {
+        all = true;  // fewer candidates than q: take every one
+      } else {
+        const int src = __ffs(who) - 1;
+        const int d = __shfl_sync(0xffffffffu, fb, src);
+        above += __shfl_sync(0xffffffffu, fa, src);
+        if (pass == 0) hi = d;
+        else lo = d;
+      }
       __syncwarp();
     }
-    const uint32_t T = ((uint32_t)hi << 8) | (uint32_t)lo;
-    const int need_eq = q - above;
-    // collect in candidate order: keys > T, and the first need_eq keys == T
+    const uint32_t T = all ? 0u : (((uint32_t)hi << 8) | (uint32_t)lo);
+    const int need_eq = all ? 0 : q - above;
     int taken = 0, ties = 0;
-    auto collect = [&](bool v, int t, uint32_t k) {
+    for_each([&](bool v, int t, uint32_t k) {
       const bool gt = v && k > T;
       const bool eq = v && k == T;
       const unsigned beq = __ballot_sync(0xffffffffu, eq);
-      const int er = ties + __popc(beq & ((1u << lane) - 1u));
-      const bool take = gt || (eq && er < need_eq);
+      const bool take = gt || (eq && ties + __popc(beq & lt) < need_eq);
       const unsigned bt = __ballot_sync(0xffffffffu, take);
-      const int slot = taken + __popc(bt & ((1u << lane) - 1u));
-      if (take && slot < q && base + slot < a.E) out[base + slot] = t;
+      const int slot = taken + __popc(bt & lt);
+      if (take && slot < q) out[base + slot] = t;
       taken += __popc(bt);
       ties += __popc(beq);
-    };
-    if (in_smem) {
-      for (int i0 = 0; i0 < m; i0 += 32) {
-        const int i = i0 + lane;
-        const bool v = i < m;
-        collect(v, v ? toks[i] : 0, v ? keys[i] : 0u);
-      }
-    } else {
-      for_each(collect);
-    }
+    });
     __syncwarp();
   }
 }
@@ -418,63 +477,116 @@ struct ResidArgs {
   __nv_bfloat16* kbar;
   __nv_bfloat16* vbar;
   float* logn;
+  int32_t* status;
 };
+
+constexpr int kTokChunk = 64;   // read tokens whose K/V rows are gathered into shared memory at once
+constexpr int kMaxRead = 2048;  // NS + E
 
 __global__ void __launch_bounds__(kGateThreads) residual_kernel(const ResidArgs a) {
   const int r = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kv = r / kG;
   const int C = a.C;
+  extern __shared__ __align__(128) float rsm[];
+  float* sSk = rsm;                                                    // [kChunkC][kD]
+  float* sSv = rsm + kChunkC * kD;                                     // [kChunkC][kD]
+  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(rsm + 2 * kChunkC * kD);  // [kTokChunk][kD]
+  __nv_bfloat16* sV = sK + kTokChunk * kD;                                         // [kTokChunk][kD]
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int s_tok[kMaxRead];
+  __shared__ int16_t s_tc[kMaxRead];
   __shared__ int s_base[kMaxC + 1];
-  __shared__ int s_selc[512], s_selt[512];
-  for (int j = tid; j < a.NS; j += blockDim.x) {
-    const int t = a.sel[(int64_t)r * a.NS + j];
-    s_selt[j] = t;
-    s_selc[j] = (t >= 0 && t < a.Lmax) ? a.asg[(int64_t)r * a.Lmax + t] : -1;
-  }
+  __shared__ int s_q[kMaxC];
+  const uint32_t bar = smem_u32(&mbar);
+  if (tid == 0) mbar_init(bar);
+  for (int c = tid; c < C; c += blockDim.x) s_q[c] = (int)a.quota[(int64_t)r * C + c];
+  __syncthreads();
   if (tid == 0) {
     int run = 0;
     for (int c = 0; c < C; ++c) {
       s_base[c] = run;
-      run += (int)a.quota[(int64_t)r * C + c];
+      run += s_q[c];
     }
     s_base[C] = run;
+  }
+  const int NT = a.NS + a.E;
+  // the row's read tokens in subtraction order (sel, then exp slots) with their clusters
+  for (int j = tid; j < NT; j += blockDim.x) {
+    const int t = j < a.NS ? a.sel[(int64_t)r * a.NS + j] : a.exp[(int64_t)r * a.E + (j - a.NS)];
+    const bool v = t >= 0 && t < a.Lmax;
+    s_tok[j] = v ? t : -1;
+    s_tc[j] = v ? (int16_t)a.asg[(int64_t)r * a.Lmax + t] : (int16_t)-1;
   }
   __syncthreads();
   const __nv_bfloat16* Kr = a.K + (int64_t)kv * a.Lmax * kD;
   const __nv_bfloat16* Vr = a.V + (int64_t)kv * a.Lmax * kD;
-  for (int c = warp; c < C; c += kGateThreads / 32) {
-    const int64_t base = ((int64_t)r * C + c) * kD;
-    float sk[4], sv[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      sk[i] = a.Sk[base + lane + 32 * i];
-      sv[i] = a.Sv[base + lane + 32 * i];
+  uint32_t phase = 0;
+  for (int c0 = 0; c0 < C; c0 += kChunkC) {
+    const int nc = min(kChunkC, C - c0);
+    if (tid == 0) {
+      const uint32_t bytes = (uint32_t)nc * kD * sizeof(float);
+      mbar_expect(bar, 2 * bytes);
+      bulk_copy(sSk, a.Sk + ((int64_t)r * C + c0) * kD, bytes, bar);
+      bulk_copy(sSv, a.Sv + ((int64_t)r * C + c0) * kD, bytes, bar);
     }
-    auto sub = [&](int t) {
-      const __nv_bfloat16* kr = Kr + (int64_t)t * kD;
-      const __nv_bfloat16* vr = Vr + (int64_t)t * kD;
+    const bool ok = mbar_wait(bar, phase);
+    phase ^= 1u;
+    if (!__syncthreads_and(ok)) {
+      if (tid == 0 && a.status != nullptr) atomicExch(a.status, 3);
+      if (!ok) mbar_wait(bar, phase ^ 1u);
+      return;
+    }
+    for (int j0 = 0; j0 < NT; j0 += kTokChunk) {
+      const int nj = min(kTokChunk, NT - j0);
+      // gather the chunk's K and V rows: 16 bytes per cp.async, 2 * 16 per row
+      for (int e = tid; e < nj * 32; e += blockDim.x) {
+        const int j = e >> 5, part = e & 31;  // part < 16: K row, else V row
+        const int t = s_tok[j0 + j];
+        const int tc = s_tc[j0 + j];
+        if (t >= 0 && tc >= c0 && tc < c0 + nc) {
+          const __nv_bfloat16* src = (part < 16 ? Kr : Vr) + (int64_t)t * kD + (part & 15) * 8;
+          __nv_bfloat16* dst = (part < 16 ? sK : sV) + j * kD + (part & 15) * 8;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+        }
+      }
+      asm volatile("cp.async.wait_all;" ::: "memory");
+      __syncthreads();
+      // subtract in order, each (cluster, dim) by one thread: warp per cluster, lane per 4 dims.
+      // A cluster's tokens in this chunk: its selected tokens (list positions < NS, checked one by
+      // one) and the part of its exp segment [NS + base_c, NS + base_c + q_c) inside the chunk.
+      for (int cc = warp; cc < nc; cc += kGateThreads / 32) {
+        const int c = c0 + cc;
+        auto sub = [&](int j) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int d = lane + 32 * i;
+            sSk[cc * kD + d] = __fsub_rn(sSk[cc * kD + d], __bfloat162float(sK[j * kD + d]));
+            sSv[cc * kD + d] = __fsub_rn(sSv[cc * kD + d], __bfloat162float(sV[j * kD + d]));
+          }
+        };
+        for (int j = j0; j < min(j0 + nj, a.NS); ++j)
+          if (s_tc[j] == c) sub(j - j0);
+        const int e_lo = max(j0, a.NS + s_base[c]), e_hi = min(j0 + nj, a.NS + min(s_base[c + 1], a.E));
+        for (int j = e_lo; j < e_hi; ++j)
+          if (s_tok[j] >= 0) sub(j - j0);
+      }
+      __syncthreads();  // the gather buffer is refilled by the next chunk
+    }
+    for (int cc = warp; cc < nc; cc += kGateThreads / 32) {
+      const int c = c0 + cc;
+      const int64_t base = ((int64_t)r * C + c) * kD;
+      const float nr = __fsub_rn(a.nt[(int64_t)r * C + c], a.quota[(int64_t)r * C + c]);
+      const float inv = __fdiv_rn(1.f, fmaxf(nr, 1.f));
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        sk[i] = __fsub_rn(sk[i], __bfloat162float(kr[lane + 32 * i]));
-        sv[i] = __fsub_rn(sv[i], __bfloat162float(vr[lane + 32 * i]));
+        const int d = lane + 32 * i;
+        a.kbar[base + d] = __float2bfloat16_rn(__fmul_rn(sSk[cc * kD + d], inv));
+        a.vbar[base + d] = __float2bfloat16_rn(__fmul_rn(sSv[cc * kD + d], inv));
       }
-    };
-    for (int j = 0; j < a.NS; ++j)
-      if (s_selc[j] == c) sub(s_selt[j]);
-    const int e0 = s_base[c], e1 = min(s_base[c + 1], a.E);
-    for (int s = e0; s < e1; ++s) {
-      const int t = a.exp[(int64_t)r * a.E + s];
-      if (t >= 0 && t < a.Lmax) sub(t);
+      if (lane == 0) a.logn[(int64_t)r * C + c] = nr > 0.5f ? ln_f(fmaxf(nr, 1.f)) : -INFINITY;
     }
-    const float nr = __fsub_rn(a.nt[(int64_t)r * C + c], a.quota[(int64_t)r * C + c]);
-    const float inv = __fdiv_rn(1.f, fmaxf(nr, 1.f));
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      a.kbar[base + lane + 32 * i] = __float2bfloat16_rn(__fmul_rn(sk[i], inv));
-      a.vbar[base + lane + 32 * i] = __float2bfloat16_rn(__fmul_rn(sv[i], inv));
-    }
-    if (lane == 0) a.logn[(int64_t)r * C + c] = nr > 0.5f ? ln_f(fmaxf(nr, 1.f)) : -INFINITY;
+    __syncthreads();  // the pooled-sum buffers are refilled by the next cluster chunk
   }
 }
 
@@ -486,14 +598,14 @@ using namespace oa;
 extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64_t B, int64_t Lmax,
                                       int64_t C, const int32_t* asg, const int32_t* sel, int64_t n_sel,
                                       const float* Sk, const float* Sk2, const float* nb, float E, float* score,
-                                      float* nt, float* quota, void* stream) {
+                                      float* nt, float* quota, int32_t* status, void* stream) {
   const char* fn = "oa_errorgate_waterfill";
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= kMaxC, "%s: need 0 < C <= %d (C=%lld)", fn, kMaxC, (long long)C);
   OA_REQUIRE(n_sel > 0 && n_sel <= 512, "%s: n_sel=%lld outside [1, 512]", fn, (long long)n_sel);
   OA_REQUIRE(q && K && asg && sel && Sk && Sk2 && nb && score && nt && quota, "%s: null pointer", fn);
   OA_REQUIRE(E >= 0.f, "%s: negative budget", fn);
   GateArgs a{static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(K), (int)Lmax, (int)C,
-             (int)n_sel, asg, sel, Sk, Sk2, nb, E, score, nt, quota};
+             (int)n_sel, asg, sel, Sk, Sk2, nb, E, score, nt, quota, status};
   errorgate_waterfill_kernel<<<(unsigned)(B * kHQ), kGateThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }
@@ -501,37 +613,47 @@ extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const voi
 extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int64_t Lmax, int64_t C,
                        const int32_t* mem, const int32_t* cstart, const int32_t* clen, const int32_t* asg,
                        const int32_t* reclist, const int32_t* reccnt, int rmax, const float* quota, int64_t E,
-                       const int32_t* n_dev, const int32_t* n0_dev, int32_t* exp_idx, void* stream) {
+                       const int32_t* n_dev, const int32_t* n0_dev, int32_t* exp_idx, int32_t* status,
+                       void* stream) {
   const char* fn = "oa_topq";
-  OA_REQUIRE(R > 0 && Lmax > 0 && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
-  OA_REQUIRE(score_stride >= Lmax, "%s: score stride < Lmax", fn);
+  OA_REQUIRE(R > 0 && Lmax > 0 && Lmax < (1 << 30) && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
+  OA_REQUIRE(score_stride >= ((Lmax + 7) & ~7ll) && score_stride % 8 == 0 && oa_aligned16(scores),
+             "%s: score rows must be 16-byte aligned and hold Lmax rounded up to 8", fn);
   OA_REQUIRE(scores && mem && cstart && clen && asg && quota && n_dev && n0_dev && exp_idx, "%s: null pointer", fn);
   OA_REQUIRE(reclist == nullptr || (reccnt != nullptr && rmax > 0), "%s: reclist needs reccnt and rmax", fn);
-  TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, mem, cstart, clen,
-             asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx};
-  constexpr size_t smem = (size_t)kTopqWarps * (kCap * 6 + 256 * 4);
-  static bool attr_set = false;  // idempotent attribute, set once per process
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(topq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-    attr_set = true;
-  }
-  topq_kernel<<<(unsigned)R, kTopqWarps * 32, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  const size_t spill_bytes = (size_t)((Lmax + 7) & ~7ll) * 2;
+  const bool in_smem = spill_bytes <= 160 * 1024;  // larger rows read their keys from global memory
+  TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, in_smem ? 1 : 0,
+             mem, cstart, clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};
+  const size_t smem = in_smem ? spill_bytes : 16;
+  cudaError_t e = cudaFuncSetAttribute(topq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+  topq_kernel<<<(unsigned)R, kTqThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }
 
 extern "C" int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, const int32_t* asg,
                            const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E, const float* Sk,
                            const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar, float* logn,
-                           void* stream) {
+                           int32_t* status, void* stream) {
   const char* fn = "oa_residual";
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
   OA_REQUIRE(n_sel > 0 && n_sel <= 512, "%s: n_sel outside [1, 512]", fn);
   OA_REQUIRE(K && V && asg && sel && exp_idx && Sk && Sv && nt && quota && kbar && vbar && logn, "%s: null pointer",
              fn);
+  OA_REQUIRE(oa_aligned16(Sk) && oa_aligned16(Sv) && oa_aligned16(K) && oa_aligned16(V),
+             "%s: Sk / Sv / K / V must be 16-byte aligned", fn);
+  OA_REQUIRE(n_sel + E <= kMaxRead, "%s: n_sel + E > %d", fn, kMaxRead);
   ResidArgs a{static_cast<const __nv_bfloat16*>(K), static_cast<const __nv_bfloat16*>(V), (int)Lmax, (int)C,
               (int)n_sel, (int)E, asg, sel, exp_idx, Sk, Sv, nt, quota, static_cast<__nv_bfloat16*>(kbar),
-              static_cast<__nv_bfloat16*>(vbar), logn};
-  residual_kernel<<<(unsigned)(B * kHQ), kGateThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+              static_cast<__nv_bfloat16*>(vbar), logn, status};
+  constexpr size_t smem = 2 * (size_t)kChunkC * kD * sizeof(float) + 2 * (size_t)kTokChunk * kD * 2;
+  static bool attr_set = false;  // idempotent attribute, set once per process
+  if (!attr_set) {
+    cudaError_t e = cudaFuncSetAttribute(residual_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+    attr_set = true;
+  }
+  residual_kernel<<<(unsigned)(B * kHQ), kGateThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }

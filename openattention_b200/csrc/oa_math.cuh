@@ -2,7 +2,7 @@
 // weights, proxy log-counts).  Each is evaluated in double precision by a fixed sequence of IEEE
 // operations written with explicit round-to-nearest intrinsics (no FMA contraction), then rounded
 // to fp32 once, so the result is reproducible bit for bit by any IEEE implementation of the same
-// sequence:
+// sequence (series coefficients multiply by exact reciprocal tables instead of dividing):
 //   ln(x)  = e*ln2 + 2*atanh(s),  s = (m-1)/(m+1),  m in [sqrt(1/2), sqrt(2)),  odd series to s^27
 //   exp(x) = 2^k * exp(r),  r = (x - k*ln2_hi) - k*ln2_lo  (Cody-Waite),  Taylor series to r^17
 //   erf(x) = 2/sqrt(pi) * exp(-x^2) * sum_n (2x^2)^n x / (1*3*...*(2n+1))  (Abramowitz & Stegun
@@ -13,6 +13,118 @@
 #include <stdint.h>
 
 namespace oa {
+
+// exact reciprocal tables (hex literals): 1/(2n+1), n = 0..400, and 1/i, i = 1..17
+__constant__ double kInvOdd[401] = {
+    0x1.0000000000000p+0, 0x1.5555555555555p-2, 0x1.999999999999ap-3, 0x1.2492492492492p-3,
+    0x1.c71c71c71c71cp-4, 0x1.745d1745d1746p-4, 0x1.3b13b13b13b14p-4, 0x1.1111111111111p-4,
+    0x1.e1e1e1e1e1e1ep-5, 0x1.af286bca1af28p-5, 0x1.8618618618618p-5, 0x1.642c8590b2164p-5,
+    0x1.47ae147ae147bp-5, 0x1.2f684bda12f68p-5, 0x1.1a7b9611a7b96p-5, 0x1.0842108421084p-5,
+    0x1.f07c1f07c1f08p-6, 0x1.d41d41d41d41dp-6, 0x1.bacf914c1bad0p-6, 0x1.a41a41a41a41ap-6,
+    0x1.8f9c18f9c18fap-6, 0x1.7d05f417d05f4p-6, 0x1.6c16c16c16c17p-6, 0x1.5c9882b931057p-6,
+    0x1.4e5e0a72f0539p-6, 0x1.4141414141414p-6, 0x1.3521cfb2b78c1p-6, 0x1.29e4129e4129ep-6,
+    0x1.1f7047dc11f70p-6, 0x1.15b1e5f75270dp-6, 0x1.0c9714fbcda3bp-6, 0x1.0410410410410p-6,
+    0x1.f81f81f81f820p-7, 0x1.e9131abf0b767p-7, 0x1.dae6076b981dbp-7, 0x1.cd85689039b0bp-7,
+    0x1.c0e070381c0e0p-7, 0x1.b4e81b4e81b4fp-7, 0x1.a98ef606a63bep-7, 0x1.9ec8e951033d9p-7,
+    0x1.948b0fcd6e9e0p-7, 0x1.8acb90f6bf3aap-7, 0x1.8181818181818p-7, 0x1.78a4c8178a4c8p-7,
+    0x1.702e05c0b8170p-7, 0x1.6816816816817p-7, 0x1.6058160581606p-7, 0x1.58ed2308158edp-7,
+    0x1.51d07eae2f815p-7, 0x1.4afd6a052bf5bp-7, 0x1.446f86562d9fbp-7, 0x1.3e22cbce4a902p-7,
+    0x1.3813813813814p-7, 0x1.323e34a2b10bfp-7, 0x1.2c9fb4d812ca0p-7, 0x1.27350b8812735p-7,
+    0x1.21fb78121fb78p-7, 0x1.1cf06ada2811dp-7, 0x1.1811811811812p-7, 0x1.135c81135c811p-7,
+    0x1.0ecf56be69c90p-7, 0x1.0a6810a6810a7p-7, 0x1.0624dd2f1a9fcp-7, 0x1.0204081020408p-7,
+    0x1.fc07f01fc07f0p-8, 0x1.f44659e4a4271p-8, 0x1.ecc07b301ecc0p-8, 0x1.e573ac901e574p-8,
+    0x1.de5d6e3f8868ap-8, 0x1.d77b654b82c34p-8, 0x1.d0cb58f6ec074p-8, 0x1.ca4b3055ee191p-8,
+    0x1.c3f8f01c3f8f0p-8, 0x1.bdd2b899406f7p-8, 0x1.b7d6c3dda338bp-8, 0x1.b2036406c80d9p-8,
+    0x1.ac5701ac5701bp-8, 0x1.a6d01a6d01a6dp-8, 0x1.a16d3f97a4b02p-8, 0x1.9c2d14ee4a102p-8,
+    0x1.970e4f80cb872p-8, 0x1.920fb49d0e229p-8, 0x1.8d3018d3018d3p-8, 0x1.886e5f0abb04ap-8,
+    0x1.83c977ab2beddp-8, 0x1.7f405fd017f40p-8, 0x1.7ad2208e0ecc3p-8, 0x1.767dce434a9b1p-8,
+    0x1.724287f46debcp-8, 0x1.6e1f76b4337c7p-8, 0x1.6a13cd1537290p-8, 0x1.661ec6a5122f9p-8,
+    0x1.623fa77016240p-8, 0x1.5e75bb8d015e7p-8, 0x1.5ac056b015ac0p-8, 0x1.571ed3c506b3ap-8,
+    0x1.5390948f40febp-8, 0x1.5015015015015p-8, 0x1.4cab88725af6ep-8, 0x1.49539e3b2d067p-8,
+    0x1.460cbc7f5cf9ap-8, 0x1.42d6625d51f87p-8, 0x1.3fb013fb013fbp-8, 0x1.3c995a47babe7p-8,
+    0x1.3991c2c187f63p-8, 0x1.3698df3de0748p-8, 0x1.33ae45b57bcb2p-8, 0x1.30d190130d190p-8,
+    0x1.2e025c04b8097p-8, 0x1.2b404ad012b40p-8, 0x1.288b01288b013p-8, 0x1.25e22708092f1p-8,
+    0x1.23456789abcdfp-8, 0x1.20b470c67c0d9p-8, 0x1.1e2ef3b3fb874p-8, 0x1.1bb4a4046ed29p-8,
+    0x1.19453808ca29cp-8, 0x1.16e0689427379p-8, 0x1.1485f0e0acd3bp-8, 0x1.12358e75d3033p-8,
+    0x1.0fef010fef011p-8, 0x1.0db20a88f4696p-8, 0x1.0b7e6ec259dc8p-8, 0x1.0953f39010954p-8,
+    0x1.073260a47f7c6p-8, 0x1.05197f7d73404p-8, 0x1.03091b51f5e1ap-8, 0x1.0101010101010p-8,
+    0x1.fe01fe01fe020p-9, 0x1.fa11caa01fa12p-9, 0x1.f6310aca0dbb5p-9, 0x1.f25f644230ab5p-9,
+    0x1.ee9c7f8458e02p-9, 0x1.eae807aba01ebp-9, 0x1.e741aa59750e4p-9, 0x1.e3a9179dc1a73p-9,
+    0x1.e01e01e01e01ep-9, 0x1.dca01dca01dcap-9, 0x1.d92f2231e7f8ap-9, 0x1.d5cac807572b2p-9,
+    0x1.d272ca3fc5b1ap-9, 0x1.cf26e5c44bfc6p-9, 0x1.cbe6d9601cbe7p-9, 0x1.c8b265afb8a42p-9,
+    0x1.c5894d10d4986p-9, 0x1.c26b5392ea01cp-9, 0x1.bf583ee868d8bp-9, 0x1.bc4fd65883e7bp-9,
+    0x1.b951e2b18ff23p-9, 0x1.b65e2e3beee05p-9, 0x1.b37484ad806cep-9, 0x1.b094b31d922a4p-9,
+    0x1.adbe87f94905ep-9, 0x1.aaf1d2f87ebfdp-9, 0x1.a82e65130e159p-9, 0x1.a574107688a4ap-9,
+    0x1.a2c2a87c51ca0p-9, 0x1.a01a01a01a01ap-9, 0x1.9d79f176b682dp-9, 0x1.9ae24ea5510dap-9,
+    0x1.9852f0d8ec0ffp-9, 0x1.95cbb0be377aep-9, 0x1.934c67f9b2ce6p-9, 0x1.90d4f120190d5p-9,
+    0x1.8e6527af1373fp-9, 0x1.8bfce8062ff3ap-9, 0x1.899c0f601899cp-9, 0x1.87427bcc092b9p-9,
+    0x1.84f00c2780614p-9, 0x1.82a4a0182a4a0p-9, 0x1.8060180601806p-9, 0x1.7e225515a4f1dp-9,
+    0x1.7beb3922e017cp-9, 0x1.79baa6bb6398bp-9, 0x1.77908119ac60dp-9, 0x1.756cac201756dp-9,
+    0x1.734f0c541fe8dp-9, 0x1.713786d9c7c09p-9, 0x1.6f26016f26017p-9, 0x1.6d1a62681c861p-9,
+    0x1.6b1490aa31a3dp-9, 0x1.691473a88d0c0p-9, 0x1.6719f3601671ap-9, 0x1.6524f853b4aa3p-9,
+    0x1.63356b88ac0dep-9, 0x1.614b36831ae94p-9, 0x1.5f66434292dfcp-9, 0x1.5d867c3ece2a5p-9,
+    0x1.5babcc647fa91p-9, 0x1.59d61f123ccaap-9, 0x1.5805601580560p-9, 0x1.56397ba7c52e2p-9,
+    0x1.54725e6bb82fep-9, 0x1.52aff56a8054bp-9, 0x1.50f22e111c4c5p-9, 0x1.4f38f62dd4c9bp-9,
+    0x1.4d843bedc2c4cp-9, 0x1.4bd3edda68fe1p-9, 0x1.4a27fad76014ap-9, 0x1.4880522014880p-9,
+    0x1.46dce34596066p-9, 0x1.453d9e2c776cap-9, 0x1.43a2730abee4dp-9, 0x1.420b5265e5951p-9,
+    0x1.40782d10e6566p-9, 0x1.3ee8f42a5af07p-9, 0x1.3d5d991aa75c6p-9, 0x1.3bd60d9232955p-9,
+    0x1.3a524387ac822p-9, 0x1.38d22d366088ep-9, 0x1.3755bd1c945eep-9, 0x1.35dce5f9f2af8p-9,
+    0x1.34679ace01346p-9, 0x1.32f5ced6a1dfap-9, 0x1.3187758e9ebb6p-9, 0x1.301c82ac40260p-9,
+    0x1.2eb4ea1fed14bp-9, 0x1.2d50a012d50a0p-9, 0x1.2bef98e5a3711p-9, 0x1.2a91c92f3c105p-9,
+    0x1.293725bb804a5p-9, 0x1.27dfa38a1ce4dp-9, 0x1.268b37cd60127p-9, 0x1.2539d7e9177b2p-9,
+    0x1.23eb79717605bp-9, 0x1.22a0122a0122ap-9, 0x1.21579804855e6p-9, 0x1.2012012012012p-9,
+    0x1.1ecf43c7fb84cp-9, 0x1.1d8f5672e4abdp-9, 0x1.1c522fc1ce059p-9, 0x1.1b17c67f2bae3p-9,
+    0x1.19e0119e0119ep-9, 0x1.18ab083902bdbp-9, 0x1.1778a191bd684p-9, 0x1.1648d50fc3201p-9,
+    0x1.151b9a3fdd5c9p-9, 0x1.13f0e8d344724p-9, 0x1.12c8b89edc0acp-9, 0x1.11a3019a74826p-9,
+    0x1.107fbbe011080p-9, 0x1.0f5edfab325a2p-9, 0x1.0e40655826011p-9, 0x1.0d24456359e3ap-9,
+    0x1.0c0a7868b4171p-9, 0x1.0af2f722eecb5p-9, 0x1.09ddba6af8360p-9, 0x1.08cabb37565e2p-9,
+    0x1.07b9f29b8eae2p-9, 0x1.06ab59c7912fbp-9, 0x1.059eea0727586p-9, 0x1.04949cc1664c5p-9,
+    0x1.038c6b78247fcp-9, 0x1.02864fc7729e9p-9, 0x1.0182436517a37p-9, 0x1.0080402010080p-9,
+    0x1.ff007fc01ff00p-10, 0x1.fd04794a10e6ap-10, 0x1.fb0c610d5e939p-10, 0x1.f9182b6813bafp-10,
+    0x1.f727cce5f530ap-10, 0x1.f53b3a3fa204ep-10, 0x1.f3526859b8cecp-10, 0x1.f16d4c4401f17p-10,
+    0x1.ef8bdb389ebadp-10, 0x1.edae0a9b3d3a5p-10, 0x1.ebd3cff850b0cp-10, 0x1.e9fd21044e799p-10,
+    0x1.e829f39aef509p-10, 0x1.e65a3dbe74d6bp-10, 0x1.e48df596f3394p-10, 0x1.e2c511719ee16p-10,
+    0x1.e0ff87c01e100p-10, 0x1.df3d4f17de4dbp-10, 0x1.dd7e5e316d94cp-10, 0x1.dbc2abe7d71d4p-10,
+    0x1.da0a2f3803b41p-10, 0x1.d854df401d855p-10, 0x1.d6a2b33ef7448p-10, 0x1.d4f3a293769cap-10,
+    0x1.d347a4bc01d34p-10, 0x1.d19eb155f08a4p-10, 0x1.cff8c01cff8c0p-10, 0x1.ce55c8eac7900p-10,
+    0x1.ccb5c3b636e3ap-10, 0x1.cb18a8930de60p-10, 0x1.c97e6fb15e44dp-10, 0x1.c7e7115d0ce95p-10,
+    0x1.c65285fd56843p-10, 0x1.c4c0c61456a8ep-10, 0x1.c331ca3e91679p-10, 0x1.c1a58b327f576p-10,
+    0x1.c01c01c01c01cp-10, 0x1.be9526d0769fap-10, 0x1.bd10f365451b6p-10, 0x1.bb8f609879493p-10,
+    0x1.ba10679bd8488p-10, 0x1.b89401b89401cp-10, 0x1.b71a284ee6b34p-10, 0x1.b5a2d4d5b081fp-10,
+    0x1.b42e00da17007p-10, 0x1.b2bba5ff26a23p-10, 0x1.b14bbdfd760e6p-10, 0x1.afde42a2cb482p-10,
+    0x1.ae732dd1c2a09p-10, 0x1.ad0a798177693p-10, 0x1.aba41fbd2e5b1p-10, 0x1.aa401aa401aa4p-10,
+    0x1.a8de64688ebabp-10, 0x1.a77ef750a56dap-10, 0x1.a621cdb4f8fdfp-10, 0x1.a4c6e200d2637p-10,
+    0x1.a36e2eb1c432dp-10, 0x1.a217ae575ff2fp-10, 0x1.a0c35b92ecdf1p-10, 0x1.9f713117200d0p-10,
+    0x1.9e2129a7d5f0ap-10, 0x1.9cd34019cd340p-10, 0x1.9b876f5262dd1p-10, 0x1.9a3db2474fb98p-10,
+    0x1.98f603fe670a0p-10, 0x1.97b05f8d56652p-10, 0x1.966cc01966cc0p-10, 0x1.952b20d73ee97p-10,
+    0x1.93eb7d0aa6759p-10, 0x1.92add0064ab74p-10, 0x1.9172152b841ddp-10, 0x1.903847ea1cec1p-10,
+    0x1.8f0063c018f00p-10, 0x1.8dca64397e408p-10, 0x1.8c9644f01efbcp-10, 0x1.8b64018b64019p-10,
+    0x1.8a3395c018a34p-10, 0x1.8904fd503744bp-10, 0x1.87d8340ab6e97p-10, 0x1.86ad35cb59a84p-10,
+    0x1.8583fe7a7c018p-10, 0x1.845c8a0ce5129p-10, 0x1.8336d48397a24p-10, 0x1.8212d9eba4018p-10,
+    0x1.80f0965dfabcbp-10, 0x1.7fd005ff40180p-10, 0x1.7eb124ffa053bp-10, 0x1.7d93ef9aa4b46p-10,
+    0x1.7c7862170949fp-10, 0x1.7b5e78c693733p-10, 0x1.7a463005e918cp-10, 0x1.792f843c689c3p-10,
+    0x1.781a71dc01782p-10, 0x1.7706f5610d8d0p-10, 0x1.75f50b522b17cp-10, 0x1.74e4b040174e5p-10,
+    0x1.73d5e0c5899f7p-10, 0x1.72c899870f91fp-10, 0x1.71bcd732e940ap-10, 0x1.70b29680e66fap-10,
+    0x1.6fa9d43244380p-10, 0x1.6ea28d118b474p-10, 0x1.6d9cbdf26eaefp-10, 0x1.6c9863b1ab429p-10,
+    0x1.6b957b34e7803p-10, 0x1.6a94016a94017p-10, 0x1.6993f349cc726p-10, 0x1.68954dd2390bap-10,
+    0x1.67980e0bf08c7p-10, 0x1.669c31075ab40p-10, 0x1.65a1b3dd13357p-10, 0x1.64a893adcd25fp-10,
+    0x1.63b0cda236e1cp-10, 0x1.62ba5eeade65ep-10, 0x1.61c544c0161c5p-10, 0x1.60d17c61da198p-10,
+    0x1.5fdf0317b5c6fp-10, 0x1.5eedd630a9fb3p-10, 0x1.5dfdf303137b6p-10, 0x1.5d0f56ec91e57p-10,
+    0x1.5c21ff51ef005p-10, 0x1.5b35e99f06714p-10, 0x1.5a4b1346add2bp-10, 0x1.596179c29d2cep-10,
+    0x1.58791a9357ccep-10, 0x1.5791f34015792p-10, 0x1.56ac0156ac015p-10, 0x1.55c7426b79286p-10,
+    0x1.54e3b4194ce66p-10, 0x1.5401540154015p-10, 0x1.53201fcb02fb1p-10, 0x1.5240152401524p-10,
+    0x1.516131c015161p-10, 0x1.508373590ec9cp-10, 0x1.4fa6d7aeb597cp-10, 0x1.4ecb5c86b3d24p-10,
+    0x1.4df0ffac83c01p-10, 0x1.4d17bef15cb4ep-10, 0x1.4c3f982c20723p-10, 0x1.4b68893948d1cp-10,
+    0x1.4a928ffad5b5cp-10, 0x1.49bdaa583b401p-10, 0x1.48e9d63e504d1p-10, 0x1.4817119f3d325p-10,
+    0x1.47455a726abf2p-10,
+};
+__constant__ double kInvInt[18] = {
+    0x0p+0, 0x1.0000000000000p+0, 0x1.0000000000000p-1, 0x1.5555555555555p-2,
+    0x1.0000000000000p-2, 0x1.999999999999ap-3, 0x1.5555555555555p-3, 0x1.2492492492492p-3,
+    0x1.0000000000000p-3, 0x1.c71c71c71c71cp-4, 0x1.999999999999ap-4, 0x1.745d1745d1746p-4,
+    0x1.5555555555555p-4, 0x1.3b13b13b13b14p-4, 0x1.2492492492492p-4, 0x1.1111111111111p-4,
+    0x1.0000000000000p-4, 0x1.e1e1e1e1e1e1ep-5,
+};
 
 __device__ __forceinline__ double pow2d(int k) {  // exact 2^k, -1022 <= k <= 1023
   return __longlong_as_double((long long)(k + 1023) << 52);
@@ -32,7 +144,7 @@ __device__ __noinline__ double ln_d(double x) {  // x > 0 and normal
 #pragma unroll 1
   for (int k = 1; k <= 13; ++k) {
     term = __dmul_rn(term, s2);
-    sum = __dadd_rn(sum, __ddiv_rn(term, (double)(2 * k + 1)));
+    sum = __dadd_rn(sum, __dmul_rn(term, kInvOdd[k]));
   }
   return __dadd_rn(__dmul_rn(2.0, sum), __dmul_rn((double)e, 0.69314718055994530942));
 }
@@ -48,7 +160,7 @@ __device__ __noinline__ double exp_d(double x) {
 #pragma unroll 1
   for (int i = 1; i <= 17; ++i) {
     term = __dmul_rn(term, r);
-    term = __ddiv_rn(term, (double)i);
+    term = __dmul_rn(term, kInvInt[i]);
     p = __dadd_rn(p, term);
   }
   const int ki = (int)k;
@@ -64,7 +176,7 @@ __device__ __noinline__ double erf_d(double x) {  // x >= 0
 #pragma unroll 1
   for (int n = 1; n < 400; ++n) {
     term = __dmul_rn(term, tx2);
-    term = __ddiv_rn(term, (double)(2 * n + 1));
+    term = __dmul_rn(term, kInvOdd[n]);
     sum = __dadd_rn(sum, term);
     if (term < __dmul_rn(sum, 1e-17)) break;
   }

@@ -46,7 +46,14 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int pos = __ldg(a.n_dev) - 1;
   __shared__ float kf[kD], vf[kD], qf[kG][kD], zp[kG][kRC];
+  __shared__ __align__(16) float sU[kD * kRQ];             // this KV head's QGS basis
+  __shared__ __align__(16) __nv_bfloat16 sW[kG * kD * kRC];  // the 4 query heads' QGC projections
   const bool have_tok = pos >= 0 && pos < a.Lmax;
+  const float* Uk = a.U + (int64_t)kv * kD * kRQ;
+  for (int i = tid; i < kD * kRQ / 4; i += 128)
+    reinterpret_cast<float4*>(sU)[i] = __ldg(reinterpret_cast<const float4*>(Uk) + i);
+  for (int i = tid; i < kG * kD * kRC / 8; i += 128)
+    reinterpret_cast<uint4*>(sW)[i] = __ldg(reinterpret_cast<const uint4*>(a.W + (int64_t)kv * kG * kD * kRC) + i);
   if (have_tok) {
     kf[tid] = __bfloat162float(a.K[((int64_t)kv * a.Lmax + pos) * kD + tid]);
     vf[tid] = __bfloat162float(a.V[((int64_t)kv * a.Lmax + pos) * kD + tid]);
@@ -56,12 +63,12 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
     for (int g = 0; g < kG; ++g) qf[g][tid] = __bfloat162float(a.q[(int64_t)(kv * kG + g) * a.q_stride + tid]);
   }
   __syncthreads();
-  const float* Uk = a.U + (int64_t)kv * kD * kRQ;
   // query projection zq[r, j] = bf16((q . U[:, j]) * scale_j), d ascending
   if (a.q != nullptr) {
     const int g = tid >> 5, j = tid & 31;
     float acc = 0.f;
-    for (int d = 0; d < kD; ++d) acc = __fmaf_rn(qf[g][d], __ldg(&Uk[d * kRQ + j]), acc);
+#pragma unroll 8
+    for (int d = 0; d < kD; ++d) acc = __fmaf_rn(qf[g][d], sU[d * kRQ + j], acc);
     a.zq[(int64_t)(kv * kG + g) * kRQ + j] = __float2bfloat16_rn(__fmul_rn(acc, __ldg(&a.scale[kv * kRQ + j])));
   }
   if (!have_tok) return;
@@ -69,7 +76,8 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
   if (tid < kRQ) {
     const int j = tid;
     float acc = 0.f;
-    for (int d = 0; d < kD; ++d) acc = __fmaf_rn(kf[d], __ldg(&Uk[d * kRQ + j]), acc);
+#pragma unroll 8
+    for (int d = 0; d < kD; ++d) acc = __fmaf_rn(kf[d], sU[d * kRQ + j], acc);
     float c = rintf(__fdiv_rn(acc, __ldg(&a.scale[kv * kRQ + j])));
     c = fminf(fmaxf(c, -127.f), 127.f);
     a.codes[((int64_t)kv * a.Lmax + pos) * kRQ + j] = (int8_t)c;
@@ -78,8 +86,9 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
   if (tid < kG * kRC) {
     const int g = tid >> 4, c = tid & 15;
     const int r = kv * kG + g;
-    const __nv_bfloat16* Wr = a.W + (int64_t)r * kD * kRC;
+    const __nv_bfloat16* Wr = sW + g * kD * kRC;
     float acc = 0.f;
+#pragma unroll 8
     for (int d = 0; d < kD; ++d) acc = __fmaf_rn(kf[d], __bfloat162float(Wr[d * kRC + c]), acc);
     zp[g][c] = __fsub_rn(bf_round(acc), __ldg(&a.colmean[r * kRC + c]));
   }
@@ -150,6 +159,7 @@ struct ScanArgs {
   int64_t sw;
   float* tmax;  // (R, tm_stride)
   int64_t tm_stride;
+  int32_t* status;  // set to 1 if a bulk copy did not complete (may be null)
 };
 
 __device__ __forceinline__ float pow2f_exact(int k) { return __uint_as_float((uint32_t)(k + 127) << 23); }
@@ -172,10 +182,20 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
   const int n = __ldg(a.n_dev);
+  __shared__ __align__(128) int8_t sbuf[kTilesPerCta * kTile * kRQ];  // the CTA's codes chunk (32 KB)
+  __shared__ __align__(8) uint64_t mbar;
   __shared__ int8_t limb[kG][4][kRQ];  // [head][limb][j]
   __shared__ int sS[kG];
-  __shared__ float s_max[8][kG];
-  // fixed-point image of each head's zq (one warp per head)
+  __shared__ float s_max[kTilesPerCta][8][kG];
+  const int t_begin = blockIdx.y * kTilesPerCta;
+  const int tok0 = t_begin * kTile;
+  const int ntok = max(0, min(min(a.Lmax, n), tok0 + kTilesPerCta * kTile) - tok0);  // tokens to fetch
+  const uint32_t bar = smem_u32(&mbar);
+  if (tid == 0) mbar_init(bar);
+  __syncthreads();
+  if (tid == 0 && ntok > 0)  // one bulk copy (TMA, no multicast) of the chunk into shared memory
+    bulk_load(sbuf, a.codes + ((int64_t)kv * a.Lmax + tok0) * kRQ, (uint32_t)ntok * kRQ, bar);
+  // fixed-point image of each head's zq (one warp per head), overlapping the copy
   if (warp < kG) {
     const float z = __bfloat162float(a.zq[(int64_t)(kv * kG + warp) * kRQ + lane]);
     float amax = fabsf(z);
@@ -210,24 +230,29 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
   }
   const int fin_head[2] = {0 + (tig >> 1), 2 + (tig >> 1)};
   const int S_h[2] = {sS[fin_head[0]], sS[fin_head[1]]};
-  const int8_t* cbase = a.codes + (int64_t)kv * a.Lmax * kRQ;
-  const int t_begin = blockIdx.y * kTilesPerCta;
-  for (int tile = t_begin; tile < t_begin + kTilesPerCta && tile < a.NT; ++tile) {
+  const bool ok = ntok == 0 || mbar_wait(bar, 0);
+  if (!__syncthreads_and(ok)) {  // the copy did not complete in time: report, wait once more, skip
+    if (tid == 0 && a.status != nullptr) atomicExch(a.status, 1);
+    if (!ok) mbar_wait(bar, 0);
+    return;
+  }
+#pragma unroll
+  for (int ti = 0; ti < kTilesPerCta; ++ti) {
+    const int tile = t_begin + ti;
     const int t0 = tile * kTile;
     float hmax[2] = {-INFINITY, -INFINITY};  // for heads fin_head[0], fin_head[1]
-    if (t0 < n) {
+    if (tile < a.NT && t0 < n) {
 #pragma unroll
       for (int grp = 0; grp < 2; ++grp) {
-        const int tb = t0 + warp * 32 + grp * 16;
-        const int ta = tb + gid, tb8 = tb + gid + 8;
+        const int lt0 = ti * kTile + warp * 32 + grp * 16;  // chunk-local first token of the 16
+        const int ta = tok0 + lt0 + gid, tb8 = ta + 8;
+        // ldmatrix x4: matrices (rows 0-7 | 8-15) x (bytes 0-15 | 16-31) of the 16 x 32-byte tile
         uint32_t af[4];
-        const uint32_t* p0 = reinterpret_cast<const uint32_t*>(cbase + (int64_t)ta * kRQ);
-        const uint32_t* p1 = reinterpret_cast<const uint32_t*>(cbase + (int64_t)tb8 * kRQ);
-        const bool ok0 = ta < a.Lmax, ok1 = tb8 < a.Lmax;
-        af[0] = ok0 ? __ldg(p0 + tig) : 0u;
-        af[1] = ok1 ? __ldg(p1 + tig) : 0u;
-        af[2] = ok0 ? __ldg(p0 + 4 + tig) : 0u;
-        af[3] = ok1 ? __ldg(p1 + 4 + tig) : 0u;
+        const int mi = lane >> 3, ri = lane & 7;
+        const int8_t* rowp = sbuf + (lt0 + (mi & 1) * 8 + ri) * kRQ + (mi >> 1) * 16;
+        asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                     : "=r"(af[0]), "=r"(af[1]), "=r"(af[2]), "=r"(af[3])
+                     : "r"(smem_u32(rowp)));
 #pragma unroll
         for (int m = 0; m < 2; ++m) {
           int d[4];
@@ -236,14 +261,14 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
           int e[4];
 #pragma unroll
           for (int i = 0; i < 4; ++i) e[i] = __shfl_xor_sync(0xffffffffu, d[i], 1);
-          // limbs 0,1 live on even tig, limbs 2,3 on odd tig
-          const int* lo = (tig & 1) ? e : d;
-          const int* hi = (tig & 1) ? d : e;
-          const int row = tig & 1;  // even tig finalises token gid, odd tig token gid+8
-          const long long tot = (long long)lo[2 * row] + ((long long)lo[2 * row + 1] << 8) +
-                                ((long long)hi[2 * row] << 16) + ((long long)hi[2 * row + 1] << 24);
+          // limbs 0,1 live on even tig, limbs 2,3 on odd tig; even tig finalises token gid, odd gid+8
+          const bool odd = (tig & 1) != 0;
+          const int l0 = odd ? e[2] : d[0], l1 = odd ? e[3] : d[1];
+          const int l2 = odd ? d[2] : e[0], l3 = odd ? d[3] : e[1];
+          const int row = tig & 1;
+          const long long tot = (long long)l0 + ((long long)l1 << 8) + ((long long)l2 << 16) + ((long long)l3 << 24);
           const int t = row ? tb8 : ta;
-          float f = scale_pow2(__ll2float_rn(tot), -S_h[m]);
+          const float f = scale_pow2(__ll2float_rn(tot), -S_h[m]);
           uint16_t sb = f2bf_bits(f);
           if (t < a.ns || t >= n - a.nl || t >= n) sb = 0xff80u;
           if (t < a.Lmax) {
@@ -253,39 +278,48 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
         }
       }
     }
-    // tile maximum per head: lanes with tig>>1 == h hold head 2m + h
+    // per-warp tile maximum per head: lanes with equal tig>>1 hold head 2m + (tig>>1)
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
       float v = hmax[m];
-      // reduce over lanes sharing (tig >> 1): xor over gid bits (4, 8, 16) and tig bit 0 (1)
       v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
       v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
       v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
       v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
-      if (lane == 0) s_max[warp][2 * m] = v;      // tig 0 -> head 2m
-      if (lane == 2) s_max[warp][2 * m + 1] = v;  // tig 2 -> head 2m + 1
+      if (lane == 0) s_max[ti][warp][2 * m] = v;      // tig 0 -> head 2m
+      if (lane == 2) s_max[ti][warp][2 * m + 1] = v;  // tig 2 -> head 2m + 1
     }
-    __syncthreads();
-    if (tid < kG) {
+  }
+  __syncthreads();
+  if (tid < kTilesPerCta * kG) {
+    const int ti = tid / kG, h = tid % kG;
+    const int tile = t_begin + ti;
+    if (tile < a.NT) {
       float v = -INFINITY;
 #pragma unroll
-      for (int w = 0; w < 8; ++w) v = fmaxf(v, s_max[w][tid]);
-      a.tmax[(int64_t)(kv * kG + tid) * a.tm_stride + tile] = v;
+      for (int w = 0; w < 8; ++w) v = fmaxf(v, s_max[ti][w][h]);
+      a.tmax[(int64_t)(kv * kG + h) * a.tm_stride + tile] = v;
     }
-    __syncthreads();
   }
 }
 
 // ------------------------------------------------------------------------ exact row top-k
+// One warp per row.  (1) the kt2 = min(2k, tiles) tiles with the largest maxima (ties -> lower
+// tile) by a warp radix select over the 32-bit float keys of the tile maxima; (2) the k largest
+// scores inside those tiles (ties -> lower position) by a radix select over 16-bit score keys;
+// (3) the k winners ranked by (score desc, position asc).
+constexpr int kSelWarps = 4;
+constexpr int kMaxKT2 = 128;
+
 struct SelectArgs {
   uint16_t* scores;
   int64_t sw;
   const float* tmax;
   int64_t tm_stride;
   const int32_t* n_dev;
-  int ns, nl, k_top, NT, Lmax;
-  int kt2_max;
+  int R, ns, nl, k_top, NT, Lmax;
   int32_t* sel;
+  int NT_pad, kt2_max;  // shared-memory slots per warp: tile keys, candidate tiles
 };
 
 __device__ __forceinline__ uint32_t fkey(float x) {  // ascending float -> ascending uint32
@@ -294,88 +328,179 @@ __device__ __forceinline__ uint32_t fkey(float x) {  // ascending float -> ascen
 }
 __device__ __forceinline__ uint32_t ukey16(uint32_t b) { return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u); }
 
-__device__ __forceinline__ unsigned long long block_max_u64(unsigned long long v, unsigned long long* red) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+// The q-th largest key among the valid keys get(i), i < m (warp-collective).  Returns the
+// threshold T and `above` = number of valid keys > T; if fewer than q keys are valid, T = 0 and
+// above = the valid count.  Digits of 8 bits from the top; hist: 256 ints of warp-private smem.
+template <int BITS, typename Get>
+__device__ __forceinline__ void warp_radix_select(int m, int q, int* hist, Get get, uint32_t& T, int& above) {
+  const int lane = threadIdx.x & 31;
+  uint32_t prefix = 0u, pmask = 0u;
+  above = 0;
+  bool ok = true;
+#pragma unroll 1
+  for (int shift = BITS - 8; shift >= 0; shift -= 8) {
+    for (int b = lane; b < 256; b += 32) hist[b] = 0;
+    __syncwarp();
+    for (int i = lane; i < m; i += 32) {
+      bool v;
+      uint32_t k;
+      get(i, v, k);
+      if (v && (k & pmask) == prefix) atomicAdd(&hist[(k >> shift) & 255u], 1);
+    }
+    __syncwarp();
+    int cnt[8], sum = 0;
 #pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const unsigned long long o = __shfl_xor_sync(0xffffffffu, v, off);
-    v = o > v ? o : v;
+    for (int i = 0; i < 8; ++i) {
+      cnt[i] = hist[255 - 8 * lane - i];
+      sum += cnt[i];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    const int excl = incl - sum;
+    const int need = q - above;
+    int fd = -1, fa = 0;
+    if (excl < need && incl >= need) {
+      int run = excl;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (fd < 0 && run + cnt[i] >= need) {
+          fd = 255 - 8 * lane - i;
+          fa = run;
+        }
+        run += cnt[i];
+      }
+    }
+    const unsigned who = __ballot_sync(0xffffffffu, fd >= 0);
+    __syncwarp();
+    if (who == 0u) {  // fewer than q valid keys: take them all
+      ok = false;
+      above += __shfl_sync(0xffffffffu, incl, 31);
+      break;
+    }
+    const int src = __ffs(who) - 1;
+    const int d = __shfl_sync(0xffffffffu, fd, src);
+    above += __shfl_sync(0xffffffffu, fa, src);
+    prefix |= (uint32_t)d << shift;
+    pmask |= 0xffu << shift;
   }
-  __syncthreads();
-  if (lane == 0) red[warp] = v;
-  __syncthreads();
-  v = red[0];
-  for (int w = 1; w < (int)(blockDim.x >> 5); ++w) v = red[w] > v ? red[w] : v;
-  return v;
+  T = ok ? prefix : 0u;
 }
 
-__global__ void __launch_bounds__(256) qgs_select_kernel(const SelectArgs a) {
-  extern __shared__ unsigned char smem_raw[];
-  const int r = blockIdx.x;
-  const int tid = threadIdx.x;
+__global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const SelectArgs a) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.x * kSelWarps + warp;
+  __shared__ int s_hist[kSelWarps][256];
+  __shared__ int s_tiles[kSelWarps][kMaxKT2];
+  __shared__ int s_pos[kSelWarps][64];
+  __shared__ uint32_t s_key[kSelWarps][64];
+  extern __shared__ __align__(16) unsigned char sel_smem[];
+  // per warp: tile keys (NT uint32), then candidate keys (kt2_max * 256 uint16)
+  uint32_t* tkey = reinterpret_cast<uint32_t*>(sel_smem) + (size_t)warp * a.NT_pad;
+  uint16_t* ckey = reinterpret_cast<uint16_t*>(reinterpret_cast<uint32_t*>(sel_smem) + (size_t)kSelWarps * a.NT_pad) +
+                   (size_t)warp * a.kt2_max * kTile;
+  if (r >= a.R) return;
+  int* hist = s_hist[warp];
+  int* tiles = s_tiles[warp];
   const int n = __ldg(a.n_dev);
   const int ntv = min(a.NT, (n + kTile - 1) / kTile);
   const int kt2 = min(2 * a.k_top, ntv);
-  // tile keys: (max, lowest tile first) -> pick kt2 largest by repeated block argmax over a small list
-  unsigned long long* red = reinterpret_cast<unsigned long long*>(smem_raw);          // 8
-  int* chosen = reinterpret_cast<int*>(smem_raw + 64);                                  // kt2_max
-  uint16_t* cand = reinterpret_cast<uint16_t*>(smem_raw + 64 + 4 * a.kt2_max);         // kt2_max * 256
-  unsigned char* taken = reinterpret_cast<unsigned char*>(cand + (size_t)a.kt2_max * kTile);  // kt2_max*256
   const float* tm = a.tmax + (int64_t)r * a.tm_stride;
-  const uint16_t* sr = a.scores + (int64_t)r * a.sw;
-  // per-thread strided tile keys; kt2 rounds of block argmax (NT <= a few thousand)
-  for (int round = 0; round < kt2; ++round) {
-    unsigned long long best = 0ull;
-    for (int t = tid; t < ntv; t += blockDim.x) {
-      bool used = false;
-      for (int i = 0; i < round; ++i) used |= (chosen[i] == t);
-      if (used) continue;
-      const unsigned long long key = ((unsigned long long)fkey(tm[t]) << 32) | (0xffffffffu - (uint32_t)t);
-      best = key > best ? key : best;
-    }
-    best = block_max_u64(best, red);
-    if (tid == 0) chosen[round] = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
-    __syncthreads();
-  }
-  // candidate scores of the chosen tiles
-  const int ncand = kt2 * kTile;
-  for (int i = tid; i < ncand; i += blockDim.x) {
-    const int t = chosen[i / kTile] * kTile + (i % kTile);
-    const bool ok = t < n;
-    cand[i] = ok ? (uint16_t)ukey16(sr[t]) : (uint16_t)0;
-    taken[i] = ok ? 0 : 1;
-  }
-  __syncthreads();
-  int32_t* out = a.sel + (int64_t)r * (a.ns + a.nl + a.k_top);
-  for (int k = 0; k < a.k_top; ++k) {
-    unsigned long long best = 0ull;
-    for (int i = tid; i < ncand; i += blockDim.x) {
-      if (taken[i]) continue;
-      const uint32_t t = (uint32_t)(chosen[i / kTile] * kTile + (i % kTile));
-      const unsigned long long key = ((unsigned long long)(cand[i] + 1u) << 32) | (0xffffffffu - t);
-      best = key > best ? key : best;
-    }
-    best = block_max_u64(best, red);
-    const int t = (int)(0xffffffffu - (uint32_t)(best & 0xffffffffu));
-    if (best == 0ull) {
-      if (tid == 0) out[a.ns + a.nl + k] = 0;  // fewer candidates than k_top (cannot happen for k_top <= n)
-    } else {
-      if (tid == 0) out[a.ns + a.nl + k] = t;
-      for (int i = tid; i < ncand; i += blockDim.x)
-        if (chosen[i / kTile] * kTile + (i % kTile) == t) taken[i] = 1;
-    }
-    __syncthreads();
-  }
-  // sink, local; selected scores -> -inf (they go last in their cluster for the within-cluster top-q)
   uint16_t* srw = a.scores + (int64_t)r * a.sw;
-  for (int i = tid; i < a.ns + a.nl; i += blockDim.x) {
-    const int t = i < a.ns ? i : n - a.nl + (i - a.ns);
-    out[i] = t;
+  for (int i = lane; i < ntv; i += 32) tkey[i] = fkey(tm[i]);
+  __syncwarp();
+  // (1) tiles
+  uint32_t Tt;
+  int above_t;
+  warp_radix_select<32>(ntv, kt2, hist, [&](int i, bool& v, uint32_t& k) { v = true; k = tkey[i]; }, Tt, above_t);
+  {
+    int taken = 0, ties = 0;
+    const int need_eq = kt2 - above_t;
+    for (int i0 = 0; i0 < ntv; i0 += 32) {
+      const int i = i0 + lane;
+      const uint32_t k = i < ntv ? tkey[i] : 0u;
+      const bool gt = i < ntv && k > Tt, eq = i < ntv && k == Tt;
+      const unsigned beq = __ballot_sync(0xffffffffu, eq);
+      const bool take = gt || (eq && ties + __popc(beq & ((1u << lane) - 1u)) < need_eq);
+      const unsigned bt = __ballot_sync(0xffffffffu, take);
+      if (take) tiles[taken + __popc(bt & ((1u << lane) - 1u))] = i;
+      taken += __popc(bt);
+      ties += __popc(beq);
+    }
+  }
+  __syncwarp();
+  // (2) candidate keys of the chosen tiles (ascending tile order) staged with 16-byte loads;
+  //     positions >= n get key 0 (below every real key, which is >= 0x7f)
+  const int m = kt2 * kTile;
+  for (int i = lane * 8; i < m; i += 32 * 8) {
+    const int pos = tiles[i >> 8] * kTile + (i & (kTile - 1));
+    const uint4 w = *reinterpret_cast<const uint4*>(srw + pos);
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const uint32_t b = (wv[u >> 1] >> (16 * (u & 1))) & 0xffffu;
+      ckey[i + u] = (pos + u < n) ? (uint16_t)ukey16(b) : (uint16_t)0;
+    }
+  }
+  __syncwarp();
+  auto cand = [&](int i, bool& v, uint32_t& k) {
+    k = ckey[i];
+    v = k != 0u;
+  };
+  uint32_t T;
+  int above;
+  warp_radix_select<16>(m, a.k_top, hist, cand, T, above);
+  {
+    int taken = 0, ties = 0;
+    const int need_eq = a.k_top - above;
+    for (int i0 = 0; i0 < m; i0 += 32) {
+      const int i = i0 + lane;
+      bool v = false;
+      uint32_t k = 0u;
+      if (i < m) cand(i, v, k);
+      const bool gt = v && k > T, eq = v && k == T;
+      const unsigned beq = __ballot_sync(0xffffffffu, eq);
+      const bool take = gt || (eq && ties + __popc(beq & ((1u << lane) - 1u)) < need_eq);
+      const unsigned bt = __ballot_sync(0xffffffffu, take);
+      const int slot = taken + __popc(bt & ((1u << lane) - 1u));
+      if (take && slot < a.k_top) {
+        s_pos[warp][slot] = tiles[i >> 8] * kTile + (i & (kTile - 1));
+        s_key[warp][slot] = k;
+      }
+      taken += __popc(bt);
+      ties += __popc(beq);
+    }
+    // (fewer candidates than k cannot happen for k_top <= n - ns - nl; pad with position 0)
+    for (int j = taken + lane; j < a.k_top; j += 32) {
+      s_pos[warp][j] = 0;
+      s_key[warp][j] = 0u;
+    }
+  }
+  __syncwarp();
+  // (3) rank order (score desc, position asc)
+  int32_t* out = a.sel + (int64_t)r * (a.ns + a.nl + a.k_top);
+  for (int j = lane; j < a.k_top; j += 32) {
+    const uint32_t kj = s_key[warp][j];
+    const int pj = s_pos[warp][j];
+    int rank = 0;
+    for (int i = 0; i < a.k_top; ++i) {
+      const uint32_t ki = s_key[warp][i];
+      const int pi = s_pos[warp][i];
+      rank += (ki > kj || (ki == kj && pi < pj)) ? 1 : 0;
+    }
+    out[a.ns + a.nl + rank] = pj;
+  }
+  __syncwarp();
+  for (int j = lane; j < a.k_top; j += 32) {
+    const int t = s_pos[warp][j];
     if (t >= 0 && t < a.Lmax) srw[t] = 0xff80u;
   }
-  __syncthreads();
-  for (int k = tid; k < a.k_top; k += blockDim.x) {
-    const int t = out[a.ns + a.nl + k];
+  for (int i = lane; i < a.ns + a.nl; i += 32) {
+    const int t = i < a.ns ? i : n - a.nl + (i - a.ns);
+    out[i] = t;
     if (t >= 0 && t < a.Lmax) srw[t] = 0xff80u;
   }
 }
@@ -409,7 +534,7 @@ extern "C" int oa_index_update(const void* K, const void* V, int64_t B, int64_t 
 
 extern "C" int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64_t Lmax, const int32_t* n_dev, int ns,
                            int nl, void* scores, int64_t score_stride, float* tile_max, int64_t tile_max_stride,
-                           void* stream) {
+                           int32_t* status, void* stream) {
   const char* fn = "oa_qgs_scan";
   OA_REQUIRE(B > 0 && Lmax > 0 && Lmax < (1ll << 30), "%s: bad sizes", fn);
   OA_REQUIRE(codes && zq && n_dev && scores && tile_max, "%s: null pointer", fn);
@@ -419,7 +544,7 @@ extern "C" int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64
              fn, (long long)score_stride, NT);
   OA_REQUIRE(ns >= 0 && nl >= 0, "%s: negative sink/local", fn);
   ScanArgs a{codes, static_cast<const __nv_bfloat16*>(zq), n_dev, ns, nl, (int)Lmax, NT,
-             static_cast<uint16_t*>(scores), score_stride, tile_max, tile_max_stride};
+             static_cast<uint16_t*>(scores), score_stride, tile_max, tile_max_stride, status};
   dim3 grid((unsigned)(B * kHKV), (unsigned)((NT + kTilesPerCta - 1) / kTilesPerCta));
   qgs_scan_kernel<<<grid, kScanThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
@@ -429,19 +554,23 @@ extern "C" int oa_qgs_select(void* scores, int64_t score_stride, const float* ti
                              int64_t R, int64_t Lmax, const int32_t* n_dev, int ns, int nl, int k_top, int32_t* sel,
                              void* stream) {
   const char* fn = "oa_qgs_select";
-  OA_REQUIRE(R > 0 && Lmax > 0 && Lmax < (1ll << 30), "%s: bad sizes", fn);
+  OA_REQUIRE(R > 0 && R < (1ll << 31) && Lmax > 0 && Lmax < (1ll << 30), "%s: bad sizes", fn);
   OA_REQUIRE(scores && tile_max && n_dev && sel, "%s: null pointer", fn);
-  OA_REQUIRE(k_top >= 1 && k_top <= 64, "%s: k_top=%d outside [1, 64]", fn, k_top);
+  OA_REQUIRE(k_top >= 1 && 2 * k_top <= kMaxKT2, "%s: k_top=%d outside [1, %d]", fn, k_top, kMaxKT2 / 2);
   OA_REQUIRE(ns >= 0 && nl >= 0, "%s: negative sink/local", fn);
   const int NT = (int)((Lmax + kTile - 1) / kTile);
+  OA_REQUIRE(score_stride % 8 == 0 && oa_aligned16(scores), "%s: scores rows must be 16-byte aligned", fn);
+  const int NT_pad = (NT + 3) & ~3;
   const int kt2_max = std::min(2 * k_top, NT);
-  SelectArgs a{static_cast<uint16_t*>(scores), score_stride, tile_max, tile_max_stride, n_dev, ns, nl, k_top, NT,
-               (int)Lmax, kt2_max, sel};
-  const size_t smem = 64 + 4 * (size_t)kt2_max + (size_t)kt2_max * kTile * 3 + 16;
+  SelectArgs a{static_cast<uint16_t*>(scores), score_stride, tile_max, tile_max_stride, n_dev, (int)R, ns, nl, k_top,
+               NT, (int)Lmax, sel, NT_pad, kt2_max};
+  const size_t smem = (size_t)kSelWarps * (NT_pad * 4 + (size_t)kt2_max * kTile * 2);
+  OA_REQUIRE(smem <= 200 * 1024, "%s: Lmax=%lld and k_top=%d need too much shared memory", fn, (long long)Lmax, k_top);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(qgs_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
   }
-  qgs_select_kernel<<<(unsigned)R, 256, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  qgs_select_kernel<<<(unsigned)((R + kSelWarps - 1) / kSelWarps), kSelWarps * 32, smem,
+                      static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }

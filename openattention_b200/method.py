@@ -146,7 +146,7 @@ class OursB200:
         self.st = [S.new_state(B, Lmax, self.C, self.dev, RMAX) for _ in range(self.NL)]
         R, Cn, E, dev = self.R, self.C, self.E, self.dev
         self.NT = (Lmax + 255) // 256
-        self.SW = self.NT * 256
+        self.SW = S.padded_len(Lmax)
         self.zq = torch.zeros(R, RQ, dtype=torch.bfloat16, device=dev)
         self.scores = torch.zeros(R, self.SW, dtype=torch.bfloat16, device=dev)
         self.tmax = torch.zeros(R, self.NT, dtype=torch.float32, device=dev)
@@ -160,6 +160,7 @@ class OursB200:
         self.out = torch.zeros(R, D, dtype=torch.bfloat16, device=dev)
         self._sel = {}
         self._n_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.status = torch.zeros(1, dtype=torch.int32, device=dev)  # kernel-side error flag (bounded waits)
         self._n0_dev = torch.zeros(1, dtype=torch.int32, device=dev)
         lib = _lib.load()
         # the automatic split count depends on the list length (chunk rounding): size for the largest
@@ -208,7 +209,8 @@ class OursB200:
                       p(init), p(cent), p(st["nb"][b]), stream)
         _lib.call("oa_cluster_sums", p(K1), p(V1), Lmax, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]),
                   p(st["clen"][b]), p(st["Sk"][b]), p(st["Sk2"][b]), p(st["Sv"][b]), stream)
-        st["reccnt"][b].zero_()
+        if "reccnt" in st:
+            st["reccnt"][b].zero_()
         self._n0_dev.fill_(T)
 
     # ---------------------------------------------------------------- decode step
@@ -223,18 +225,18 @@ class OursB200:
         st, Lmax = self.st[l], self.Lmax
         K, V = C.K[l], C.V[l]
         n_dev = C.n_dev if C.n_dev is not None else self._n_dev.fill_(n)
-        n0_dev = C.n0_dev if C.n0_dev is not None else self._n0_dev
         ns, nl, k_top = step_split(n, self.a.rho, self.C, self.E)
         qr = q.reshape(self.R, D)
         if not qr.is_contiguous():
             qr = qr.contiguous()
         sel = self._sel_buf(ns + nl + k_top)
         S.index_update(K, V, st, n_dev, q=qr, zq=self.zq)
-        S.qgs_scan(st["codes"], self.zq, n_dev, ns, nl, self.scores, self.tmax)
+        S.qgs_scan(st["codes"], self.zq, n_dev, ns, nl, self.scores, self.tmax, self.status)
         S.qgs_select(self.scores, self.tmax, Lmax, n_dev, ns, nl, k_top, sel)
-        S.errorgate_waterfill(qr, K, st, sel, self.E, self.score, self.nt, self.quota)
-        S.topq(self.scores, st, self.quota, self.E, n_dev, n0_dev, self.exp_idx)
-        S.residual(K, V, st, sel, self.exp_idx, self.nt, self.quota, self.kbar, self.vbar, self.logn)
+        S.errorgate_waterfill(qr, K, st, sel, self.E, self.score, self.nt, self.quota, self.status)
+        n0_dev = C.n0_dev if C.n0_dev is not None else self._n0_dev
+        S.topq(self.scores, st, self.quota, self.E, n_dev, n0_dev, self.exp_idx, self.status)
+        S.residual(K, V, st, sel, self.exp_idx, self.nt, self.quota, self.kbar, self.vbar, self.logn, self.status)
         self._quota = self.quota
         self.read_frac = (ns + nl + k_top + self.E + 1.5 * self.C) / n
         return qr, sel

@@ -44,14 +44,14 @@ def index_update(K, V, st, n_dev, q=None, zq=None):
               _stream(K))
 
 
-def qgs_scan(codes, zq, n_dev, ns, nl, scores, tile_max):
+def qgs_scan(codes, zq, n_dev, ns, nl, scores, tile_max, status=None):
     B, _, Lmax, _ = codes.shape
     _need("codes", codes, torch.int8)
     _need("zq", zq, torch.bfloat16, (B * HQ, RQ))
     if scores.dtype != torch.bfloat16 or tile_max.dtype != torch.float32 or scores.stride(1) != 1:
         raise RuntimeError("scores must be bf16 (R, >= Lmax) and tile_max fp32 (R, >= NT)")
     _lib.call("oa_qgs_scan", _ptr(codes), _ptr(zq), B, Lmax, _ptr(n_dev), int(ns), int(nl), _ptr(scores),
-              scores.stride(0), _ptr(tile_max), tile_max.stride(0), _stream(codes))
+              scores.stride(0), _ptr(tile_max), tile_max.stride(0), _ptr(status), _stream(codes))
 
 
 def qgs_select(scores, tile_max, Lmax, n_dev, ns, nl, k_top, sel):
@@ -61,7 +61,7 @@ def qgs_select(scores, tile_max, Lmax, n_dev, ns, nl, k_top, sel):
               _ptr(n_dev), int(ns), int(nl), int(k_top), _ptr(sel), _stream(scores))
 
 
-def errorgate_waterfill(q, K, st, sel, E, score, nt, quota):
+def errorgate_waterfill(q, K, st, sel, E, score, nt, quota, status=None):
     B, _, Lmax, _ = K.shape
     C = st["nb"].shape[-1]
     R = B * HQ
@@ -70,10 +70,10 @@ def errorgate_waterfill(q, K, st, sel, E, score, nt, quota):
     _need("sel", sel, torch.int32)
     _lib.call("oa_errorgate_waterfill", _ptr(q), q.stride(0), _ptr(K), B, Lmax, C, _ptr(st["asg"]), _ptr(sel),
               sel.shape[1], _ptr(st["Sk"]), _ptr(st["Sk2"]), _ptr(st["nb"]), float(E), _ptr(score), _ptr(nt),
-              _ptr(quota), _stream(K))
+              _ptr(quota), _ptr(status), _stream(K))
 
 
-def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx):
+def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx, status=None):
     R = scores.shape[0]
     B, _, Lmax = st["asg"].shape
     C = st["nb"].shape[-1]
@@ -82,10 +82,10 @@ def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx):
     _lib.call("oa_topq", _ptr(scores), scores.stride(0), R, Lmax, C, _ptr(st["mem"]), _ptr(st["cstart"]),
               _ptr(st["clen"]), _ptr(st["asg"]), _ptr(rec), _ptr(st.get("reccnt")),
               0 if rec is None else rec.shape[-1], _ptr(quota), E, _ptr(n_dev), _ptr(n0_dev), _ptr(exp_idx),
-              _stream(scores))
+              _ptr(status), _stream(scores))
 
 
-def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn):
+def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn, status=None):
     B, _, Lmax, _ = K.shape
     C = st["nb"].shape[-1]
     R = B * HQ
@@ -94,15 +94,25 @@ def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn):
     _need("logn", logn, torch.float32, (R, C))
     _lib.call("oa_residual", _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["asg"]), _ptr(sel), sel.shape[1], _ptr(exp_idx),
               exp_idx.shape[1], _ptr(st["Sk"]), _ptr(st["Sv"]), _ptr(nt), _ptr(quota), _ptr(kbar), _ptr(vbar),
-              _ptr(logn), _stream(K))
+              _ptr(logn), _ptr(status), _stream(K))
+
+
+def padded_len(Lmax: int) -> int:
+    """Row length of the per-token score buffer: Lmax rounded up to 256 tokens."""
+    return (Lmax + 255) // 256 * 256
 
 
 def new_state(B: int, Lmax: int, C: int, device, rmax: int = 256) -> dict:
-    """Per-layer index state (the layout contract of methods_eager.Ours / OursG2 state, int8 codes)."""
+    """Per-layer index state: the layout contract of methods_eager.Ours / OursG2 (int8 codes, CSR
+    member lists, generated-token lists of rmax entries per cluster; rmax = 0 leaves them out, the
+    top-q stage then finds generated tokens by scanning the assignments)."""
     z = lambda *s, dt=torch.float32: torch.zeros(*s, device=device, dtype=dt)  # noqa: E731
-    return dict(codes=z(B, HKV, Lmax, RQ, dt=torch.int8), U=z(B, HKV, D, RQ), scale=z(B, HKV, RQ),
-                W=z(B, HQ, D, RC, dt=torch.bfloat16), colmean=z(B, HQ, RC), cent=z(B, HQ, C, RC),
-                asg=z(B, HQ, Lmax, dt=torch.int32), nb=z(B, HQ, C), Sk=z(B, HQ, C, D), Sk2=z(B, HQ, C, D),
-                Sv=z(B, HQ, C, D), mem=z(B, HQ, Lmax, dt=torch.int32), cstart=z(B, HQ, C, dt=torch.int32),
-                clen=z(B, HQ, C, dt=torch.int32), reclist=z(B, HQ, C, rmax, dt=torch.int32),
-                reccnt=z(B, HQ, C, dt=torch.int32))
+    st = dict(codes=z(B, HKV, Lmax, RQ, dt=torch.int8), U=z(B, HKV, D, RQ), scale=z(B, HKV, RQ),
+              W=z(B, HQ, D, RC, dt=torch.bfloat16), colmean=z(B, HQ, RC), cent=z(B, HQ, C, RC),
+              asg=z(B, HQ, Lmax, dt=torch.int32), nb=z(B, HQ, C), Sk=z(B, HQ, C, D), Sk2=z(B, HQ, C, D),
+              Sv=z(B, HQ, C, D), mem=z(B, HQ, Lmax, dt=torch.int32), cstart=z(B, HQ, C, dt=torch.int32),
+              clen=z(B, HQ, C, dt=torch.int32))
+    if rmax > 0:
+        st["reclist"] = z(B, HQ, C, rmax, dt=torch.int32)
+        st["reccnt"] = z(B, HQ, C, dt=torch.int32)
+    return st
