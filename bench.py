@@ -42,7 +42,7 @@ METRIC = "decode-attn-stage µs/step @32K ctx, bs32, 1% read; % HBM roofline; ms
 UNIT = "µs/step"
 B_PER_GPU, N_CTX, RHO = 32, 32768, 0.01
 SCAN_BYTES_PER_TOKEN = 32  # int8 codes per token per KV head (the scan's algorithmic bytes)
-LAUNCHES_PER_STEP = 7      # index_update, qgs_scan, qgs_select, errorgate_waterfill, topq, residual, flash
+LAUNCHES_PER_STEP = 6      # index_update, qgs_scan, qgs_select, errorgate_waterfill, topq, residual_flash
 
 
 def dist_env():

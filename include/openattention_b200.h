@@ -100,14 +100,14 @@ int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64
 
 /* QGS scan: scores (B*32, score_stride) bf16 = exact int8 dot products of codes and zq, rounded to
  * fp32 then bf16, -inf for t < ns and t >= n - nl; tile_max (B*32, tile_max_stride) fp32 = maximum
- * of each 256-token tile.  Replaces _k_qgs_scan_tm (inference/graph_runner.py:100-120).
+ * of each 32-token tile (tile_max_stride >= ceil(Lmax / 32)).  Replaces _k_qgs_scan_tm (inference/graph_runner.py:100-120).
  * status (may be NULL): device int32 set to 1 if a bulk copy of the codes did not complete within
  * the kernel's bounded wait (the affected tiles are then not computed). */
 int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64_t Lmax, const int32_t* n_dev, int ns, int nl,
                 void* scores, int64_t score_stride, float* tile_max, int64_t tile_max_stride, int32_t* status,
                 void* stream);
 
-/* Row top-k among the 2k tiles with the largest maxima (exact), ties -> lower position;
+/* Row top-k among the 2k 32-token tiles with the largest maxima (exact), ties -> lower position;
  * sel (R, ns+nl+k_top) int32 = [0..ns-1, n-nl..n-1, top-k by rank]; the selected scores are set to
  * -inf in `scores`.  Replaces _k_select (inference/graph_runner.py:123-159).  k_top <= 64. */
 int oa_qgs_select(void* scores, int64_t score_stride, const float* tile_max, int64_t tile_max_stride, int64_t R,
@@ -145,6 +145,18 @@ int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C
                 const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E, const float* Sk,
                 const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar, float* log_n,
                 int32_t* status, void* stream);
+
+/* Residual proxies and OpenAttention.flash in one pass (per-query-head proxies, the deployed
+ * combination of oa_residual + oa_flash_qhead_proxies): the read tokens' K/V rows are gathered once
+ * and used both for the pooled-sum subtraction and for the online softmax; the bf16-rounded proxies
+ * are attended from on-chip memory.  kbar / vbar / log_n outputs may be NULL (then not written).
+ * Inputs as oa_residual; out (B*32, 128) bf16 or fp32 (out_dtype) with row stride out_stride.
+ * status: as oa_errorgate_waterfill (value 5). */
+int oa_residual_flash(const void* q, int64_t q_stride, const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C,
+                      const int32_t* asg, const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E,
+                      const float* Sk, const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar,
+                      float* log_n, void* out, int64_t out_stride, int out_dtype, float sm_scale, int32_t* status,
+                      void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * Per-request build (prefill).  Each call works on ONE request: K, V (8, Lmax, 128) bf16 with the

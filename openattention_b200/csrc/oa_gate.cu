@@ -49,7 +49,6 @@ struct GateArgs {
   int32_t* status;
 };
 
-constexpr int kChunkC = 64;  // clusters whose pooled-sum rows are staged in shared memory at once
 
 __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const GateArgs a) {
   const int r = blockIdx.x;
@@ -236,14 +235,14 @@ __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const
 }
 
 // ------------------------------------------------------------------------ within-cluster top-q
-// One CTA (16 warps) per row.  The row's bf16 score spill is staged in shared memory by one bulk
+// One CTA (8 warps) per row.  The row's bf16 score spill is staged in shared memory by one bulk
 // copy when it fits (else keys are read from global memory).  Warps take the clusters with q > 0:
 // the candidates are the cluster's CSR members (ascending position) followed by its generated
 // tokens (the per-cluster list, or a scan of asg over [n0, n) when the list overflowed).
 //   q <= 32 and <= 1024 candidates: packed (key, list index) words in registers, q rounds of warp
 //     max extraction (ties -> lower list index = lower position), winners sorted by position
 //   otherwise: two 8-bit radix passes for the threshold key, then an ordered collection
-constexpr int kTqThreads = 512;
+constexpr int kTqThreads = 256;
 constexpr int kTqWarps = kTqThreads / 32;
 constexpr int kRegCand = 32;  // candidates per lane in the register path
 constexpr int kSmallQ = 32;
@@ -268,7 +267,7 @@ struct TopqArgs {
 
 __device__ __forceinline__ uint32_t ukey16(uint32_t b) { return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u); }
 
-__global__ void __launch_bounds__(kTqThreads, 1) topq_kernel(const TopqArgs a) {
+__global__ void __launch_bounds__(kTqThreads, 2) topq_kernel(const TopqArgs a) {
   extern __shared__ __align__(128) uint16_t s_spill[];  // the row's scores (when a.smem_keys)
   __shared__ __align__(8) uint64_t mbar;
   __shared__ int s_base[kMaxC + 1];
@@ -462,8 +461,25 @@ __global__ void __launch_bounds__(kTqThreads, 1) topq_kernel(const TopqArgs a) {
   }
 }
 
-// ------------------------------------------------------------------------ residual proxies
+// ------------------------------------------------------------------------ residual proxies (+ flash)
+// One CTA (8 warps) per row; warp w owns the clusters c = c0 + w + 8k (k < 8) of each 64-cluster
+// chunk and keeps their running sums Sk - sum k, Sv - sum v in registers (lane <-> dims lane + 32i).
+// The row's read tokens (sel, then the exp slots) are gathered 32 at a time into a double-buffered
+// shared-memory ring (cp.async), so the next chunk loads while this one is used.  For every chunk a
+// warp subtracts, in list order, the tokens of its clusters (a cluster's exp tokens are one
+// contiguous segment [base_c, base_c + q_c)); with ATTEND the warps also run the online softmax
+// over the chunk's tokens (P1/P2).  At the end each warp turns its sums into kbar' / vbar' (bf16, as
+// the reference stores them) and ln n', writes them if asked, and with ATTEND attends them as
+// proxies (P3) straight from registers; the 8 warp states are merged into the output.
+constexpr int kRW = 8;         // warps per CTA
+constexpr int kRPer = 8;       // clusters per warp per chunk
+constexpr int kChunkC = kRW * kRPer;
+constexpr int kTok = 32;       // tokens per gather buffer
+constexpr int kMaxRead = 2048;  // NS + E
+
 struct ResidArgs {
+  const __nv_bfloat16* q;  // ATTEND only
+  int64_t q_stride;
   const __nv_bfloat16* K;
   const __nv_bfloat16* V;
   int Lmax, C, NS, E;
@@ -474,33 +490,68 @@ struct ResidArgs {
   const float* Sv;
   const float* nt;
   const float* quota;
-  __nv_bfloat16* kbar;
+  __nv_bfloat16* kbar;  // may be null (then not written)
   __nv_bfloat16* vbar;
   float* logn;
+  void* out;  // ATTEND only
+  int64_t out_stride;
+  int out_f32;
+  float qk_scale;  // sm_scale * log2(e)
   int32_t* status;
 };
 
-constexpr int kTokChunk = 64;   // read tokens whose K/V rows are gathered into shared memory at once
-constexpr int kMaxRead = 2048;  // NS + E
+struct SoftmaxState {
+  float m, l, acc[4];
+  __device__ __forceinline__ void init() {
+    m = -INFINITY;
+    l = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = 0.f;
+  }
+  // one entry with log2-domain logit z (warp-uniform) and value lanes v[4]
+  __device__ __forceinline__ void add(float z, const float (&v)[4]) {
+    if (z == -INFINITY) return;
+    const float mx = fmaxf(m, z);
+    const float alpha = exp2f(m - mx);
+    const float p = exp2f(z - mx);
+    l = fmaf(l, alpha, p);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = fmaf(acc[i], alpha, p * v[i]);
+    m = mx;
+  }
+};
 
-__global__ void __launch_bounds__(kGateThreads) residual_kernel(const ResidArgs a) {
+__device__ __forceinline__ float warp_dot4(const float (&a)[4], const float (&b)[4]) {
+  float d = a[0] * b[0];
+  d = fmaf(a[1], b[1], d);
+  d = fmaf(a[2], b[2], d);
+  d = fmaf(a[3], b[3], d);
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) d += __shfl_xor_sync(0xffffffffu, d, off);
+  return d;
+}
+
+template <bool ATTEND>
+__global__ void __launch_bounds__(kRW * 32, 2) residual_kernel(const ResidArgs a) {
   const int r = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kv = r / kG;
   const int C = a.C;
-  extern __shared__ __align__(128) float rsm[];
-  float* sSk = rsm;                                                    // [kChunkC][kD]
-  float* sSv = rsm + kChunkC * kD;                                     // [kChunkC][kD]
-  __nv_bfloat16* sK = reinterpret_cast<__nv_bfloat16*>(rsm + 2 * kChunkC * kD);  // [kTokChunk][kD]
-  __nv_bfloat16* sV = sK + kTokChunk * kD;                                         // [kTokChunk][kD]
-  __shared__ __align__(8) uint64_t mbar;
+  __shared__ __align__(16) __nv_bfloat16 sK[2][kTok][kD];
+  __shared__ __align__(16) __nv_bfloat16 sV[2][kTok][kD];
   __shared__ int s_tok[kMaxRead];
   __shared__ int16_t s_tc[kMaxRead];
   __shared__ int s_base[kMaxC + 1];
   __shared__ int s_q[kMaxC];
-  const uint32_t bar = smem_u32(&mbar);
-  if (tid == 0) mbar_init(bar);
+  __shared__ float s_m[kRW], s_l[kRW];
   for (int c = tid; c < C; c += blockDim.x) s_q[c] = (int)a.quota[(int64_t)r * C + c];
+  const int NT = a.NS + a.E;
+  for (int j = tid; j < NT; j += blockDim.x) {
+    const int t = j < a.NS ? a.sel[(int64_t)r * a.NS + j] : a.exp[(int64_t)r * a.E + (j - a.NS)];
+    const bool v = t >= 0 && t < a.Lmax;
+    s_tok[j] = v ? t : -1;
+    s_tc[j] = v ? (int16_t)a.asg[(int64_t)r * a.Lmax + t] : (int16_t)-1;
+  }
   __syncthreads();
   if (tid == 0) {
     int run = 0;
@@ -510,59 +561,65 @@ __global__ void __launch_bounds__(kGateThreads) residual_kernel(const ResidArgs 
     }
     s_base[C] = run;
   }
-  const int NT = a.NS + a.E;
-  // the row's read tokens in subtraction order (sel, then exp slots) with their clusters
-  for (int j = tid; j < NT; j += blockDim.x) {
-    const int t = j < a.NS ? a.sel[(int64_t)r * a.NS + j] : a.exp[(int64_t)r * a.E + (j - a.NS)];
-    const bool v = t >= 0 && t < a.Lmax;
-    s_tok[j] = v ? t : -1;
-    s_tc[j] = v ? (int16_t)a.asg[(int64_t)r * a.Lmax + t] : (int16_t)-1;
+  float qv[4];
+  SoftmaxState sm;
+  sm.init();
+  if (ATTEND) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qv[i] = __bfloat162float(a.q[(int64_t)r * a.q_stride + lane + 32 * i]);
   }
-  __syncthreads();
   const __nv_bfloat16* Kr = a.K + (int64_t)kv * a.Lmax * kD;
   const __nv_bfloat16* Vr = a.V + (int64_t)kv * a.Lmax * kD;
-  uint32_t phase = 0;
+  const int nchunks = (NT + kTok - 1) / kTok;
+  __syncthreads();
   for (int c0 = 0; c0 < C; c0 += kChunkC) {
-    const int nc = min(kChunkC, C - c0);
-    if (tid == 0) {
-      const uint32_t bytes = (uint32_t)nc * kD * sizeof(float);
-      mbar_expect(bar, 2 * bytes);
-      bulk_copy(sSk, a.Sk + ((int64_t)r * C + c0) * kD, bytes, bar);
-      bulk_copy(sSv, a.Sv + ((int64_t)r * C + c0) * kD, bytes, bar);
+    const bool first = c0 == 0;  // the token streams are attended during the first cluster chunk
+    // this warp's clusters and their running sums
+    float sk[kRPer][4], sv[kRPer][4];
+#pragma unroll
+    for (int k = 0; k < kRPer; ++k) {
+      const int c = c0 + warp + kRW * k;
+      const int64_t base = ((int64_t)r * C + min(c, C - 1)) * kD;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        sk[k][i] = c < C ? a.Sk[base + lane + 32 * i] : 0.f;
+        sv[k][i] = c < C ? a.Sv[base + lane + 32 * i] : 0.f;
+      }
     }
-    const bool ok = mbar_wait(bar, phase);
-    phase ^= 1u;
-    if (!__syncthreads_and(ok)) {
-      if (tid == 0 && a.status != nullptr) atomicExch(a.status, 3);
-      if (!ok) mbar_wait(bar, phase ^ 1u);
-      return;
-    }
-    for (int j0 = 0; j0 < NT; j0 += kTokChunk) {
-      const int nj = min(kTokChunk, NT - j0);
-      // gather the chunk's K and V rows: 16 bytes per cp.async, 2 * 16 per row
+    auto gather = [&](int ch) {  // rows of chunk ch into buffer ch & 1 (one cp.async group)
+      const int j0 = ch * kTok, nj = min(kTok, NT - j0), b = ch & 1;
       for (int e = tid; e < nj * 32; e += blockDim.x) {
         const int j = e >> 5, part = e & 31;  // part < 16: K row, else V row
         const int t = s_tok[j0 + j];
         const int tc = s_tc[j0 + j];
-        if (t >= 0 && tc >= c0 && tc < c0 + nc) {
+        if (t >= 0 && (first || (tc >= c0 && tc < c0 + kChunkC))) {
           const __nv_bfloat16* src = (part < 16 ? Kr : Vr) + (int64_t)t * kD + (part & 15) * 8;
-          __nv_bfloat16* dst = (part < 16 ? sK : sV) + j * kD + (part & 15) * 8;
+          __nv_bfloat16* dst = (part < 16 ? &sK[b][j][0] : &sV[b][j][0]) + (part & 15) * 8;
           asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
         }
       }
-      asm volatile("cp.async.wait_all;" ::: "memory");
+      asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    gather(0);
+    for (int ch = 0; ch < nchunks; ++ch) {
+      if (ch + 1 < nchunks) {
+        gather(ch + 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      }
       __syncthreads();
-      // subtract in order, each (cluster, dim) by one thread: warp per cluster, lane per 4 dims.
-      // A cluster's tokens in this chunk: its selected tokens (list positions < NS, checked one by
-      // one) and the part of its exp segment [NS + base_c, NS + base_c + q_c) inside the chunk.
-      for (int cc = warp; cc < nc; cc += kGateThreads / 32) {
-        const int c = c0 + cc;
+      const int j0 = ch * kTok, nj = min(kTok, NT - j0), b = ch & 1;
+      // residual: this warp's clusters, tokens in list order
+#pragma unroll
+      for (int k = 0; k < kRPer; ++k) {
+        const int c = c0 + warp + kRW * k;
+        if (c >= C) break;
         auto sub = [&](int j) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
-            const int d = lane + 32 * i;
-            sSk[cc * kD + d] = __fsub_rn(sSk[cc * kD + d], __bfloat162float(sK[j * kD + d]));
-            sSv[cc * kD + d] = __fsub_rn(sSv[cc * kD + d], __bfloat162float(sV[j * kD + d]));
+            sk[k][i] = __fsub_rn(sk[k][i], __bfloat162float(sK[b][j][lane + 32 * i]));
+            sv[k][i] = __fsub_rn(sv[k][i], __bfloat162float(sV[b][j][lane + 32 * i]));
           }
         };
         for (int j = j0; j < min(j0 + nj, a.NS); ++j)
@@ -571,22 +628,79 @@ __global__ void __launch_bounds__(kGateThreads) residual_kernel(const ResidArgs 
         for (int j = e_lo; j < e_hi; ++j)
           if (s_tok[j] >= 0) sub(j - j0);
       }
-      __syncthreads();  // the gather buffer is refilled by the next chunk
+      if (ATTEND && first) {  // P1/P2: warp w takes the chunk's tokens w, w+8, ...
+        for (int j = warp; j < nj; j += kRW) {
+          if (s_tok[j0 + j] < 0) continue;
+          float kx[4], vx[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            kx[i] = __bfloat162float(sK[b][j][lane + 32 * i]);
+            vx[i] = __bfloat162float(sV[b][j][lane + 32 * i]);
+          }
+          sm.add(warp_dot4(qv, kx) * a.qk_scale, vx);
+        }
+      }
+      __syncthreads();  // buffer b is refilled by chunk ch + 2
     }
-    for (int cc = warp; cc < nc; cc += kGateThreads / 32) {
-      const int c = c0 + cc;
-      const int64_t base = ((int64_t)r * C + c) * kD;
+    // proxies of this warp's clusters
+#pragma unroll
+    for (int k = 0; k < kRPer; ++k) {
+      const int c = c0 + warp + kRW * k;
+      if (c >= C) break;
       const float nr = __fsub_rn(a.nt[(int64_t)r * C + c], a.quota[(int64_t)r * C + c]);
       const float inv = __fdiv_rn(1.f, fmaxf(nr, 1.f));
+      const int64_t base = ((int64_t)r * C + c) * kD;
+      float kb[4], vb[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int d = lane + 32 * i;
-        a.kbar[base + d] = __float2bfloat16_rn(__fmul_rn(sSk[cc * kD + d], inv));
-        a.vbar[base + d] = __float2bfloat16_rn(__fmul_rn(sSv[cc * kD + d], inv));
+        const __nv_bfloat16 kh = __float2bfloat16_rn(__fmul_rn(sk[k][i], inv));
+        const __nv_bfloat16 vh = __float2bfloat16_rn(__fmul_rn(sv[k][i], inv));
+        kb[i] = __bfloat162float(kh);
+        vb[i] = __bfloat162float(vh);
+        if (a.kbar != nullptr) {
+          a.kbar[base + lane + 32 * i] = kh;
+          a.vbar[base + lane + 32 * i] = vh;
+        }
       }
-      if (lane == 0) a.logn[(int64_t)r * C + c] = nr > 0.5f ? ln_f(fmaxf(nr, 1.f)) : -INFINITY;
+      float ln = 0.f;
+      if (lane == 0) {
+        ln = nr > 0.5f ? ln_f(fmaxf(nr, 1.f)) : -INFINITY;
+        if (a.logn != nullptr) a.logn[(int64_t)r * C + c] = ln;
+      }
+      if (ATTEND) {
+        ln = __shfl_sync(0xffffffffu, ln, 0);
+        if (ln > -INFINITY) sm.add(fmaf(warp_dot4(qv, kb), a.qk_scale, ln * kLog2e), vb);
+      }
     }
-    __syncthreads();  // the pooled-sum buffers are refilled by the next cluster chunk
+  }
+  if (!ATTEND) return;
+  // the gather ring is free now (every chunk loop ended with a barrier): merge area for the warps
+  float(*s_acc)[kD] = reinterpret_cast<float(*)[kD]>(&sK[0][0][0]);
+  if (lane == 0) {
+    s_m[warp] = sm.m;
+    s_l[warp] = sm.l;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) s_acc[warp][lane + 32 * i] = sm.acc[i];
+  __syncthreads();
+  if (tid < kD) {
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < kRW; ++w) M = fmaxf(M, s_m[w]);
+    float L = 0.f, A = 0.f;
+    if (M > -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < kRW; ++w) {
+        const float wt = exp2f(s_m[w] - M);
+        L = fmaf(wt, s_l[w], L);
+        A = fmaf(wt, s_acc[w][tid], A);
+      }
+    }
+    const float o = L > 0.f ? A / L : 0.f;
+    if (a.out_f32)
+      reinterpret_cast<float*>(a.out)[(int64_t)r * a.out_stride + tid] = o;
+    else
+      reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)r * a.out_stride + tid] = __float2bfloat16_rn(o);
   }
 }
 
@@ -638,22 +752,33 @@ extern "C" int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax
                            int32_t* status, void* stream) {
   const char* fn = "oa_residual";
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
-  OA_REQUIRE(n_sel > 0 && n_sel <= 512, "%s: n_sel outside [1, 512]", fn);
+  OA_REQUIRE(n_sel > 0 && n_sel + E <= kMaxRead, "%s: need 0 < n_sel and n_sel + E <= %d", fn, kMaxRead);
   OA_REQUIRE(K && V && asg && sel && exp_idx && Sk && Sv && nt && quota && kbar && vbar && logn, "%s: null pointer",
              fn);
-  OA_REQUIRE(oa_aligned16(Sk) && oa_aligned16(Sv) && oa_aligned16(K) && oa_aligned16(V),
-             "%s: Sk / Sv / K / V must be 16-byte aligned", fn);
-  OA_REQUIRE(n_sel + E <= kMaxRead, "%s: n_sel + E > %d", fn, kMaxRead);
-  ResidArgs a{static_cast<const __nv_bfloat16*>(K), static_cast<const __nv_bfloat16*>(V), (int)Lmax, (int)C,
-              (int)n_sel, (int)E, asg, sel, exp_idx, Sk, Sv, nt, quota, static_cast<__nv_bfloat16*>(kbar),
-              static_cast<__nv_bfloat16*>(vbar), logn, status};
-  constexpr size_t smem = 2 * (size_t)kChunkC * kD * sizeof(float) + 2 * (size_t)kTokChunk * kD * 2;
-  static bool attr_set = false;  // idempotent attribute, set once per process
-  if (!attr_set) {
-    cudaError_t e = cudaFuncSetAttribute(residual_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-    attr_set = true;
-  }
-  residual_kernel<<<(unsigned)(B * kHQ), kGateThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  OA_REQUIRE(oa_aligned16(K) && oa_aligned16(V), "%s: K / V must be 16-byte aligned", fn);
+  ResidArgs a{nullptr, 0, static_cast<const __nv_bfloat16*>(K), static_cast<const __nv_bfloat16*>(V), (int)Lmax,
+              (int)C, (int)n_sel, (int)E, asg, sel, exp_idx, Sk, Sv, nt, quota, static_cast<__nv_bfloat16*>(kbar),
+              static_cast<__nv_bfloat16*>(vbar), logn, nullptr, 0, 0, 0.f, status};
+  residual_kernel<false><<<(unsigned)(B * kHQ), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  return oa_check_launch(fn);
+}
+
+extern "C" int oa_residual_flash(const void* q, int64_t q_stride, const void* K, const void* V, int64_t B, int64_t Lmax,
+                                 int64_t C, const int32_t* asg, const int32_t* sel, int64_t n_sel,
+                                 const int32_t* exp_idx, int64_t E, const float* Sk, const float* Sv, const float* nt,
+                                 const float* quota, void* kbar, void* vbar, float* logn, void* out,
+                                 int64_t out_stride, int out_dtype, float sm_scale, int32_t* status, void* stream) {
+  const char* fn = "oa_residual_flash";
+  OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
+  OA_REQUIRE(n_sel > 0 && n_sel + E <= kMaxRead, "%s: need 0 < n_sel and n_sel + E <= %d", fn, kMaxRead);
+  OA_REQUIRE(q && K && V && asg && sel && exp_idx && Sk && Sv && nt && quota && out, "%s: null pointer", fn);
+  OA_REQUIRE((kbar == nullptr) == (vbar == nullptr), "%s: kbar and vbar are given together", fn);
+  OA_REQUIRE(out_dtype == OA_BF16 || out_dtype == OA_F32, "%s: out_dtype must be OA_BF16 or OA_F32", fn);
+  OA_REQUIRE(oa_aligned16(K) && oa_aligned16(V), "%s: K / V must be 16-byte aligned", fn);
+  ResidArgs a{static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(K),
+              static_cast<const __nv_bfloat16*>(V), (int)Lmax, (int)C, (int)n_sel, (int)E, asg, sel, exp_idx, Sk, Sv,
+              nt, quota, static_cast<__nv_bfloat16*>(kbar), static_cast<__nv_bfloat16*>(vbar), logn, out,
+              out_stride, out_dtype == OA_F32 ? 1 : 0, sm_scale * kLog2e, status};
+  residual_kernel<true><<<(unsigned)(B * kHQ), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }

@@ -145,8 +145,9 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
 }
 
 // ------------------------------------------------------------------------ QGS scan (int8 MMA)
-constexpr int kTile = 256;         // tokens per tile maximum
-constexpr int kScanThreads = 256;  // 8 warps x 32 tokens = one tile per step
+constexpr int kTile = 256;         // tokens per CTA step (8 warps x 32 tokens)
+constexpr int kMaxTile = 32;       // tokens per tile maximum (one warp's share of a step)
+constexpr int kScanThreads = 256;
 constexpr int kTilesPerCta = 4;
 
 struct ScanArgs {
@@ -186,7 +187,6 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
   __shared__ __align__(8) uint64_t mbar;
   __shared__ int8_t limb[kG][4][kRQ];  // [head][limb][j]
   __shared__ int sS[kG];
-  __shared__ float s_max[kTilesPerCta][8][kG];
   const int t_begin = blockIdx.y * kTilesPerCta;
   const int tok0 = t_begin * kTile;
   const int ntok = max(0, min(min(a.Lmax, n), tok0 + kTilesPerCta * kTile) - tok0);  // tokens to fetch
@@ -241,7 +241,7 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
     const int tile = t_begin + ti;
     const int t0 = tile * kTile;
     float hmax[2] = {-INFINITY, -INFINITY};  // for heads fin_head[0], fin_head[1]
-    if (tile < a.NT && t0 < n) {
+    if (t0 < n && t0 < a.Lmax) {
 #pragma unroll
       for (int grp = 0; grp < 2; ++grp) {
         const int lt0 = ti * kTile + warp * 32 + grp * 16;  // chunk-local first token of the 16
@@ -278,7 +278,9 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
         }
       }
     }
-    // per-warp tile maximum per head: lanes with equal tig>>1 hold head 2m + (tig>>1)
+    // maximum of this warp's 32 tokens per head (a 32-token tile): lanes with equal tig>>1 hold
+    // head 2m + (tig>>1); written directly, no cross-warp reduction
+    const int wt = tile * (kTile / kMaxTile) + warp;  // 32-token tile index
 #pragma unroll
     for (int m = 0; m < 2; ++m) {
       float v = hmax[m];
@@ -286,19 +288,8 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
       v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
       v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
       v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
-      if (lane == 0) s_max[ti][warp][2 * m] = v;      // tig 0 -> head 2m
-      if (lane == 2) s_max[ti][warp][2 * m + 1] = v;  // tig 2 -> head 2m + 1
-    }
-  }
-  __syncthreads();
-  if (tid < kTilesPerCta * kG) {
-    const int ti = tid / kG, h = tid % kG;
-    const int tile = t_begin + ti;
-    if (tile < a.NT) {
-      float v = -INFINITY;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) v = fmaxf(v, s_max[ti][w][h]);
-      a.tmax[(int64_t)(kv * kG + h) * a.tm_stride + tile] = v;
+      if (wt < a.NT && (lane == 0 || lane == 2))
+        a.tmax[(int64_t)(kv * kG + 2 * m + (lane >> 1)) * a.tm_stride + wt] = v;
     }
   }
 }
@@ -401,12 +392,12 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   // per warp: tile keys (NT uint32), then candidate keys (kt2_max * 256 uint16)
   uint32_t* tkey = reinterpret_cast<uint32_t*>(sel_smem) + (size_t)warp * a.NT_pad;
   uint16_t* ckey = reinterpret_cast<uint16_t*>(reinterpret_cast<uint32_t*>(sel_smem) + (size_t)kSelWarps * a.NT_pad) +
-                   (size_t)warp * a.kt2_max * kTile;
+                   (size_t)warp * a.kt2_max * kMaxTile;
   if (r >= a.R) return;
   int* hist = s_hist[warp];
   int* tiles = s_tiles[warp];
   const int n = __ldg(a.n_dev);
-  const int ntv = min(a.NT, (n + kTile - 1) / kTile);
+  const int ntv = min(a.NT, (n + kMaxTile - 1) / kMaxTile);
   const int kt2 = min(2 * a.k_top, ntv);
   const float* tm = a.tmax + (int64_t)r * a.tm_stride;
   uint16_t* srw = a.scores + (int64_t)r * a.sw;
@@ -434,9 +425,9 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   __syncwarp();
   // (2) candidate keys of the chosen tiles (ascending tile order) staged with 16-byte loads;
   //     positions >= n get key 0 (below every real key, which is >= 0x7f)
-  const int m = kt2 * kTile;
+  const int m = kt2 * kMaxTile;
   for (int i = lane * 8; i < m; i += 32 * 8) {
-    const int pos = tiles[i >> 8] * kTile + (i & (kTile - 1));
+    const int pos = tiles[i >> 5] * kMaxTile + (i & (kMaxTile - 1));
     const uint4 w = *reinterpret_cast<const uint4*>(srw + pos);
     const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
@@ -467,7 +458,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
       const unsigned bt = __ballot_sync(0xffffffffu, take);
       const int slot = taken + __popc(bt & ((1u << lane) - 1u));
       if (take && slot < a.k_top) {
-        s_pos[warp][slot] = tiles[i >> 8] * kTile + (i & (kTile - 1));
+        s_pos[warp][slot] = tiles[i >> 5] * kMaxTile + (i & (kMaxTile - 1));
         s_key[warp][slot] = k;
       }
       taken += __popc(bt);
@@ -539,13 +530,14 @@ extern "C" int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64
   OA_REQUIRE(B > 0 && Lmax > 0 && Lmax < (1ll << 30), "%s: bad sizes", fn);
   OA_REQUIRE(codes && zq && n_dev && scores && tile_max, "%s: null pointer", fn);
   OA_REQUIRE(oa_aligned16(codes), "%s: codes must be 16-byte aligned", fn);
-  const int NT = (int)((Lmax + kTile - 1) / kTile);
+  const int NT = (int)((Lmax + kMaxTile - 1) / kMaxTile);
   OA_REQUIRE(score_stride >= Lmax && tile_max_stride >= NT, "%s: score stride %lld < Lmax or tile-max stride < %d",
              fn, (long long)score_stride, NT);
   OA_REQUIRE(ns >= 0 && nl >= 0, "%s: negative sink/local", fn);
   ScanArgs a{codes, static_cast<const __nv_bfloat16*>(zq), n_dev, ns, nl, (int)Lmax, NT,
              static_cast<uint16_t*>(scores), score_stride, tile_max, tile_max_stride, status};
-  dim3 grid((unsigned)(B * kHKV), (unsigned)((NT + kTilesPerCta - 1) / kTilesPerCta));
+  const int nsteps = (int)((Lmax + kTile - 1) / kTile);
+  dim3 grid((unsigned)(B * kHKV), (unsigned)((nsteps + kTilesPerCta - 1) / kTilesPerCta));
   qgs_scan_kernel<<<grid, kScanThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }
@@ -558,13 +550,13 @@ extern "C" int oa_qgs_select(void* scores, int64_t score_stride, const float* ti
   OA_REQUIRE(scores && tile_max && n_dev && sel, "%s: null pointer", fn);
   OA_REQUIRE(k_top >= 1 && 2 * k_top <= kMaxKT2, "%s: k_top=%d outside [1, %d]", fn, k_top, kMaxKT2 / 2);
   OA_REQUIRE(ns >= 0 && nl >= 0, "%s: negative sink/local", fn);
-  const int NT = (int)((Lmax + kTile - 1) / kTile);
+  const int NT = (int)((Lmax + kMaxTile - 1) / kMaxTile);
   OA_REQUIRE(score_stride % 8 == 0 && oa_aligned16(scores), "%s: scores rows must be 16-byte aligned", fn);
   const int NT_pad = (NT + 3) & ~3;
   const int kt2_max = std::min(2 * k_top, NT);
   SelectArgs a{static_cast<uint16_t*>(scores), score_stride, tile_max, tile_max_stride, n_dev, (int)R, ns, nl, k_top,
                NT, (int)Lmax, sel, NT_pad, kt2_max};
-  const size_t smem = (size_t)kSelWarps * (NT_pad * 4 + (size_t)kt2_max * kTile * 2);
+  const size_t smem = (size_t)kSelWarps * (NT_pad * 4 + (size_t)kt2_max * kMaxTile * 2);
   OA_REQUIRE(smem <= 200 * 1024, "%s: Lmax=%lld and k_top=%d need too much shared memory", fn, (long long)Lmax, k_top);
   if (smem > 48 * 1024) {
     cudaError_t e = cudaFuncSetAttribute(qgs_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

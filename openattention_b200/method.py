@@ -127,8 +127,15 @@ def load_static_metric(a, layers: int):
 # ------------------------------------------------------------------ the method
 class OursB200:
     """OpenAttention decode (QGS scan + top-k, ErrorGate + water-filling, within-cluster top-q,
-    residual proxies, OpenAttention.flash) with the per-request QGC/QGS build."""
+    residual proxies, OpenAttention.flash) with the per-request QGC/QGS build.
+
+    FUSED (default): the residual proxies and the attention run as one kernel (the K/V rows of the
+    read tokens are gathered once); keep_proxies additionally writes kbar', vbar', ln n' out.
+    FUSED = False runs oa_residual and then calls `flash.ours_flash` through the module attribute,
+    the hook the reference's tests spy on."""
     name = "ours3"
+    FUSED = True
+    keep_proxies = False
 
     def __init__(self, a, B, Lmax, dev, layers: int | None = None):
         self.a, self.B, self.Lmax = a, B, Lmax
@@ -145,7 +152,7 @@ class OursB200:
         self.scaling = scaling
         self.st = [S.new_state(B, Lmax, self.C, self.dev, RMAX) for _ in range(self.NL)]
         R, Cn, E, dev = self.R, self.C, self.E, self.dev
-        self.NT = (Lmax + 255) // 256
+        self.NT = (Lmax + 31) // 32          # 32-token tiles of the QGS tile maxima
         self.SW = S.padded_len(Lmax)
         self.zq = torch.zeros(R, RQ, dtype=torch.bfloat16, device=dev)
         self.scores = torch.zeros(R, self.SW, dtype=torch.bfloat16, device=dev)
@@ -219,9 +226,9 @@ class OursB200:
             self._sel[NS] = torch.zeros(self.R, NS, dtype=torch.int32, device=self.dev)
         return self._sel[NS]
 
-    def select(self, l, q, n):
+    def select(self, l, q, n, residual=True):
         """Stages 1-5 of the step: index update + zq, QGS scan + top-k, ErrorGate + water-filling,
-        within-cluster top-q, residual proxies.  Returns (sel, exp_idx, kbar', vbar', log n')."""
+        within-cluster top-q and (residual=True) the residual proxies.  Returns (q rows, sel)."""
         st, Lmax = self.st[l], self.Lmax
         K, V = C.K[l], C.V[l]
         n_dev = C.n_dev if C.n_dev is not None else self._n_dev.fill_(n)
@@ -236,14 +243,24 @@ class OursB200:
         S.errorgate_waterfill(qr, K, st, sel, self.E, self.score, self.nt, self.quota, self.status)
         n0_dev = C.n0_dev if C.n0_dev is not None else self._n0_dev
         S.topq(self.scores, st, self.quota, self.E, n_dev, n0_dev, self.exp_idx, self.status)
-        S.residual(K, V, st, sel, self.exp_idx, self.nt, self.quota, self.kbar, self.vbar, self.logn, self.status)
+        if residual:
+            S.residual(K, V, st, sel, self.exp_idx, self.nt, self.quota, self.kbar, self.vbar, self.logn,
+                       self.status)
         self._quota = self.quota
+        self.last_sel = sel
         self.read_frac = (ns + nl + k_top + self.E + 1.5 * self.C) / n
         return qr, sel
 
     def decode(self, l, q, n):
-        qr, sel = self.select(l, q, n)
-        return self.attend(l, qr, sel, self.exp_idx, self.kbar, self.vbar, self.logn)
+        if not self.FUSED:
+            qr, sel = self.select(l, q, n)
+            return self.attend(l, qr, sel, self.exp_idx, self.kbar, self.vbar, self.logn)
+        qr, sel = self.select(l, q, n, residual=False)
+        keep = self.keep_proxies
+        S.residual_flash(qr, C.K[l], C.V[l], self.st[l], sel, self.exp_idx, self.nt, self.quota, self.out,
+                         kbar=self.kbar if keep else None, vbar=self.vbar if keep else None,
+                         logn=self.logn if keep else None, status=self.status)
+        return self.out.view(self.B, HQ, 1, D)
 
     def attend(self, l, qr, sel, exp_idx, kbar_r, vbar_r, logn):
         """OpenAttention.flash with per-query-head proxies, called through the module attribute

@@ -97,6 +97,21 @@ def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn, status=None):
               _ptr(logn), _ptr(status), _stream(K))
 
 
+def residual_flash(q, K, V, st, sel, exp_idx, nt, quota, out, kbar=None, vbar=None, logn=None, sm_scale=128 ** -0.5,
+                   status=None):
+    """Residual proxies + OpenAttention.flash in one kernel; out (B*32, D) bf16 or fp32."""
+    B, _, Lmax, _ = K.shape
+    C = st["nb"].shape[-1]
+    R = B * HQ
+    if out.shape != (R, D) or out.stride(1) != 1 or out.dtype not in (torch.bfloat16, torch.float32):
+        raise RuntimeError("out must be (B*32, 128) bf16 or fp32 with a contiguous last dim")
+    code = _lib.OA_F32 if out.dtype == torch.float32 else _lib.OA_BF16
+    _lib.call("oa_residual_flash", _ptr(q), q.stride(0), _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["asg"]), _ptr(sel),
+              sel.shape[1], _ptr(exp_idx), exp_idx.shape[1], _ptr(st["Sk"]), _ptr(st["Sv"]), _ptr(nt), _ptr(quota),
+              _ptr(kbar), _ptr(vbar), _ptr(logn), _ptr(out), out.stride(0), code, float(sm_scale), _ptr(status),
+              _stream(K))
+
+
 def padded_len(Lmax: int) -> int:
     """Row length of the per-token score buffer: Lmax rounded up to 256 tokens."""
     return (Lmax + 255) // 256 * 256

@@ -17,6 +17,7 @@ import oracle as O
 from helpers import state_from_fixture, to_gpu_state, to_np
 from openattention_b200 import flash as F
 from openattention_b200 import method as Mth
+from openattention_b200 import selection as S
 from openattention_b200.geometry import HQ
 
 pytestmark = pytest.mark.gpu
@@ -81,6 +82,51 @@ def test_decode_steps_bit_exact(name, golden_dir):
         # and the method's own bf16 output is the rounding of that
         ob = m.attend(0, qr, sel, m.exp_idx, m.kbar, m.vbar, m.logn).float().cpu().numpy().reshape(R, D)
         assert np.abs(ob - ref).max() <= 2e-3 + np.abs(ref).max() * 2 ** -8
+
+
+@pytest.mark.parametrize("name", list(cases.DECODE_CASES))
+def test_fused_residual_flash(name, golden_dir):
+    """The fused residual + flash kernel: proxies bit-identical to the oracle's residual, output within
+    the stated tolerance of the fp64 estimator, bf16 output = rounding of the fp32 one (one ulp)."""
+    x = cases.decode_inputs(name)
+    z = np.load(os.path.join(golden_dir, f"{name}.npz"))
+    st_np, K, V = state_from_fixture(x, z)
+    B, n0, Lmax, rho = x["B"], x["n0"], x["Lmax"], x["rho"]
+    m = _method(B, Lmax, rho)
+    C, E, R = m.C, m.E, B * HQ
+    m.st[0] = to_gpu_state(st_np)
+    Mth.C.K, Mth.C.V = [x["K"].cuda()], [x["V"].cuda()]
+    Mth.C.n_dev = None
+    Mth.C.n0_dev = torch.tensor([n0], dtype=torch.int32, device="cuda")
+    n = n0 + 1
+    Mth.C.K[0][:, :, n - 1] = x["new_k"][0].cuda()
+    Mth.C.V[0][:, :, n - 1] = x["new_v"][0].cuda()
+    K[:, :, n - 1], V[:, :, n - 1] = O.bits(x["new_k"][0]), O.bits(x["new_v"][0])
+    q = x["qdec"][0]
+    qr, sel = m.select(0, q.cuda(), n, residual=False)
+    kb = torch.zeros_like(m.kbar)
+    vb = torch.zeros_like(m.vbar)
+    ln = torch.zeros_like(m.logn)
+    out32 = torch.empty(R, D, dtype=torch.float32, device="cuda")
+    S.residual_flash(qr, Mth.C.K[0], Mth.C.V[0], m.st[0], sel, m.exp_idx, m.nt, m.quota, out32, kbar=kb, vbar=vb,
+                     logn=ln, status=m.status)
+    out16 = torch.empty(R, D, dtype=torch.bfloat16, device="cuda")
+    S.residual_flash(qr, Mth.C.K[0], Mth.C.V[0], m.st[0], sel, m.exp_idx, m.nt, m.quota, out16, status=m.status)
+    torch.cuda.synchronize()
+    o = O.decode_step(st_np, O.bits(q.reshape(R, D)), K, V, n, rho, C, E)
+    _eq("exp_idx", m.exp_idx, o["exp_idx"])
+    _eq("fused.kbar", kb, o["kbar"])
+    _eq("fused.vbar", vb, o["vbar"])
+    _eq("fused.logn", ln, o["logn"])
+    ref = o["out"]
+    got = out32.cpu().double().numpy()
+    assert np.abs(got - ref).max() <= 2e-3
+    assert np.linalg.norm(got - ref) <= 1e-3 * np.linalg.norm(ref)
+    g16 = out16.float().cpu()
+    r16 = out32.cpu().to(torch.bfloat16).float()
+    ulp = torch.maximum(r16.abs(), torch.full_like(r16, 2.0 ** -126)) * 2.0 ** -7
+    assert bool(((g16 - r16).abs() <= ulp).all())
+    assert int(m.status.item()) == 0
 
 
 @pytest.mark.parametrize("name", list(cases.DECODE_CASES))
