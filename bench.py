@@ -264,7 +264,9 @@ def run_ours(a):
         dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
         pg = dist
     steps_total = a.warmup + 2 * a.steps + 8
-    m, Mth, qs, nks, nvs, n0, Lmax = build_workload(dev, seed=1000 * rank + 17, steps_total=steps_total)
+    from openattention_b200 import shard
+    # every rank runs its own B=32 requests (request sharding, shard.plan with batch = 32 * world)
+    m, Mth, qs, nks, nvs, n0, Lmax = build_workload(dev, seed=shard.request_seed(17, rank), steps_total=steps_total)
     gs = GraphStep(m, Mth, n0, dev)
     snap = {k: v.clone() for k, v in m.st[0].items()}
     n_snap, kv_snap = Mth.C.n_dev.clone(), Mth.C.kv_idx.clone()
@@ -285,11 +287,7 @@ def run_ours(a):
         torch.cuda.synchronize()
 
     def max_over_ranks(x):
-        if pg is None:
-            return x
-        t = torch.tensor([x], device=dev, dtype=torch.float64)
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-        return float(t.item())
+        return shard.max_over_ranks(x, device=dev)
 
     # ---- value: device-resident inputs (clocks sampled over warm-up and the timed region)
     clk = Clocks(dev).__enter__()
