@@ -75,6 +75,34 @@ int oa_flash_qhead_proxies(const void* q, int64_t q_stride, const void* k, const
  * nsplit = 0 is resolved the same way the entry points resolve it). */
 size_t oa_flash_workspace_bytes(int64_t BQ, int64_t n_sel, int64_t n_exp, int64_t NB, int nsplit);
 
+/* oa_flash_qhead_proxies for callers that cannot allocate device memory.  This entry point has no
+ * counterpart in the reference.
+ *
+ * Who needs it: a plugin that is handed only raw device pointers across a foreign-function
+ * boundary and has no allocator of its own; a serving host that has already given all device
+ * memory to its own pool, so cudaMalloc would fail; a decode loop that cannot let an allocation
+ * stall the device.  Such callers pass inputs and outputs only.  The split-K scratch (ticket
+ * counters and partial softmax states) lives in one fixed 4 MiB (4194304-byte) array inside the
+ * library, held by every GPU that loads the library until the process exits.
+ *
+ * Arguments and results are those of oa_flash_qhead_proxies without workspace/workspace_bytes.
+ * A call whose split needs more than 4 MiB (oa_flash_workspace_bytes(...) > 4194304) is rejected
+ * with status 1 and a message; pass a smaller nsplit, or use oa_flash_qhead_proxies.  The entry
+ * point calls no cudaMalloc, cudaFree or other allocating routine.
+ *
+ * Set-up: the first call on a device (with that device current) looks up the array's device
+ * address and keeps it; make that first call before any stream capture.  Every call clears the
+ * ticket counters on `stream` before its kernel.  All calls on one device share the one array, which
+ * keeps the last call's contents: calls that overlap on the GPU (other streams, other host threads)
+ * race on it and give wrong results, so order them (one stream, or events). */
+int oa_flash_qhead_proxies_noalloc(const void* q, int64_t q_stride, const void* k, const void* v,
+                                   int64_t kv_stride_h, int64_t kv_stride_t, const int32_t* sel, int64_t n_sel,
+                                   const int32_t* exp_idx, int64_t n_exp, const void* kbar, const void* vbar,
+                                   int64_t kbar_stride_h, int64_t kbar_stride_b, const float* log_n,
+                                   int64_t log_n_stride, void* out, int64_t out_stride, int out_dtype,
+                                   int64_t BQ, int64_t BH, int64_t K, int64_t NB, float sm_scale, int nsplit,
+                                   void* stream);
+
 /* ------------------------------------------------------------------------------------------------
  * Decode-step selection.  State layouts (all contiguous; B requests, C clusters, Lmax positions):
  *   K, V     (B, 8, Lmax, 128) bf16 caches, new token already written at position n-1

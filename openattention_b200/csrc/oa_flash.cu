@@ -15,6 +15,8 @@
 // (atomic ticket, no waiting) merges the row's partials in chunk order, so the result does not
 // depend on which CTA finishes last.
 #include "oa_common.cuh"
+
+#include <mutex>
 #include "../../include/openattention_b200.h"
 
 namespace oa {
@@ -358,4 +360,83 @@ extern "C" int oa_flash_qhead_proxies(const void* q, int64_t q_stride, const voi
   return oa::flash_entry(true, q, q_stride, k, v, kv_stride_h, kv_stride_t, sel, n_sel, exp_idx, n_exp, kbar,
                          vbar, kbar_stride_h, kbar_stride_b, log_n, log_n_stride, out, out_stride, out_dtype, BQ,
                          BH, K, NB, sm_scale, nsplit, workspace, workspace_bytes, stream);
+}
+
+// ------------------------------------------------------------------------------------------------
+// Split-K flash without caller-provided workspace.  Some callers cannot call cudaMalloc: a plugin
+// handed only raw device pointers across a foreign-function boundary (no allocator of its own), a
+// serving host that has already given all device memory to its own pool, or a decode loop that
+// must not let an allocation stall the device.  For them the split-K scratch (ticket counters and
+// the partial (m, l, acc) arrays) lives in one fixed file-scope array that every GPU loading this
+// library holds until the process exits.
+namespace oa {
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;  // 4 MiB per device
+constexpr int kNoAllocMaxDevices = 64;
+
+__device__ __align__(256) unsigned char g_flash_scratch[kNoAllocScratchBytes];
+
+std::mutex g_scratch_mu;
+void* g_scratch_ptr[kNoAllocMaxDevices] = {};
+
+// Device address of g_flash_scratch on the current device, looked up once per device (with that
+// device current) and kept for later calls.  Returns a status; *out is set on success.
+int scratch_on_current_device(const char* fn, void** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: cudaGetDevice failed: %s", fn, cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return oa_fail(OA_ERR_UNSUPPORTED, "%s: device ordinal %d is beyond the %d devices this entry point tracks", fn,
+                   dev, kNoAllocMaxDevices);
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_flash_scratch);
+    if (e != cudaSuccess || !p)
+      return oa_fail(OA_ERR_CUDA, "%s: cudaGetSymbolAddress of the scratch array failed on device %d: %s", fn, dev,
+                     cudaGetErrorString(e));
+    g_scratch_ptr[dev] = p;
+  }
+  *out = g_scratch_ptr[dev];
+  return OA_OK;
+}
+
+}  // namespace
+}  // namespace oa
+
+extern "C" int oa_flash_qhead_proxies_noalloc(const void* q, int64_t q_stride, const void* k, const void* v,
+                                              int64_t kv_stride_h, int64_t kv_stride_t, const int32_t* sel,
+                                              int64_t n_sel, const int32_t* exp_idx, int64_t n_exp,
+                                              const void* kbar, const void* vbar, int64_t kbar_stride_h,
+                                              int64_t kbar_stride_b, const float* log_n, int64_t log_n_stride,
+                                              void* out, int64_t out_stride, int out_dtype, int64_t BQ,
+                                              int64_t BH, int64_t K, int64_t NB, float sm_scale, int nsplit,
+                                              void* stream) {
+  const char* fn = "oa_flash_qhead_proxies_noalloc";
+  OA_REQUIRE(BQ > 0 && BQ <= 0x7fffffff && n_sel >= 0 && n_exp >= 0 && NB >= 0 &&
+                 n_sel + n_exp + NB < (int64_t)1 << 30,
+             "%s: bad sizes (BQ=%lld n_sel=%lld n_exp=%lld NB=%lld)", fn, (long long)BQ, (long long)n_sel,
+             (long long)n_exp, (long long)NB);
+  int chunk = 8;
+  const int ns = oa::resolve_split(BQ, n_sel + n_exp + NB, nsplit, &chunk);
+  const size_t need = oa::workspace_bytes(BQ, ns);
+  OA_REQUIRE(need <= oa::kNoAllocScratchBytes,
+             "%s: %d chunks for %lld rows need %zu bytes of scratch, above this entry point's fixed %zu bytes; "
+             "pass a smaller nsplit or use oa_flash_qhead_proxies with a workspace",
+             fn, ns, (long long)BQ, need, oa::kNoAllocScratchBytes);
+  void* scratch = nullptr;
+  if (need > 0) {
+    const int rc = oa::scratch_on_current_device(fn, &scratch);
+    if (rc != OA_OK) return rc;
+    // The ticket counters must start at zero; clear them rather than trust what an earlier call left.
+    const cudaError_t e =
+        cudaMemsetAsync(scratch, 0, (size_t)BQ * sizeof(unsigned), static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) {
+      return oa_fail(OA_ERR_CUDA, "%s: clearing the ticket counters failed: %s", fn, cudaGetErrorString(e));
+    }
+  }
+  return oa::flash_entry(true, q, q_stride, k, v, kv_stride_h, kv_stride_t, sel, n_sel, exp_idx, n_exp, kbar,
+                         vbar, kbar_stride_h, kbar_stride_b, log_n, log_n_stride, out, out_stride, out_dtype, BQ,
+                         BH, K, NB, sm_scale, nsplit, scratch, need, stream);
 }
