@@ -1,7 +1,7 @@
 #!/usr/bin/env python3
 """Decode-attention-stage benchmark of the OpenAttention deployed path on B200 (BASELINE config c2).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
 
 Workload per GPU: B=32 requests, 32K-token bf16 KV caches (seeded synthetic, see
 openattention_b200/synth.py), 1% read (C=64, E=216), ONE layer's decode step: index update + QGS
@@ -57,12 +57,14 @@ def peaks():
     return 6650.0, "fallback"
 
 
-def traffic_from_profiles():
-    """DRAM bytes per scan launch from the committed ncu summary (None when not captured yet)."""
+def traffic_from_profiles(kernel):
+    """DRAM bytes (read + write) per full-size launch of `kernel` from the committed ncu summary
+    profiles/roofline_traffic.json (None when that kernel has not been captured)."""
     p = os.path.join(ROOT, "profiles", "roofline_traffic.json")
     if os.path.exists(p):
         try:
-            return json.load(open(p)).get("qgs_scan_per_launch_bytes")
+            v = json.load(open(p)).get(kernel)
+            return v.get("bytes_per_launch") if isinstance(v, dict) else v
         except (ValueError, OSError):
             return None
     return None
@@ -199,23 +201,70 @@ class GraphStep:
         self.graph.replay()
 
 
-def time_scan(m, Mth, dev, iters):
-    """Average duration of the QGS scan kernel alone (CUDA events on its launch stream)."""
+def stage_profile(m, Mth, gs, iters):
+    """Each kernel of the step timed alone on the current stream: CUDA events around single launches,
+    L2 flushed (a 256 MB write) before each, mean over `iters`; with its algorithmic bytes per launch
+    (unique bytes the stage must move: inputs read once, outputs written once, no on-chip intermediates)."""
     from openattention_b200 import selection as S
-    from openattention_b200.geometry import step_split
+    from openattention_b200.geometry import D, HKV, HQ, step_split
+    st, B, C, E = m.st[0], m.B, m.C, m.E
+    R, Rkv = B * HQ, B * HKV
     n = int(Mth.C.n_dev.item())
-    ns, nl, _ = step_split(n, RHO, m.C, m.E)
-    st = m.st[0]
-    for _ in range(3):
-        S.qgs_scan(st["codes"], m.zq, Mth.C.n_dev, ns, nl, m.scores, m.tmax, m.status)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    for _ in range(iters):
-        S.qgs_scan(st["codes"], m.zq, Mth.C.n_dev, ns, nl, m.scores, m.tmax, m.status)
-    e1.record()
-    torch.cuda.synchronize()
-    return e0.elapsed_time(e1) / iters, n
+    ns, nl, k_top = step_split(gs.n_host, RHO, C, E)
+    NS = ns + nl + k_top
+    sel = m._sel_buf(NS)
+    K, V = Mth.C.K[0], Mth.C.V[0]
+    qr = gs.q_in.reshape(R, D)
+    n_dev, n0_dev = Mth.C.n_dev, Mth.C.n0_dev
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=K.device)
+    scores_snap = m.scores.clone()
+
+    def timed(fn, prep=None):
+        for _ in range(3):
+            if prep:
+                prep()
+            fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(iters):
+            if prep:
+                prep()
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            fn()
+            e1.record()
+            torch.cuda.synchronize()
+            tot += e0.elapsed_time(e1)
+        return tot / iters
+
+    ms = {
+        "qgs_scan_kernel": timed(lambda: S.qgs_scan(st["codes"], m.zq, n_dev, ns, nl, m.scores, m.tmax, m.status)),
+        "qgs_select_kernel": timed(lambda: S.qgs_select(m.scores, m.tmax, m.Lmax, n_dev, ns, nl, k_top, sel),
+                                   prep=lambda: m.scores.copy_(scores_snap)),
+        "errorgate_waterfill_kernel": timed(lambda: S.errorgate_waterfill(qr, K, st, sel, E, m.score, m.nt, m.quota,
+                                                                          m.status)),
+        "topq_kernel": timed(lambda: S.topq(m.scores, st, m.quota, E, n_dev, n0_dev, m.exp_idx, m.status)),
+        "residual_flash_kernel": timed(lambda: S.residual_flash(qr, K, V, st, sel, m.exp_idx, m.nt, m.quota, m.out,
+                                                                status=m.status)),
+    }
+    # data-dependent byte counts of this step
+    quota = m.quota.view(B, HQ, C)
+    members = int((st["clen"].float() * (quota > 0)).sum().item())
+    reads = int((m.exp_idx >= 0).sum().item()) + R * NS
+    nt_tiles = (n + 31) // 32
+    alg = {
+        "qgs_scan_kernel": Rkv * n * 32,
+        "qgs_select_kernel": R * (nt_tiles * 4 + NS * 4),
+        "errorgate_waterfill_kernel": R * (2 * C * D * 4 + C * 4 + NS * (D * 2 + 4) + D * 2 + 3 * C * 4),
+        "topq_kernel": members * 6 + R * (2 * C * 4 + E * 4),
+        "residual_flash_kernel": reads * 2 * D * 2 + R * (2 * C * D * 4 + 2 * C * 4 + (NS + E) * 4 + 2 * D * 2),
+    }
+    # the whole step's algorithmic bytes: codes, the three fp32 sum arrays once, the read rows, the small
+    # per-row arrays, the index-update operands and the chosen clusters' member lists
+    step_alg = (Rkv * n * 32 + 3 * R * C * D * 4 + reads * 2 * D * 2 + R * C * 4 + R * (NS + E) * 4 + 2 * R * D * 2
+                + R * (D * 16 * 2 + C * 16 * 4) + Rkv * D * 32 * 4 + members * 6)
+    return ms, alg, step_alg, n
 
 
 def cpu_baseline_sample(m, Mth, qs, nks, nvs, budget_s=12.0):
@@ -340,12 +389,16 @@ def run_ours(a):
     ms_e2e = max_over_ranks(f0.elapsed_time(f1) / a.steps)
     h2d = (qs[0].numel() + nks[0].numel() + nvs[0].numel()) * 2
     d2h = gs.out.numel() * 2
-    # ---- roofline of the dominant kernel (QGS scan), timed alone
-    scan_ms, n_now = time_scan(m, Mth, dev, max(10, a.steps))
-    scan_ms = max_over_ranks(scan_ms)
-    alg_bytes = B_PER_GPU * 8 * n_now * SCAN_BYTES_PER_TOKEN
+    # ---- every kernel of the step timed alone; roofline of the dominant one
+    st_ms, st_alg, step_alg, n_now = stage_profile(m, Mth, gs, max(10, min(a.steps, 50)))
+    st_ms = {k: max_over_ranks(v) for k, v in st_ms.items()}
     peak, peak_kind = peaks()
-    achieved = alg_bytes / (scan_ms * 1e-3) / 1e9
+    dom = max(st_ms, key=st_ms.get)
+    achieved = st_alg[dom] / (st_ms[dom] * 1e-3) / 1e9
+    stages = {k: {"us": round(st_ms[k] * 1e3, 2), "alg_bytes": st_alg[k],
+                  "gbs": round(st_alg[k] / (st_ms[k] * 1e-3) / 1e9, 1),
+                  "frac": round(st_alg[k] / (st_ms[k] * 1e-3) / 1e9 / peak, 4)} for k in st_ms}
+    step_gbs = step_alg / (ms * 1e-3 * 1.0) / 1e9
     res = None
     if rank == 0:
         cpu = cpu_baseline_sample(m, Mth, qs, nks, nvs) if world == 1 else None
@@ -361,10 +414,13 @@ def run_ours(a):
             "e2e": {"value": round(ms_e2e * 1e3 / world, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": LAUNCHES_PER_STEP * a.steps,
-            "roofline": {"kernel": "qgs_scan_kernel", "bound": "hbm", "achieved": round(achieved, 1),
-                         "peak": peak, "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": traffic_from_profiles(), "alg_bytes_per_launch": alg_bytes,
-                         "launch_us": round(scan_ms * 1e3, 3)},
+            "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": traffic_from_profiles(dom), "alg_bytes_per_launch": st_alg[dom],
+                         "launch_us": round(st_ms[dom] * 1e3, 3)},
+            "stages": stages,
+            "step_roofline": {"alg_bytes": step_alg, "achieved": round(step_gbs, 1), "unit": "GB/s",
+                              "frac": round(step_gbs / peak, 4), "n": n_now},
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
             "stage_us_per_step_per_gpu": round(ms * 1e3, 3),
@@ -434,12 +490,16 @@ def run_reference(a):
 
 
 def main():
+    global B_PER_GPU
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--batch", type=int, default=B_PER_GPU,
+                    help="requests per GPU (default 32, the benchmark config; smaller only for profiling)")
     a = ap.parse_args()
+    B_PER_GPU = a.batch
     if a.warmup < 3:
         a.warmup = 3
     res = run_reference(a) if a.impl == "reference" else run_ours(a)

@@ -704,6 +704,308 @@ __global__ void __launch_bounds__(kRW * 32, 2) residual_kernel(const ResidArgs a
   }
 }
 
+
+// ------------------------------------------------------------------------------------------------
+// Residual proxies folded into the flash pass (no proxy tensors kept).  For a live cluster c
+// (n'_c = nt_c - q_c > 0.5) with read set R_c (its selected and expanded tokens):
+//   q.kbar'_c = (q.Sk_c - sum_{t in R_c} q.k_t) / max(n'_c, 1)
+// so the proxy logit needs only the SCALAR q.dk_c, a sum of the token dots the flash computes
+// anyway; and with w_c = p_c / max(n'_c, 1) the value side is
+//   sum_t p_t v_t + sum_c p_c vbar'_c = sum_t (p_t - w_c(t)) v_t + sum_c w_c Sv_c.
+// Pass A gathers K rows and Sk rows (token and proxy logits), pass B gathers V rows and Sv rows
+// with the final weights.  No per-cluster vector sums are held, so a CTA is 4 warps with a few KB
+// of shared memory and every load of a pass can be in flight at once.  The proxies are the fp32
+// estimator's (kbar' = (Sk - dk)/n' unrounded); the bf16-rounded proxies of the reference's
+// _k_resid_norm (ours_fused.py:388-407) are produced by residual_kernel when they are requested.
+constexpr int kPF = 128;      // threads per CTA
+constexpr int kPFHalf = kPF / 16;
+constexpr int kPFU = 8;       // rows a half-warp has in flight
+
+struct PFShared {
+  int* tok;      // [NT] token position or -1
+  int16_t* cl;   // [NT] cluster of the token or -1
+  float* z;      // [NT] q.k dot, then the pass-B coefficient
+  int* base;     // [C + 1] exclusive prefix of the quotas
+  float* qsk;    // [C] q.Sk_c (live clusters)
+  float* w;      // [C] proxy weight / max(n', 1), 0 when not live
+  float* zc;     // [C] proxy logit (log2 domain) or -inf
+  float* inv;    // [C]
+};
+
+__device__ __forceinline__ float hw_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 8);
+  x += __shfl_xor_sync(0xffffffffu, x, 4);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  return x;
+}
+
+__device__ __forceinline__ float dot8(const float* q, const uint4& w) {
+  float d = q[0] * bf_lo(w.x);
+  d = fmaf(q[1], bf_hi(w.x), d);
+  d = fmaf(q[2], bf_lo(w.y), d);
+  d = fmaf(q[3], bf_hi(w.y), d);
+  d = fmaf(q[4], bf_lo(w.z), d);
+  d = fmaf(q[5], bf_hi(w.z), d);
+  d = fmaf(q[6], bf_lo(w.w), d);
+  d = fmaf(q[7], bf_hi(w.w), d);
+  return d;
+}
+
+__device__ __forceinline__ float dot8f(const float* q, const float4& a, const float4& b) {
+  float d = q[0] * a.x;
+  d = fmaf(q[1], a.y, d);
+  d = fmaf(q[2], a.z, d);
+  d = fmaf(q[3], a.w, d);
+  d = fmaf(q[4], b.x, d);
+  d = fmaf(q[5], b.y, d);
+  d = fmaf(q[6], b.z, d);
+  d = fmaf(q[7], b.w, d);
+  return d;
+}
+
+__device__ __forceinline__ float block_reduce_pf(float v, bool is_max, float* s_red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const float o = __shfl_xor_sync(0xffffffffu, v, off);
+    v = is_max ? fmaxf(v, o) : v + o;
+  }
+  __syncthreads();
+  if (lane == 0) s_red[warp] = v;
+  __syncthreads();
+  float r = s_red[0];
+#pragma unroll
+  for (int i = 1; i < kPF / 32; ++i) r = is_max ? fmaxf(r, s_red[i]) : r + s_red[i];
+  return r;
+}
+
+__global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) {
+  extern __shared__ __align__(16) unsigned char pf_smem[];
+  const int r = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int hw = tid >> 4, hl = tid & 15;
+  const int kv = r / kG;
+  const int C = a.C, NS = a.NS, NT = a.NS + a.E;
+  __shared__ float s_red[kPF / 32];
+  __shared__ __align__(16) float s_acc[kPFHalf][kD];
+  PFShared S;
+  {
+    unsigned char* p = pf_smem;
+    S.z = reinterpret_cast<float*>(p);
+    p += sizeof(float) * ((NT + 3) & ~3);
+    S.qsk = reinterpret_cast<float*>(p);
+    p += sizeof(float) * ((C + 3) & ~3);
+    S.w = reinterpret_cast<float*>(p);
+    p += sizeof(float) * ((C + 3) & ~3);
+    S.zc = reinterpret_cast<float*>(p);
+    p += sizeof(float) * ((C + 3) & ~3);
+    S.inv = reinterpret_cast<float*>(p);
+    p += sizeof(float) * ((C + 3) & ~3);
+    S.tok = reinterpret_cast<int*>(p);
+    p += sizeof(int) * ((NT + 3) & ~3);
+    S.base = reinterpret_cast<int*>(p);
+    p += sizeof(int) * ((C + 4) & ~3);
+    S.cl = reinterpret_cast<int16_t*>(p);
+  }
+  const int64_t rowC = (int64_t)r * C;
+  // ---- row metadata: quotas (prefix), tokens, clusters of the selected tokens
+  for (int c = tid; c < C; c += kPF) S.w[c] = a.quota[rowC + c];  // staged quota (w is free until later)
+  for (int j = tid; j < NT; j += kPF) {
+    const int t = j < NS ? a.sel[(int64_t)r * NS + j] : a.exp[(int64_t)r * a.E + (j - NS)];
+    const bool v = t >= 0 && t < a.Lmax;
+    S.tok[j] = v ? t : -1;
+    if (j < NS) S.cl[j] = v ? (int16_t)a.asg[(int64_t)r * a.Lmax + t] : (int16_t)-1;
+  }
+  float qv[8];
+  {
+    const uint4 qw = *reinterpret_cast<const uint4*>(a.q + (int64_t)r * a.q_stride + hl * 8);
+    qv[0] = bf_lo(qw.x); qv[1] = bf_hi(qw.x); qv[2] = bf_lo(qw.y); qv[3] = bf_hi(qw.y);
+    qv[4] = bf_lo(qw.z); qv[5] = bf_hi(qw.z); qv[6] = bf_lo(qw.w); qv[7] = bf_hi(qw.w);
+  }
+  __syncthreads();
+  if (warp == 0) {  // exclusive prefix of the quotas, lanes own consecutive runs of clusters
+    const int per = (C + 31) / 32;
+    const int c0 = lane * per, c1 = min(C, c0 + per);
+    int run = 0;
+    for (int c = c0; c < c1; ++c) run += (int)S.w[c];
+    int incl = run;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int o = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += o;
+    }
+    int ex = incl - run;
+    for (int c = c0; c < c1; ++c) {
+      S.base[c] = ex;
+      ex += (int)S.w[c];
+    }
+    if (lane == 31) S.base[C] = incl;
+  }
+  __syncthreads();
+  for (int j = NS + tid; j < NT; j += kPF) {  // expanded slot -> its cluster segment
+    const int slot = j - NS;
+    int c = -1;
+    if (S.tok[j] >= 0 && slot < S.base[C]) {
+      int lo = 0, hi = C;  // largest c with base[c] <= slot
+      while (hi - lo > 1) {
+        const int mid = (lo + hi) >> 1;
+        if (S.base[mid] <= slot) lo = mid; else hi = mid;
+      }
+      c = lo;
+    }
+    S.cl[j] = (int16_t)c;
+  }
+  for (int c = tid; c < C; c += kPF) {
+    const float nr = __fsub_rn(a.nt[rowC + c], S.w[c]);
+    S.inv[c] = nr > 0.5f ? __fdiv_rn(1.f, fmaxf(nr, 1.f)) : 0.f;
+    S.zc[c] = nr > 0.5f ? ln_f(fmaxf(nr, 1.f)) * kLog2e : -INFINITY;  // ln n' term, completed below
+  }
+  __syncthreads();
+  const __nv_bfloat16* Kr = a.K + (int64_t)kv * a.Lmax * kD + hl * 8;
+  const __nv_bfloat16* Vr = a.V + (int64_t)kv * a.Lmax * kD + hl * 8;
+  // ---- pass A: token dots (K rows) and q.Sk for live clusters
+  for (int j0 = hw; j0 < NT; j0 += kPFHalf * kPFU) {
+    uint4 kw[kPFU];
+#pragma unroll
+    for (int u = 0; u < kPFU; ++u) {
+      const int j = j0 + u * kPFHalf;
+      const int t = j < NT ? S.tok[j] : -1;
+      kw[u] = t >= 0 ? ldg_stream(reinterpret_cast<const uint4*>(Kr + (int64_t)t * kD)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kPFU; ++u) {
+      const int j = j0 + u * kPFHalf;
+      const float d = hw_sum(dot8(qv, kw[u]));
+      if (hl == 0 && j < NT) S.z[j] = d;
+    }
+  }
+  const float* Skr = a.Sk + rowC * kD + hl * 8;
+  for (int c0 = hw; c0 < C; c0 += kPFHalf * 4) {
+    float4 x[4], y[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + u * kPFHalf;
+      const bool live = c < C && S.inv[c] > 0.f;
+      x[u] = live ? __ldg(reinterpret_cast<const float4*>(Skr + (int64_t)c * kD)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      y[u] = live ? __ldg(reinterpret_cast<const float4*>(Skr + (int64_t)c * kD + 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + u * kPFHalf;
+      const float d = hw_sum(dot8f(qv, x[u], y[u]));
+      if (hl == 0 && c < C) S.qsk[c] = d;
+    }
+  }
+  __syncthreads();
+  // ---- proxy logits: q.dk_c summed over the cluster's read tokens in a fixed order
+  for (int c = warp; c < C; c += kPF / 32) {
+    if (!(S.inv[c] > 0.f)) continue;  // warp-uniform
+    float part = 0.f;
+    for (int j = lane; j < NS; j += 32)
+      if (S.cl[j] == c) part += S.z[j];
+    const int e0 = NS + S.base[c], e1 = NS + min(S.base[c + 1], a.E);
+    for (int j = e0 + lane; j < e1; j += 32)
+      if (S.tok[j] >= 0) part += S.z[j];
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+    if (lane == 0) S.zc[c] = fmaf(__fmul_rn(__fsub_rn(S.qsk[c], part), S.inv[c]), a.qk_scale, S.zc[c]);
+  }
+  __syncthreads();
+  // ---- softmax normaliser: max over token and proxy logits, then weights
+  float mx = -INFINITY;
+  for (int j = tid; j < NT; j += kPF)
+    if (S.tok[j] >= 0) mx = fmaxf(mx, S.z[j] * a.qk_scale);
+  for (int c = tid; c < C; c += kPF) mx = fmaxf(mx, S.zc[c]);
+  const float M = block_reduce_pf(mx, true, s_red);
+  float lsum = 0.f;
+  for (int c = tid; c < C; c += kPF) {
+    const float p = S.zc[c] > -INFINITY ? exp2f(S.zc[c] - M) : 0.f;
+    lsum += p;
+    S.w[c] = __fmul_rn(p, S.inv[c]);
+  }
+  __syncthreads();  // w complete before the token coefficients read it
+  for (int j = tid; j < NT; j += kPF) {
+    float coef = 0.f;
+    if (S.tok[j] >= 0) {
+      const float p = exp2f(S.z[j] * a.qk_scale - M);
+      lsum += p;
+      const int c = S.cl[j];
+      coef = c >= 0 ? __fsub_rn(p, S.w[c]) : p;
+    }
+    S.z[j] = coef;
+  }
+  const float L = block_reduce_pf(lsum, false, s_red);  // its barriers also publish z and w
+  // ---- pass B: V rows with the coefficients, Sv rows with the proxy weights
+  float acc[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+  for (int j0 = hw; j0 < NT; j0 += kPFHalf * kPFU) {
+    uint4 vw[kPFU];
+#pragma unroll
+    for (int u = 0; u < kPFU; ++u) {
+      const int j = j0 + u * kPFHalf;
+      const int t = j < NT ? S.tok[j] : -1;
+      vw[u] = t >= 0 ? ldg_stream(reinterpret_cast<const uint4*>(Vr + (int64_t)t * kD)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < kPFU; ++u) {
+      const int j = j0 + u * kPFHalf;
+      const float cf = j < NT ? S.z[j] : 0.f;
+      acc[0] = fmaf(cf, bf_lo(vw[u].x), acc[0]);
+      acc[1] = fmaf(cf, bf_hi(vw[u].x), acc[1]);
+      acc[2] = fmaf(cf, bf_lo(vw[u].y), acc[2]);
+      acc[3] = fmaf(cf, bf_hi(vw[u].y), acc[3]);
+      acc[4] = fmaf(cf, bf_lo(vw[u].z), acc[4]);
+      acc[5] = fmaf(cf, bf_hi(vw[u].z), acc[5]);
+      acc[6] = fmaf(cf, bf_lo(vw[u].w), acc[6]);
+      acc[7] = fmaf(cf, bf_hi(vw[u].w), acc[7]);
+    }
+  }
+  const float* Svr = a.Sv + rowC * kD + hl * 8;
+  for (int c0 = hw; c0 < C; c0 += kPFHalf * 4) {
+    float4 x[4], y[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + u * kPFHalf;
+      const bool use = c < C && S.w[c] != 0.f;
+      x[u] = use ? __ldg(reinterpret_cast<const float4*>(Svr + (int64_t)c * kD)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      y[u] = use ? __ldg(reinterpret_cast<const float4*>(Svr + (int64_t)c * kD + 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int c = c0 + u * kPFHalf;
+      const float wc = c < C ? S.w[c] : 0.f;
+      acc[0] = fmaf(wc, x[u].x, acc[0]);
+      acc[1] = fmaf(wc, x[u].y, acc[1]);
+      acc[2] = fmaf(wc, x[u].z, acc[2]);
+      acc[3] = fmaf(wc, x[u].w, acc[3]);
+      acc[4] = fmaf(wc, y[u].x, acc[4]);
+      acc[5] = fmaf(wc, y[u].y, acc[5]);
+      acc[6] = fmaf(wc, y[u].z, acc[6]);
+      acc[7] = fmaf(wc, y[u].w, acc[7]);
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s_acc[hw][hl * 8 + i] = acc[i];
+  __syncthreads();
+  if (tid < kD) {
+    float A = 0.f;
+#pragma unroll
+    for (int h = 0; h < kPFHalf; ++h) A += s_acc[h][tid];
+    const float o = L > 0.f ? A / L : 0.f;
+    if (a.out_f32)
+      reinterpret_cast<float*>(a.out)[(int64_t)r * a.out_stride + tid] = o;
+    else
+      reinterpret_cast<__nv_bfloat16*>(a.out)[(int64_t)r * a.out_stride + tid] = __float2bfloat16_rn(o);
+  }
+}
+
+size_t proxy_flash_smem(int NT, int C) {
+  return sizeof(float) * ((NT + 3) & ~3) + 4 * sizeof(float) * ((C + 3) & ~3) + sizeof(int) * ((NT + 3) & ~3) +
+         sizeof(int) * ((C + 4) & ~3) + sizeof(int16_t) * ((NT + 7) & ~7);
+}
+
 }  // namespace
 }  // namespace oa
 
@@ -779,6 +1081,13 @@ extern "C" int oa_residual_flash(const void* q, int64_t q_stride, const void* K,
               static_cast<const __nv_bfloat16*>(V), (int)Lmax, (int)C, (int)n_sel, (int)E, asg, sel, exp_idx, Sk, Sv,
               nt, quota, static_cast<__nv_bfloat16*>(kbar), static_cast<__nv_bfloat16*>(vbar), logn, out,
               out_stride, out_dtype == OA_F32 ? 1 : 0, sm_scale * kLog2e, status};
-  residual_kernel<true><<<(unsigned)(B * kHQ), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  if (kbar == nullptr && logn == nullptr) {
+    OA_REQUIRE(oa_aligned16(q) && q_stride % 8 == 0, "%s: q rows must be 16-byte aligned", fn);
+    OA_REQUIRE(oa_aligned16(Sk) && oa_aligned16(Sv), "%s: Sk / Sv must be 16-byte aligned", fn);
+    const size_t smem = proxy_flash_smem((int)(n_sel + E), (int)C);
+    proxy_flash_kernel<<<(unsigned)(B * kHQ), kPF, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  } else {
+    residual_kernel<true><<<(unsigned)(B * kHQ), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  }
   return oa_check_launch(fn);
 }

@@ -191,6 +191,36 @@ def estimator_fp32(q, k, v, sel, exp_idx, Skr, Svr, nr, sm_scale=SC):
     return out
 
 
+def residual_sums(K, V, asg, sel, exp_idx, Sk, Sv, nt, quota):
+    """Unrounded residual sums in float64 (the inputs of estimator_fp32): Skr = Sk - the read tokens'
+    k summed per cluster (selected tokens by their assignment, expanded tokens by the quota segment
+    their slot falls in; pads skipped), Svr likewise, nr = nt - quota.  Same read sets as
+    oro_residual (ours_fused.py:367-407)."""
+    R, C, _ = Sk.shape
+    B, _, Lmax, _ = K.shape
+    Kf = K.reshape(B * HKV, Lmax, D)
+    Vf = V.reshape(B * HKV, Lmax, D)
+    Skr = Sk.astype(np.float64).copy()
+    Svr = Sv.astype(np.float64).copy()
+    for r in range(R):
+        kv = r // (HQ // HKV)
+        base = np.concatenate([[0], np.cumsum(quota[r].astype(np.int64))])
+        toks, cls = [], []
+        for t in sel[r]:
+            if 0 <= t < Lmax:
+                toks.append(t)
+                cls.append(asg[r, t])
+        for j, t in enumerate(exp_idx[r]):
+            if 0 <= t < Lmax and j < base[C]:
+                toks.append(t)
+                cls.append(int(np.searchsorted(base, j, side="right") - 1))
+        if toks:
+            toks, cls = np.array(toks), np.array(cls)
+            np.subtract.at(Skr[r], cls, bf16_to_f32(Kf[kv, toks]).astype(np.float64))
+            np.subtract.at(Svr[r], cls, bf16_to_f32(Vf[kv, toks]).astype(np.float64))
+    return Skr, Svr, (nt.astype(np.float64) - quota.astype(np.float64))
+
+
 # ------------------------------------------------------------------ build stages (one request)
 def build_codes(K1, U1, T):
     """K1 uint16 (8, Lmax, D), U1 (8, D, 32) -> scale (8, 32), codes (8, Lmax, 32) (first T rows)."""
