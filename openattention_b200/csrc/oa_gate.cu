@@ -266,8 +266,82 @@ struct TopqArgs {
 };
 
 __device__ __forceinline__ uint32_t ukey16(uint32_t b) { return (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u); }
+// ukey16 of both 16-bit halves of a word
+__device__ __forceinline__ uint32_t ukey16x2(uint32_t x) {
+  return x ^ ((((x >> 15) & 0x10001u) * 0xffffu) | 0x80008000u);
+}
 
-__global__ void __launch_bounds__(kTqThreads, 2) topq_kernel(const TopqArgs a) {
+// Register path of top-q for one cluster (one warp): NC member slots per lane, filled with 16-byte
+// loads of the member list (lane l holds list words 128 j + 4 l + e, j < NC / 4, relative to the
+// 16-byte boundary at or below the list start), plus two slots for generated tokens (up to 64).  Each slot
+// holds (ukey16 << 16) | (0xffff - list index), so the maximum is the best score with ties to the
+// lower list index (= lower position).  Every lane keeps its own maximum; a round takes the warp
+// maximum and only the owning lane rescans its slots.
+template <int NC>
+__device__ __forceinline__ void topq_regs(const TopqArgs& a, int r, int64_t rc, const int32_t* mp, int nmem,
+                                          const int32_t* rec, int ngen, int q, const uint16_t* keys,
+                                          int32_t* out, int lane) {
+  const uintptr_t addr = reinterpret_cast<uintptr_t>(mp);
+  const int o = (int)((addr & 15u) >> 2);  // list words before the start inside the first vector
+  const int32_t* a0 = mp - o;
+  const int32_t* row_end = a.mem + (int64_t)gridDim.x * a.Lmax;
+  uint32_t v[NC + 2];
+#pragma unroll
+  for (int j = 0; j < NC / 4; ++j) {
+    const int w = 128 * j + 4 * lane;  // word offset from a0
+    const int32_t* p = a0 + w;
+    int4 x = make_int4(-1, -1, -1, -1);
+    if (w - o < nmem) {
+      if (p + 4 <= row_end) {
+        x = __ldg(reinterpret_cast<const int4*>(p));
+      } else {
+        x.x = p + 0 < row_end ? p[0] : -1;
+        x.y = p + 1 < row_end ? p[1] : -1;
+        x.z = p + 2 < row_end ? p[2] : -1;
+        x.w = p + 3 < row_end ? p[3] : -1;
+      }
+    }
+    const int t[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int idx = w + e - o;
+      v[4 * j + e] = (idx >= 0 && idx < nmem) ? (ukey16(keys[t[e]]) << 16) | (uint32_t)(0xffff - idx) : 0u;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int gi = lane + 32 * g;
+    v[NC + g] = gi < ngen ? (ukey16(keys[rec[gi]]) << 16) | (uint32_t)(0xffff - (nmem + gi)) : 0u;
+  }
+  uint32_t lm = 0u;
+#pragma unroll
+  for (int i = 0; i < NC + 2; ++i) lm = max(lm, v[i]);
+  int my_idx = 0x7fffffff;  // list index of the winner this lane records (lane k <-> k-th winner)
+  for (int k = 0; k < q; ++k) {
+    uint32_t wm = lm;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) wm = max(wm, __shfl_xor_sync(0xffffffffu, wm, off));
+    if (wm == 0u) break;
+    if (lm == wm) {  // the unique owner drops it and rescans
+      uint32_t nm = 0u;
+#pragma unroll
+      for (int i = 0; i < NC + 2; ++i) {
+        v[i] = v[i] == wm ? 0u : v[i];
+        nm = max(nm, v[i]);
+      }
+      lm = nm;
+    }
+    if (lane == k) my_idx = 0xffff - (int)(wm & 0xffffu);
+  }
+  int rank = 0;
+  for (int j = 0; j < q; ++j) {
+    const int oth = __shfl_sync(0xffffffffu, my_idx, j);
+    rank += (oth < my_idx) ? 1 : 0;
+  }
+  if (lane < q && my_idx != 0x7fffffff) out[rank] = my_idx < nmem ? mp[my_idx] : rec[my_idx - nmem];
+}
+
+__global__ void __launch_bounds__(kTqThreads, 3) topq_kernel(const TopqArgs a) {
   extern __shared__ __align__(128) uint16_t s_spill[];  // the row's scores (when a.smem_keys)
   __shared__ __align__(8) uint64_t mbar;
   __shared__ int s_base[kMaxC + 1];
@@ -326,43 +400,14 @@ __global__ void __launch_bounds__(kTqThreads, 2) topq_kernel(const TopqArgs a) {
     const bool use_list = a.reclist != nullptr && cnt <= a.rmax;
     const int32_t* rec = use_list ? a.reclist + rc * a.rmax : nullptr;
     const int ngen = use_list ? cnt : 0;
-    if (use_list && q <= kSmallQ && nmem + ngen <= 32 * kRegCand) {
-      // ---- register path
-      const int m = nmem + ngen;
-      uint32_t v[kRegCand];
-#pragma unroll
-      for (int i = 0; i < kRegCand; ++i) {
-        const int idx = i * 32 + lane;
-        v[i] = idx < nmem ? (uint32_t)mp[idx] : (idx < m ? (uint32_t)rec[idx - nmem] : 0xffffffffu);
-      }
-#pragma unroll
-      for (int i = 0; i < kRegCand; ++i) {
-        const int idx = i * 32 + lane;
-        v[i] = v[i] == 0xffffffffu ? 0u : (ukey16(keys[v[i]]) << 16) | (uint32_t)(0xffff - idx);
-      }
-      int my_idx = 0x7fffffff;  // list index of the winner this lane records (lane k <-> k-th winner)
-      for (int k = 0; k < q; ++k) {
-        uint32_t lm = 0u;
-#pragma unroll
-        for (int i = 0; i < kRegCand; ++i) lm = max(lm, v[i]);
-        uint32_t wm = lm;
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) wm = max(wm, __shfl_xor_sync(0xffffffffu, wm, off));
-        if (wm == 0u) break;
-        if (lm == wm) {  // unique owner (list indices are unique)
-#pragma unroll
-          for (int i = 0; i < kRegCand; ++i)
-            if (v[i] == wm) v[i] = 0u;
-        }
-        if (lane == k) my_idx = 0xffff - (int)(wm & 0xffffu);
-      }
-      // winners in position order: rank of my_idx among the q recorded indices
-      int rank = 0;
-      for (int j = 0; j < q; ++j) {
-        const int o = __shfl_sync(0xffffffffu, my_idx, j);
-        rank += (o < my_idx) ? 1 : 0;
-      }
-      if (lane < q && my_idx != 0x7fffffff) out[base + rank] = my_idx < nmem ? mp[my_idx] : rec[my_idx - nmem];
+    if (use_list && q <= kSmallQ && ngen <= 64 && nmem + 3 <= 32 * kRegCand) {
+      const int span = nmem + 3;
+      if (span <= 256)
+        topq_regs<8>(a, r, rc, mp, nmem, rec, ngen, q, keys, out + base, lane);
+      else if (span <= 512)
+        topq_regs<16>(a, r, rc, mp, nmem, rec, ngen, q, keys, out + base, lane);
+      else
+        topq_regs<32>(a, r, rc, mp, nmem, rec, ngen, q, keys, out + base, lane);
       continue;
     }
     // ---- radix path: candidates enumerated in order (members, then generated tokens)
@@ -459,6 +504,354 @@ __global__ void __launch_bounds__(kTqThreads, 2) topq_kernel(const TopqArgs a) {
     });
     __syncwarp();
   }
+}
+
+// ------------------------------------------------------------------------ top-q, streamed member keys
+// Persistent variant of top-q for rows that fit in shared memory (about 49K positions): one CTA of
+// 16 warps per SM walks rows r = blockIdx.x, + gridDim.x, ...  Per row:
+//   phase 1: the whole CSR member list of the row is streamed with 16-byte loads (every thread has
+//            several in flight) and turned into a contiguous array of 16-bit score keys in CSR order
+//            (the score row itself was staged by a bulk copy); keys of generated positions [n0, n)
+//            are staged too;
+//   phase 2: warps take the clusters with q > 0 and select from contiguous shared-memory keys
+//            (register path: (key, list index) words, q rounds of warp maximum; radix path as in
+//            topq_kernel); winners are recorded in shared memory as CSR slots (or positions of
+//            generated tokens) and turned into positions by one parallel pass over the row.
+// While phase 2 runs, the next row's score row is already being copied into the freed buffer.
+constexpr int kTsThreads = 512;
+constexpr int kTsWarps = kTsThreads / 32;
+constexpr int kTsGenCap = 4096;  // generated positions whose keys are staged
+constexpr int kTsU = 16;         // 16-byte member vectors a thread has in flight in phase 1
+
+struct TsRow {
+  const uint16_t* key;   // member keys of the row, CSR order (key[i] = member i; key - mo is 8-byte aligned)
+  const uint16_t* gkey;  // keys of positions n0 .. n0 + gcount - 1
+  const uint16_t* sr;    // the row's score bits in global memory
+  const int32_t* mrow;   // the row's member list in global memory
+  int n0, nsp, gcount, mo;
+};
+
+__device__ __forceinline__ uint32_t ts_key_at(const TsRow& w, int t) {
+  if (t < 0 || t >= w.nsp) return 0u;
+  if (t >= w.n0 && t - w.n0 < w.gcount) return w.gkey[t - w.n0];
+  return ukey16(w.sr[t]);
+}
+
+// Winner encodings in the row's shared-memory list: a CSR slot (>= 0) of a member, or -(position+1)
+// of a generated token.
+__device__ __forceinline__ int ts_enc(int idx, int cs, int nmem, const int32_t* rec) {
+  return idx < nmem ? cs + idx : -(rec[idx - nmem] + 1);
+}
+
+template <int NC>
+__device__ __forceinline__ void topq_keys_regs(const TsRow& w, int cs, int nmem, const int32_t* rec, int ngen,
+                                               int q, int* win, int lim, int lane) {
+  const int o = (cs + w.mo) & 3, a0 = cs - o;  // w.key + a0 is 8-byte aligned
+  uint32_t v[NC + 2];
+#pragma unroll
+  for (int j = 0; j < NC / 4; ++j) {
+    const int wd = 128 * j + 4 * lane;
+    const uint2 x = *reinterpret_cast<const uint2*>(w.key + a0 + wd);
+    const uint32_t k4[4] = {x.x & 0xffffu, x.x >> 16, x.y & 0xffffu, x.y >> 16};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int idx = wd + e - o;
+      v[4 * j + e] = (idx >= 0 && idx < nmem) ? (k4[e] << 16) | (uint32_t)(0xffff - idx) : 0u;
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < 2; ++g) {
+    const int gi = lane + 32 * g;
+    v[NC + g] = gi < ngen ? (ts_key_at(w, rec[gi]) << 16) | (uint32_t)(0xffff - (nmem + gi)) : 0u;
+  }
+  // lane-local best two; a lane gives up its values in decreasing order, so the values it still holds
+  // are exactly those below the last one it gave up (words are unique)
+  uint32_t m1 = 0u, m2 = 0u;
+#pragma unroll
+  for (int i = 0; i < NC + 2; ++i) {
+    m2 = max(m2, min(m1, v[i]));
+    m1 = max(m1, v[i]);
+  }
+  bool have2 = true;  // m2 is this lane's second best
+  int my_idx = 0x7fffffff;
+  for (int k = 0; k < q; ++k) {
+    const uint32_t wm = __reduce_max_sync(0xffffffffu, m1);
+    if (wm == 0u) break;
+    if (m1 == wm) {  // the unique owner
+      if (have2) {
+        m1 = m2;
+        have2 = false;
+      } else {  // rescan below the value just taken
+        m1 = 0u;
+        m2 = 0u;
+#pragma unroll
+        for (int i = 0; i < NC + 2; ++i) {
+          const uint32_t c = v[i] < wm ? v[i] : 0u;
+          m2 = max(m2, min(m1, c));
+          m1 = max(m1, c);
+        }
+        have2 = true;
+      }
+    }
+    if (lane == k) my_idx = 0xffff - (int)(wm & 0xffffu);
+  }
+  int rank = 0;
+  for (int j = 0; j < q; ++j) {
+    const int oth = __shfl_sync(0xffffffffu, my_idx, j);
+    rank += (oth < my_idx) ? 1 : 0;
+  }
+  if (lane < q && my_idx != 0x7fffffff && rank < lim) win[rank] = ts_enc(my_idx, cs, nmem, rec);
+}
+
+__global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqArgs a, int R, int spill_cap,
+                                                                    int key_cap) {
+  extern __shared__ __align__(128) unsigned char ts_smem[];
+  uint16_t* s_spill = reinterpret_cast<uint16_t*>(ts_smem);
+  uint16_t* s_key = reinterpret_cast<uint16_t*>(ts_smem + spill_cap);
+  uint16_t* s_gkey = s_key + key_cap;
+  int* s_win = reinterpret_cast<int*>(s_gkey + kTsGenCap);  // a.E winner encodings
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int s_base_[2][kMaxC + 1];  // row metadata, double-buffered: the next row's loads while
+  __shared__ int s_q_[2][kMaxC], s_cs_[2][kMaxC], s_cl_[2][kMaxC], s_rcnt_[2][kMaxC];  // this row runs
+  __shared__ int s_next;
+  __shared__ int s_hist[kTsWarps][256];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int C = a.C;
+  const int n = __ldg(a.n_dev), n0 = __ldg(a.n0_dev);
+  const int nsp = min(n, a.Lmax);
+  const uint32_t nbytes = (uint32_t)((nsp + 7) & ~7) * 2u;
+  const int gcount = min(max(0, nsp - n0), kTsGenCap);
+  const uint32_t bar = smem_u32(&mbar);
+  const int32_t* mem_end = a.mem + (int64_t)R * a.Lmax;
+  auto load_meta = [&](int row, int set) {
+    const int64_t rc0 = (int64_t)row * C;
+    for (int c = tid; c < C; c += kTsThreads) {
+      s_q_[set][c] = (int)a.quota[rc0 + c];
+      s_cs_[set][c] = a.cstart[rc0 + c];
+      s_cl_[set][c] = a.clen[rc0 + c];
+      s_rcnt_[set][c] = a.reclist ? a.reccnt[rc0 + c] : 0x7fffffff;
+    }
+  };
+  auto prefix = [&](int set) {  // one warp: exclusive prefix of the quotas
+    const int per = (C + 31) / 32;
+    const int c0 = lane * per, c1 = min(C, c0 + per);
+    int run = 0;
+    for (int c = c0; c < c1; ++c) run += s_q_[set][c];
+    int incl = run;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += x;
+    }
+    int ex = incl - run;
+    for (int c = c0; c < c1; ++c) {
+      s_base_[set][c] = ex;
+      ex += s_q_[set][c];
+    }
+    if (lane == 31) s_base_[set][C] = incl;
+  };
+  auto winners_out = [&](int row, int cnt) {  // CSR slots / generated positions -> positions
+    int32_t* pout = a.exp + (int64_t)row * a.E;
+    const int32_t* pm = a.mem + (int64_t)row * a.Lmax;
+    for (int i = tid; i < cnt; i += kTsThreads) {
+      const int e = s_win[i];
+      pout[i] = e >= 0 ? pm[e] : -e - 1;
+    }
+  };
+  if (tid == 0) {
+    mbar_init(bar);
+    if (nbytes) bulk_load(s_spill, a.scores + (int64_t)blockIdx.x * a.sw, nbytes, bar);
+  }
+  load_meta(blockIdx.x, 0);
+  __syncthreads();
+  if (warp == 0) prefix(0);
+  const unsigned lt = (1u << lane) - 1u;
+  int it = 0, cur = 0, prev_r = -1, prev_cnt = 0;
+  for (int r = blockIdx.x; r < R; r += gridDim.x, ++it, cur ^= 1) {
+    const int nr = r + (int)gridDim.x;
+    const int64_t rC = (int64_t)r * C;
+    const int* s_q = s_q_[cur];
+    const int* s_cs = s_cs_[cur];
+    const int* s_cl = s_cl_[cur];
+    const int* s_rcnt = s_rcnt_[cur];
+    const int* s_base = s_base_[cur];
+    const bool ok = nbytes == 0 || mbar_wait(bar, (uint32_t)(it & 1));
+    if (!__syncthreads_and(ok)) {
+      if (tid == 0 && a.status != nullptr) atomicExch(a.status, 4);
+      if (!ok) mbar_wait(bar, (uint32_t)(it & 1));  // let the copy in flight land before leaving
+      return;
+    }
+    // overlapping phase 1: the previous row's winner positions, the next row's metadata, this row's pads
+    if (prev_r >= 0) winners_out(prev_r, prev_cnt);
+    if (nr < R) load_meta(nr, cur ^ 1);
+    int32_t* out = a.exp + (int64_t)r * a.E;
+    for (int i = s_base[C] + tid; i < a.E; i += kTsThreads) out[i] = -1;
+    if (tid == 0) s_next = 0;
+    // ---- phase 1: member keys in CSR order (key slot = member index + mo, so every 16-byte vector of
+    // the member list becomes one 8-byte store of four keys), generated-position keys
+    const int total = s_cs[C - 1] + s_cl[C - 1];
+    const int32_t* mrow = a.mem + (int64_t)r * a.Lmax;
+    const int mo = (int)((reinterpret_cast<uintptr_t>(mrow) & 15u) >> 2);
+    const int32_t* m0 = mrow - mo;
+    const int nvec = (total + mo + 3) >> 2;
+    const uint32_t lim = (uint32_t)(spill_cap / 2 - 1);  // list entries are positions; clamp keeps reads inside
+    for (int v0 = tid; v0 < nvec; v0 += kTsThreads * kTsU) {
+      int4 x[kTsU];
+#pragma unroll
+      for (int u = 0; u < kTsU; ++u) {
+        const int vi = v0 + u * kTsThreads;
+        const int32_t* p = m0 + 4 * vi;
+        x[u] = make_int4(0, 0, 0, 0);
+        if (vi < nvec) {
+          if (p + 4 <= mem_end) {
+            x[u] = __ldg(reinterpret_cast<const int4*>(p));
+          } else {
+            x[u].x = p + 0 < mem_end ? p[0] : 0;
+            x[u].y = p + 1 < mem_end ? p[1] : 0;
+            x[u].z = p + 2 < mem_end ? p[2] : 0;
+            x[u].w = p + 3 < mem_end ? p[3] : 0;
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kTsU; ++u) {
+        const int vi = v0 + u * kTsThreads;
+        if (vi < nvec) {
+          const uint32_t k0 = s_spill[min((uint32_t)x[u].x, lim)], k1 = s_spill[min((uint32_t)x[u].y, lim)];
+          const uint32_t k2 = s_spill[min((uint32_t)x[u].z, lim)], k3 = s_spill[min((uint32_t)x[u].w, lim)];
+          *reinterpret_cast<uint2*>(s_key + 4 * vi) = make_uint2(ukey16x2(k0 | (k1 << 16)), ukey16x2(k2 | (k3 << 16)));
+        }
+      }
+    }
+    for (int i = tid; i < gcount; i += kTsThreads) s_gkey[i] = (uint16_t)ukey16(s_spill[n0 + i]);
+    __syncthreads();
+    if (tid == 0 && nr < R && nbytes) {  // the staged row is free: fetch the next one
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      bulk_load(s_spill, a.scores + (int64_t)nr * a.sw, nbytes, bar);
+    }
+    if (warp == 0 && nr < R) prefix(cur ^ 1);
+    // ---- phase 2: clusters with q > 0
+    TsRow w{s_key + mo, s_gkey, a.scores + (int64_t)r * a.sw, mrow, n0, nsp, gcount, mo};
+    int* hist = s_hist[warp];
+    const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
+    while (true) {
+      int c = 0;
+      if (lane == 0) {
+        do {
+          c = atomicAdd(&s_next, 1);
+        } while (c < C && s_q[c] <= 0);
+      }
+      c = __shfl_sync(0xffffffffu, c, 0);
+      if (c >= C) break;
+      const int q = s_q[c], base = s_base[c], cs = s_cs[c], nmem = s_cl[c];
+      const int cnt = s_rcnt[c];
+      const bool use_list = a.reclist != nullptr && cnt <= a.rmax;
+      const int32_t* rec = use_list ? a.reclist + (rC + c) * a.rmax : nullptr;
+      const int ngen = use_list ? cnt : 0;
+      if (use_list && q <= kSmallQ && ngen <= 64 && nmem + 3 <= 1024) {
+        const int span = nmem + 3;
+        if (span <= 256)
+          topq_keys_regs<8>(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
+        else if (span <= 512)
+          topq_keys_regs<16>(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
+        else
+          topq_keys_regs<32>(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
+        continue;
+      }
+      // radix path over (list index, key): members from the key array, then generated tokens
+      const int ngen_scan = max(0, n - n0);
+      auto enc_of = [&](int idx) -> int {
+        if (idx < nmem) return cs + idx;
+        return -((use_list ? rec[idx - nmem] : n0 + (idx - nmem)) + 1);
+      };
+      auto for_each = [&](auto&& f) {
+        for (int i0 = 0; i0 < nmem; i0 += 32) {
+          const int i = i0 + lane;
+          const bool v = i < nmem;
+          f(v, i, v ? (uint32_t)w.key[cs + i] : 0u);
+        }
+        if (use_list) {
+          for (int i0 = 0; i0 < cnt; i0 += 32) {
+            const int i = i0 + lane;
+            const bool v = i < cnt;
+            f(v, nmem + i, v ? ts_key_at(w, rec[i]) : 0u);
+          }
+        } else {
+          for (int i0 = 0; i0 < ngen_scan; i0 += 32) {
+            const int t = n0 + i0 + lane;
+            const bool v = (i0 + lane < ngen_scan) && asg_r[t] == c;
+            f(v, nmem + i0 + lane, v ? ts_key_at(w, t) : 0u);
+          }
+        }
+      };
+      int above = 0, hi = 0, lo = 0;
+      bool all = false;
+      for (int pass = 0; pass < 2 && !all; ++pass) {
+        for (int b = lane; b < 256; b += 32) hist[b] = 0;
+        __syncwarp();
+        for_each([&](bool v, int, uint32_t k) {
+          if (v && (pass == 0 || (int)(k >> 8) == hi)) atomicAdd(&hist[pass == 0 ? (k >> 8) : (k & 255)], 1);
+        });
+        __syncwarp();
+        int cnt8[8], sum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          cnt8[i] = hist[255 - 8 * lane - i];
+          sum += cnt8[i];
+        }
+        int incl = sum;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const int x = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += x;
+        }
+        const int excl = incl - sum;
+        const int need = q - above;
+        int fb = -1, fa = 0;
+        if (excl < need && incl >= need) {
+          int run = excl;
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            if (fb < 0 && run + cnt8[i] >= need) {
+              fb = 255 - 8 * lane - i;
+              fa = run;
+            }
+            run += cnt8[i];
+          }
+        }
+        const unsigned who = __ballot_sync(0xffffffffu, fb >= 0);
+        if (who == 0u) {
+          all = true;
+        } else {
+          const int src = __ffs(who) - 1;
+          const int d = __shfl_sync(0xffffffffu, fb, src);
+          above += __shfl_sync(0xffffffffu, fa, src);
+          if (pass == 0) hi = d;
+          else lo = d;
+        }
+        __syncwarp();
+      }
+      const uint32_t T = all ? 0u : (((uint32_t)hi << 8) | (uint32_t)lo);
+      const int need_eq = all ? 0 : q - above;
+      int taken = 0, ties = 0;
+      for_each([&](bool v, int idx, uint32_t k) {
+        const bool gt = v && k > T;
+        const bool eq = v && k == T;
+        const unsigned beq = __ballot_sync(0xffffffffu, eq);
+        const bool take = gt || (eq && ties + __popc(beq & lt) < need_eq);
+        const unsigned bt = __ballot_sync(0xffffffffu, take);
+        const int slot = taken + __popc(bt & lt);
+        if (take && slot < q && base + slot < a.E) s_win[base + slot] = enc_of(idx);
+        taken += __popc(bt);
+        ties += __popc(beq);
+      });
+      __syncwarp();
+    }
+    __syncthreads();  // winners complete; keys and the cluster counter are reused by the next row
+    prev_r = r;
+    prev_cnt = min(s_base[C], a.E);
+  }
+  if (prev_r >= 0) winners_out(prev_r, prev_cnt);
 }
 
 // ------------------------------------------------------------------------ residual proxies (+ flash)
@@ -1038,6 +1431,24 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
   OA_REQUIRE(scores && mem && cstart && clen && asg && quota && n_dev && n0_dev && exp_idx, "%s: null pointer", fn);
   OA_REQUIRE(reclist == nullptr || (reccnt != nullptr && rmax > 0), "%s: reclist needs reccnt and rmax", fn);
   const size_t spill_bytes = (size_t)((Lmax + 7) & ~7ll) * 2;
+  {  // persistent streamed-key kernel when the score row, the member keys and the generated keys fit
+    const int key_cap = (int)(((Lmax + 7) & ~7ll) + 1040);  // list slack of the register path
+    const size_t smem_ts = spill_bytes + (size_t)(key_cap + kTsGenCap) * 2 + (size_t)E * 4;
+    if (smem_ts <= 196 * 1024) {
+      int dev = 0, sms = 148;
+      cudaGetDevice(&dev);
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, 1, mem, cstart,
+                 clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};
+      cudaError_t e =
+          cudaFuncSetAttribute(topq_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_ts);
+      if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+      const int grid = (int)std::min<int64_t>(R, sms);
+      topq_stream_kernel<<<grid, kTsThreads, smem_ts, static_cast<cudaStream_t>(stream)>>>(
+          a, (int)R, (int)spill_bytes, key_cap);
+      return oa_check_launch(fn);
+    }
+  }
   const bool in_smem = spill_bytes <= 160 * 1024;  // larger rows read their keys from global memory
   TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, in_smem ? 1 : 0,
              mem, cstart, clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};

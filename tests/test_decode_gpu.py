@@ -229,3 +229,54 @@ def test_decode_graph_replay_matches_eager():
         torch.cuda.synchronize()
         outs[mode] = torch.stack(res)
     assert torch.equal(outs["eager"], outs["graph"])
+
+
+@pytest.mark.parametrize("rho", [0.01, 0.03])
+def test_decode_32k_steps_bit_exact(rho):
+    """The GPU-built state of one 32K-token request, then decode steps checked against the oracle:
+    clusters of a few hundred to over a thousand members (every width of the top-q register path
+    and its radix path), then steps whose new key repeats one cached key, so one cluster's list of
+    generated tokens grows past 64 with tied scores (ties go to the lower position)."""
+    from openattention_b200 import synth
+    dev = torch.device("cuda")
+    B, n0, steps = 1, 32768, 100
+    Lmax = n0 + steps + 8
+    K, V, mus = synth.kv_torch(23, B, n0, Lmax, dev)
+    Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40] * B
+    m = _method(B, Lmax, rho)
+    C, E, R = m.C, m.E, B * HQ
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    qpre = torch.zeros(1, HQ, n0, D, dtype=torch.bfloat16, device=dev)
+    qpre[:, :, n0 - 64:] = torch.randn(1, HQ, 64, D, generator=g, device=dev).to(torch.bfloat16)
+    m.build(0, 0, qpre, n0)
+    Mth.C.n_dev = None
+    Mth.C.n0_dev = torch.tensor([n0], dtype=torch.int32, device=dev)
+    st_np = {k: (O.bits(v) if v.dtype == torch.bfloat16 else v.cpu().numpy()).copy() for k, v in m.st[0].items()}
+    Kn, Vn = O.bits(K).copy(), O.bits(V).copy()
+    out = torch.empty(R, D, dtype=torch.float32, device=dev)
+    big = int(m.st[0]["clen"].max().item())
+    for s in range(steps):
+        n = n0 + s + 1
+        if s < 20:
+            nk, nv = synth.new_tokens_torch(500 + s, mus, n - 1)
+        else:
+            nk, nv = K[:, :, 1234].clone(), V[:, :, 1234].clone()
+        K[:, :, n - 1], V[:, :, n - 1] = nk, nv
+        Kn[:, :, n - 1], Vn[:, :, n - 1] = O.bits(nk), O.bits(nv)
+        q = torch.randn(B, HQ, 1, D, generator=g, device=dev).to(torch.bfloat16)
+        qr, sel = m.select(0, q, n, residual=False)
+        S.residual_flash(qr, K, V, m.st[0], sel, m.exp_idx, m.nt, m.quota, out, status=m.status)
+        torch.cuda.synchronize()
+        o = O.decode_step(st_np, O.bits(q.reshape(R, D)), Kn, Vn, n, rho, C, E)
+        _eq(f"step{s}.sel", sel, o["sel"])
+        _eq(f"step{s}.quota", m.quota, o["quota"])
+        _eq(f"step{s}.exp_idx", m.exp_idx, o["exp_idx"])
+        got = out.cpu().double().numpy()
+        assert np.abs(got - o["out"]).max() <= 2e-3
+        assert np.linalg.norm(got - o["out"]) <= 1e-3 * np.linalg.norm(o["out"])
+    _eq("reccnt", m.st[0]["reccnt"], st_np["reccnt"])
+    assert int(st_np["reccnt"].max()) > 64, "the repeated key must fill one cluster's generated list past 64"
+    if C == 64:
+        assert big > 512, f"largest cluster {big}: the wider register paths must be reached"
+    assert int(m.status.item()) == 0
