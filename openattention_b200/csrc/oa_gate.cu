@@ -50,114 +50,220 @@ struct GateArgs {
 };
 
 
-__global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const GateArgs a) {
+// One CTA of 2 warps per row, so that every row of a batch is resident at once (the work of a row is
+// a chain of short dependent steps; rows in parallel hide its latency).  Warp w owns the clusters
+// w + 2k and streams their Sk / Sk2 rows (lane l holds dims 4l .. 4l+3, one 16-byte load) in batches of four,
+// the next batch in flight while one is used; the selected tokens' K rows are staged in shared
+// memory and subtracted, in list order, from their clusters; the two dots per cluster use the fixed
+// warp-tree order.  The scalar tail (ln, erf, ln) and the water-filling run one thread per cluster
+// (threads c, c + 64, ...): ranks by counting, the integer prefix of the caps in ratio order (one
+// warp) beside the double suffix sum of the weights (one thread of the other warp).
+constexpr int kEgThreads = 64;
+constexpr int kEgW = kEgThreads / 32;
+constexpr int kEgB = 4;            // clusters per batch per warp
+constexpr int kEgSelCache = 64;    // selected tokens whose K rows are staged in shared memory
+
+struct EgShared {
+  float *score, *nt, *lg, *zd, *sd, *w, *cap, *ratio, *qb, *capo, *wo, *rato, *cex, *wsuf, *inv;
+  int *ord, *rank2, *nsel, *selc, *selt;
+  __nv_bfloat16* selk;
+};
+
+size_t eg_smem_bytes(int C, int NS) {
+  const size_t c4 = (size_t)((C + 3) & ~3);
+  const size_t ns4 = (size_t)((NS + 3) & ~3);
+  return c4 * 4 * 18 + ns4 * 4 * 2 + (size_t)std::min(NS, kEgSelCache) * kD * 2;  // 15 fp32 + 3 int per cluster
+}
+
+__global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(const GateArgs a) {
+  extern __shared__ __align__(16) unsigned char eg_smem[];
   const int r = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kv = r / kG;
-  const int C = a.C;
-  __shared__ float s_score[kMaxC], s_nt[kMaxC], s_w[kMaxC], s_cap[kMaxC], s_ratio[kMaxC], s_qb[kMaxC];
-  __shared__ float s_cex[kMaxC], s_wsuf[kMaxC];
-  __shared__ int s_ord[kMaxC], s_rank2[kMaxC];
-  __shared__ int s_selc[512];
-  __shared__ int s_selt[512];
-  __shared__ float s_red[8];
-  __shared__ int s_redi[8];
-  for (int j = tid; j < a.NS; j += blockDim.x) {
-    const int t = a.sel[(int64_t)r * a.NS + j];
-    s_selt[j] = t;
-    s_selc[j] = (t >= 0 && t < a.Lmax) ? a.asg[(int64_t)r * a.Lmax + t] : -1;
+  const int C = a.C, NS = a.NS;
+  __shared__ float s_red[kEgW];
+  __shared__ int s_redi[kEgW];
+  EgShared S;
+  {
+    unsigned char* p = eg_smem;
+    const int c4 = (C + 3) & ~3, ns4 = (NS + 3) & ~3;
+    float* f = reinterpret_cast<float*>(p);
+    S.score = f;
+    S.nt = f + c4;
+    S.lg = f + 2 * c4;
+    S.zd = f + 3 * c4;
+    S.sd = f + 4 * c4;
+    S.w = f + 5 * c4;
+    S.cap = f + 6 * c4;
+    S.ratio = f + 7 * c4;
+    S.qb = f + 8 * c4;
+    S.capo = f + 9 * c4;
+    S.wo = f + 10 * c4;
+    S.rato = f + 11 * c4;
+    S.cex = f + 12 * c4;
+    S.wsuf = f + 13 * c4;
+    S.inv = f + 14 * c4;
+    p += sizeof(float) * 15 * c4;
+    S.ord = reinterpret_cast<int*>(p);
+    p += sizeof(int) * c4;
+    S.rank2 = reinterpret_cast<int*>(p);
+    p += sizeof(int) * c4;
+    S.nsel = reinterpret_cast<int*>(p);
+    p += sizeof(int) * c4;
+    S.selc = reinterpret_cast<int*>(p);
+    p += sizeof(int) * ns4;
+    S.selt = reinterpret_cast<int*>(p);
+    p += sizeof(int) * ns4;
+    S.selk = reinterpret_cast<__nv_bfloat16*>(p);
   }
+  const int64_t rC = (int64_t)r * C;
+  const __nv_bfloat16* Kr = a.K + (int64_t)kv * a.Lmax * kD;
+  // ---- the first two batches of pooled-sum rows go out first: they depend on nothing
+  float ck[kEgB][4], ck2[kEgB][4], nk[kEgB][4], nk2[kEgB][4];  // this batch, the next one
+  auto fetch = [&](int b, float (&x)[kEgB][4], float (&x2)[kEgB][4]) {
+#pragma unroll
+    for (int k = 0; k < kEgB; ++k) {
+      const int c = warp + kEgW * (b * kEgB + k);
+      const int64_t base = (rC + min(c, C - 1)) * kD;
+      const float4 u = c < C ? __ldg(reinterpret_cast<const float4*>(a.Sk + base) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+      const float4 u2 = c < C ? __ldg(reinterpret_cast<const float4*>(a.Sk2 + base) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
+      x[k][0] = u.x; x[k][1] = u.y; x[k][2] = u.z; x[k][3] = u.w;
+      x2[k][0] = u2.x; x2[k][1] = u2.y; x2[k][2] = u2.z; x2[k][3] = u2.w;
+    }
+  };
+  const int nbatch = (C + kEgW * kEgB - 1) / (kEgW * kEgB);
+  fetch(0, ck, ck2);
+  if (nbatch > 1) fetch(1, nk, nk2);
+  // ---- selected tokens: their clusters and their K rows are fetched side by side
+  for (int j = tid; j < NS; j += kEgThreads) {
+    const int t = a.sel[(int64_t)r * NS + j];
+    const bool v = t >= 0 && t < a.Lmax;
+    S.selt[j] = v ? t : -1;
+    S.selc[j] = v ? a.asg[(int64_t)r * a.Lmax + t] : -1;
+  }
+  for (int e = tid; e < min(NS, kEgSelCache) * 16; e += kEgThreads) {
+    const int j = e >> 4, part = e & 15;
+    const int t = a.sel[(int64_t)r * NS + j];
+    if (t >= 0 && t < a.Lmax)
+      *reinterpret_cast<uint4*>(S.selk + j * kD + part * 8) =
+          __ldg(reinterpret_cast<const uint4*>(Kr + (int64_t)t * kD + part * 8));
+  }
+  __syncthreads();
   float qv[4], q2[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    qv[i] = __bfloat162float(a.q[(int64_t)r * a.q_stride + lane + 32 * i]);
+    qv[i] = __bfloat162float(a.q[(int64_t)r * a.q_stride + 4 * lane + i]);
     q2[i] = __fmul_rn(qv[i], qv[i]);
   }
+  // tail counts and ln n_t, one thread per cluster, while the rows are in flight
+  for (int c = tid; c < C; c += kEgThreads) {
+    float ntc = a.nb[rC + c];
+    int ns_c = 0;
+    for (int j = 0; j < NS; ++j)
+      if (S.selc[j] == c) {
+        ntc = __fsub_rn(ntc, 1.f);
+        ++ns_c;
+      }
+    S.nt[c] = ntc;
+    S.nsel[c] = ns_c;
+    S.inv[c] = __fdiv_rn(1.f, fmaxf(ntc, 1.f));
+    S.lg[c] = ln_f(fmaxf(ntc, 1.f));
+  }
   __syncthreads();
-  // ---- ErrorGate: warp per cluster; the next cluster's pooled-sum rows are requested before the
-  //      current one is processed
-  constexpr int kStride = kGateThreads / 32;
-  float nk[4], nk2[4];
-  auto fetch = [&](int c, float (&x)[4], float (&x2)[4]) {
-    const int64_t base = ((int64_t)r * C + min(c, C - 1)) * kD;
+  // ---- ErrorGate dots, batch by batch
+  for (int b = 0; b < nbatch; ++b) {
+    float sk[kEgB][4], sk2[kEgB][4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      x[i] = a.Sk[base + lane + 32 * i];
-      x2[i] = a.Sk2[base + lane + 32 * i];
-    }
-  };
-  if (warp < C) fetch(warp, nk, nk2);
-  for (int c = warp; c < C; c += kStride) {
-    float skt[4], sk2t[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      skt[i] = nk[i];
-      sk2t[i] = nk2[i];
-    }
-    if (c + kStride < C) fetch(c + kStride, nk, nk2);
-    float ntc = a.nb[(int64_t)r * C + c];
-    for (int j = 0; j < a.NS; ++j) {
-      if (s_selc[j] != c) continue;
-      const __nv_bfloat16* kr = a.K + ((int64_t)kv * a.Lmax + s_selt[j]) * kD;
+    for (int k = 0; k < kEgB; ++k)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float kf = __bfloat162float(kr[lane + 32 * i]);
-        skt[i] = __fsub_rn(skt[i], kf);
-        sk2t[i] = __fsub_rn(sk2t[i], __fmul_rn(kf, kf));
+        sk[k][i] = ck[k][i];
+        sk2[k][i] = ck2[k][i];
+        ck[k][i] = nk[k][i];
+        ck2[k][i] = nk2[k][i];
       }
-      ntc = __fsub_rn(ntc, 1.f);
-    }
-    const float inv = __fdiv_rn(1.f, fmaxf(ntc, 1.f));
-    float kb[4], var[4];
+    if (b + 2 < nbatch) fetch(b + 2, nk, nk2);
+    const int cb = warp + kEgW * b * kEgB;  // clusters cb + kEgW * k
+    int any = 0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      kb[i] = __fmul_rn(skt[i], inv);
-      const float p1 = __fmul_rn(sk2t[i], inv);
-      const float p2 = __fmul_rn(kb[i], kb[i]);
-      var[i] = fmaxf(__fsub_rn(p1, p2), 0.f);
+    for (int k = 0; k < kEgB; ++k) any |= (cb + kEgW * k < C) ? S.nsel[cb + kEgW * k] : 0;
+    for (int j = 0; any && j < NS; ++j) {  // selected tokens leave their clusters, in list order
+      const int cj = S.selc[j];
+      const int d = cj - cb;
+      if (cj < 0 || d < 0 || d >= kEgW * kEgB || d % kEgW != 0) continue;  // warp-uniform
+      float kf[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+        kf[i] = __bfloat162float(j < kEgSelCache ? S.selk[j * kD + 4 * lane + i]
+                                                 : Kr[(int64_t)S.selt[j] * kD + 4 * lane + i]);
+#pragma unroll
+      for (int k = 0; k < kEgB; ++k) {
+        if (d == kEgW * k) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            sk[k][i] = __fsub_rn(sk[k][i], kf[i]);
+            sk2[k][i] = __fsub_rn(sk2[k][i], __fmul_rn(kf[i], kf[i]));
+          }
+        }
+      }
     }
-    const float zd = warp_tree_dot(qv, kb);
-    const float sd = warp_tree_dot(q2, var);
+    float zd[kEgB], sd[kEgB];
+#pragma unroll
+    for (int k = 0; k < kEgB; ++k) {
+      const int c = cb + kEgW * k;
+      const float inv = c < C ? S.inv[c] : 1.f;
+      float kb[4], var[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        kb[i] = __fmul_rn(sk[k][i], inv);
+        const float p1 = __fmul_rn(sk2[k][i], inv);
+        const float p2 = __fmul_rn(kb[i], kb[i]);
+        var[i] = fmaxf(__fsub_rn(p1, p2), 0.f);
+      }
+      zd[k] = warp_tree_dot(qv, kb);
+      sd[k] = warp_tree_dot(q2, var);
+    }
     if (lane == 0) {
-      s_w[c] = zd;  // staging: dots and tail counts, the scalar tail runs one thread per cluster below
-      s_cap[c] = sd;
-      s_nt[c] = ntc;
+#pragma unroll
+      for (int k = 0; k < kEgB; ++k) {
+        const int c = cb + kEgW * k;
+        if (c < C) {
+          S.zd[c] = zd[k];
+          S.sd[c] = sd[k];
+        }
+      }
     }
   }
   __syncthreads();
-  if (tid < C) {
-    const float zbar = __fmul_rn(0.08838834764831845f, s_w[tid]);
-    const float s2 = __fmul_rn(0.0078125f, s_cap[tid]);
-    const float lg = ln_f(fmaxf(s_nt[tid], 1.f));
+  float smax = -INFINITY;
+  for (int c = tid; c < C; c += kEgThreads) {
+    const float zbar = __fmul_rn(0.08838834764831845f, S.zd[c]);
+    const float s2 = __fmul_rn(0.0078125f, S.sd[c]);
     const float er = erf_f(__fmul_rn(__fsqrt_rn(s2), 0.70710677f));
     const float le = ln_f(fmaxf(er, 1e-30f));
-    float sc = __fadd_rn(zbar, lg);
+    float sc = __fadd_rn(zbar, S.lg[c]);
     sc = __fadd_rn(sc, __fmul_rn(0.5f, s2));
     sc = __fadd_rn(sc, le);
-    s_score[tid] = sc;
+    S.score[c] = sc;
+    smax = fmaxf(smax, S.nt[c] > 1.f ? sc : -INFINITY);
   }
-  __syncthreads();
-  // ---- water-filling (thread c <-> cluster c)
-  const int c = tid;
-  const bool act = c < C;
-  const bool live = act && s_nt[c] > 1.f;
-  const float sm = live ? s_score[c] : -INFINITY;
-  float smax = sm;
+  // ---- water-filling
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) smax = fmaxf(smax, __shfl_xor_sync(0xffffffffu, smax, off));
   if (lane == 0) s_red[warp] = smax;
   __syncthreads();
   smax = s_red[0];
 #pragma unroll
-  for (int w = 1; w < 8; ++w) smax = fmaxf(smax, s_red[w]);
-  float w = 0.f, cap = 0.f, ratio = INFINITY;
-  if (act) {
-    w = live ? exp_f(__fsub_rn(sm, smax)) : 0.f;
-    cap = live ? s_nt[c] : 0.f;
-    ratio = w > 0.f ? __fdiv_rn(cap, fmaxf(w, 1e-30f)) : INFINITY;
-    s_w[c] = w;
-    s_cap[c] = cap;
-    s_ratio[c] = ratio;
+  for (int v = 1; v < kEgW; ++v) smax = fmaxf(smax, s_red[v]);
+  float tot_part = 0.f;
+  for (int c = tid; c < C; c += kEgThreads) {
+    const bool live = S.nt[c] > 1.f;
+    const float w = live ? exp_f(__fsub_rn(S.score[c], smax)) : 0.f;
+    const float cap = live ? S.nt[c] : 0.f;
+    S.w[c] = w;
+    S.cap[c] = cap;
+    S.ratio[c] = w > 0.f ? __fdiv_rn(cap, fmaxf(w, 1e-30f)) : INFINITY;
+    tot_part = __fadd_rn(tot_part, cap);
   }
   // integer-valued sums (< 2^24): exact in any order, so a block reduction gives the sequential value
   auto block_sum = [&](float v) {
@@ -168,42 +274,60 @@ __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const
     __syncthreads();
     float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < kGateThreads / 32; ++w) t = __fadd_rn(t, s_red[w]);
+    for (int w = 0; w < kEgW; ++w) t = __fadd_rn(t, s_red[w]);
     return t;
   };
-  const float tot = block_sum(act ? cap : 0.f);
-  if (act) {
-    // rank by (ratio asc, cluster asc); rank by (score desc, cluster asc)
+  const float tot = block_sum(tot_part);  // its barriers also publish w, cap, ratio, score
+  for (int c = tid; c < C; c += kEgThreads) {  // ranks by (ratio asc, cluster asc), (score desc, cluster asc)
+    const float ratio = S.ratio[c];
+    const float sm = S.nt[c] > 1.f ? S.score[c] : -INFINITY;
     int r1 = 0, r2 = 0;
     for (int j = 0; j < C; ++j) {
-      const float rj = s_ratio[j];
+      const float rj = S.ratio[j];
       r1 += (rj < ratio || (rj == ratio && j < c)) ? 1 : 0;
-      const bool lj = s_nt[j] > 1.f;
-      const float sj = lj ? s_score[j] : -INFINITY;
+      const float sj = S.nt[j] > 1.f ? S.score[j] : -INFINITY;
       r2 += (sj > sm || (sj == sm && j < c)) ? 1 : 0;
     }
-    s_ord[r1] = c;
-    s_rank2[c] = r2;
+    S.ord[r1] = c;
+    S.rank2[c] = r2;
   }
   __syncthreads();
-  if (act) {  // exclusive prefix of the caps in ratio order (integers)
-    float cex = 0.f;
-    for (int j = 0; j < c; ++j) cex = __fadd_rn(cex, s_cap[s_ord[j]]);
-    s_cex[c] = cex;  // indexed by sorted position c
+  for (int j = tid; j < C; j += kEgThreads) {  // caps, weights and ratios in ratio order
+    const int o = S.ord[j];
+    S.capo[j] = S.cap[o];
+    S.wo[j] = S.w[o];
+    S.rato[j] = S.ratio[o];
   }
-  if (tid == 0) {  // suffix sums of the weights in ratio order, accumulated in double from the end
+  __syncthreads();
+  if (warp == 0) {  // exclusive prefix of the caps in ratio order (integers)
+    const int per = (C + 31) / 32;
+    const int j0 = lane * per, j1 = min(C, j0 + per);
+    float run = 0.f;
+    for (int j = j0; j < j1; ++j) run = __fadd_rn(run, S.capo[j]);
+    float incl = run;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const float x = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl = __fadd_rn(incl, x);
+    }
+    float ex = __fsub_rn(incl, run);
+    for (int j = j0; j < j1; ++j) {
+      S.cex[j] = ex;
+      ex = __fadd_rn(ex, S.capo[j]);
+    }
+  } else if (lane == 0) {  // suffix sums of the weights in ratio order, accumulated in double from the end
     double acc = 0.0;
     for (int j = C - 1; j >= 0; --j) {
-      acc = __dadd_rn(acc, (double)s_w[s_ord[j]]);
-      s_wsuf[j] = __double2float_rn(acc);
+      acc = __dadd_rn(acc, (double)S.wo[j]);
+      S.wsuf[j] = __double2float_rn(acc);
     }
   }
   __syncthreads();
   int jj = 0x7fffffff;
-  if (act) {
-    const float ws = s_wsuf[c];
-    const float f = ws > 0.f ? __fadd_rn(s_cex[c], __fmul_rn(s_ratio[s_ord[c]], ws)) : INFINITY;
-    if (f >= a.E) jj = c;
+  for (int j = tid; j < C; j += kEgThreads) {
+    const float ws = S.wsuf[j];
+    const float f = ws > 0.f ? __fadd_rn(S.cex[j], __fmul_rn(S.rato[j], ws)) : INFINITY;
+    if (f >= a.E) jj = min(jj, j);
   }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) jj = min(jj, __shfl_xor_sync(0xffffffffu, jj, off));
@@ -211,26 +335,27 @@ __global__ void __launch_bounds__(kGateThreads) errorgate_waterfill_kernel(const
   __syncthreads();
   jj = s_redi[0];
 #pragma unroll
-  for (int v = 1; v < 8; ++v) jj = min(jj, s_redi[v]);
+  for (int v = 1; v < kEgW; ++v) jj = min(jj, s_redi[v]);
   if (jj == 0x7fffffff) jj = 0;
-  const float lam = __fdiv_rn(__fsub_rn(a.E, s_cex[jj]), fmaxf(s_wsuf[jj], 1e-30f));
-  float qb = 0.f;
-  if (act) {
-    qb = fminf(cap, floorf(__fmul_rn(lam, w)));
-    if (tot <= a.E) qb = cap;
-    s_qb[c] = qb;
+  const float lam = __fdiv_rn(__fsub_rn(a.E, S.cex[jj]), fmaxf(S.wsuf[jj], 1e-30f));
+  float q_part = 0.f;
+  for (int c = tid; c < C; c += kEgThreads) {
+    float qb = fminf(S.cap[c], floorf(__fmul_rn(lam, S.w[c])));
+    if (tot <= a.E) qb = S.cap[c];
+    S.qb[c] = qb;
+    q_part = __fadd_rn(q_part, qb);
   }
-  const float sumq = block_sum(act ? qb : 0.f);
+  const float sumq = block_sum(q_part);
   const float rem = fmaxf(__fsub_rn(fminf(tot, a.E), sumq), 0.f);
-  if (act) {
-    const bool room = qb < cap;
-    int before = 0;  // clusters with room ranked ahead by (score desc, cluster asc)
-    const int my = s_rank2[c];
-    for (int j = 0; j < C; ++j) before += (s_qb[j] < s_cap[j] && s_rank2[j] < my) ? 1 : 0;
+  for (int c = tid; c < C; c += kEgThreads) {  // leftovers: one each to the best-scoring clusters with room
+    const int my = S.rank2[c];
+    int before = 0;
+    for (int j = 0; j < C; ++j) before += (S.qb[j] < S.cap[j] && S.rank2[j] < my) ? 1 : 0;
+    const bool room = S.qb[c] < S.cap[c];
     const float add = (room && (float)before < rem) ? 1.f : 0.f;
-    a.quota[(int64_t)r * C + c] = __fadd_rn(qb, add);
-    a.nt[(int64_t)r * C + c] = s_nt[c];
-    a.score[(int64_t)r * C + c] = s_score[c];
+    a.quota[rC + c] = __fadd_rn(S.qb[c], add);
+    a.nt[rC + c] = S.nt[c];
+    a.score[rC + c] = S.score[c];
   }
 }
 
@@ -1413,9 +1538,11 @@ extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const voi
   OA_REQUIRE(n_sel > 0 && n_sel <= 512, "%s: n_sel=%lld outside [1, 512]", fn, (long long)n_sel);
   OA_REQUIRE(q && K && asg && sel && Sk && Sk2 && nb && score && nt && quota, "%s: null pointer", fn);
   OA_REQUIRE(E >= 0.f, "%s: negative budget", fn);
+  OA_REQUIRE(oa_aligned16(Sk) && oa_aligned16(Sk2), "%s: Sk / Sk2 must be 16-byte aligned", fn);
   GateArgs a{static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(K), (int)Lmax, (int)C,
              (int)n_sel, asg, sel, Sk, Sk2, nb, E, score, nt, quota, status};
-  errorgate_waterfill_kernel<<<(unsigned)(B * kHQ), kGateThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  const size_t smem = eg_smem_bytes((int)C, (int)n_sel);
+  errorgate_waterfill_kernel<<<(unsigned)(B * kHQ), kEgThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }
 

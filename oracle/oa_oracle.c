@@ -418,16 +418,16 @@ void oro_select(int R, int n, int ns, int nl, int k_top, uint16_t* s, int64_t sw
   }
 }
 
-/* 128-term dot product in the order one warp computes it: lane l accumulates
- * fma(a[l+96], b[l+96], fma(a[l+64], b[l+64], fma(a[l+32], b[l+32], a[l]*b[l]))), then the 32
- * partials are combined by an xor butterfly over offsets 16, 8, 4, 2, 1. */
+/* 128-term dot product in the order one warp computes it: lane l holds dims 4l .. 4l+3 and
+ * accumulates fma(a[4l+3], b[4l+3], fma(a[4l+2], b[4l+2], fma(a[4l+1], b[4l+1], a[4l]*b[4l]))), then
+ * the 32 partials are combined by an xor butterfly over offsets 16, 8, 4, 2, 1. */
 float oro_dot128_tree(const float* a, const float* b) {
   float p[32], t[32];
   for (int l = 0; l < 32; ++l) {
-    float v = a[l] * b[l];
-    v = fmaf(a[l + 32], b[l + 32], v);
-    v = fmaf(a[l + 64], b[l + 64], v);
-    v = fmaf(a[l + 96], b[l + 96], v);
+    float v = a[4 * l] * b[4 * l];
+    v = fmaf(a[4 * l + 1], b[4 * l + 1], v);
+    v = fmaf(a[4 * l + 2], b[4 * l + 2], v);
+    v = fmaf(a[4 * l + 3], b[4 * l + 3], v);
     p[l] = v;
   }
   for (int off = 16; off >= 1; off >>= 1) {
