@@ -220,32 +220,48 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
     if (lane == 0) sS[warp] = S;
   }
   __syncthreads();
-  // B fragments: column n = gid -> head 2m + gid/4, limb gid%4; rows k = tig*4..+3 and 16 + tig*4..+3
+  // B fragments of the two MMAs: column n = gid -> head gid / 2, limb 2m + gid % 2 (m = 0: limbs 0-1,
+  // m = 1: limbs 2-3); rows k = tig*4..+3 and 16 + tig*4..+3.  The accumulators of thread (gid, tig)
+  // then hold all four limbs of head tig for tokens gid and gid + 8: no exchange between lanes.
   uint32_t bf[2][2];
 #pragma unroll
   for (int m = 0; m < 2; ++m) {
-    const int h = 2 * m + (gid >> 2), k = gid & 3;
+    const int h = gid >> 1, k = 2 * m + (gid & 1);
     bf[m][0] = *reinterpret_cast<const uint32_t*>(&limb[h][k][tig * 4]);
     bf[m][1] = *reinterpret_cast<const uint32_t*>(&limb[h][k][16 + tig * 4]);
   }
-  const int fin_head[2] = {0 + (tig >> 1), 2 + (tig >> 1)};
-  const int S_h[2] = {sS[fin_head[0]], sS[fin_head[1]]};
+  const int S_h = sS[tig];
+  const bool one_mul = S_h >= -100 && S_h <= 100;  // 2^-S is a normal float: one exact multiply
+  const float inv2S = one_mul ? pow2f_exact(-S_h) : 0.f;
+  uint16_t* srow = a.scores + (int64_t)(kv * kG + tig) * a.sw;
   const bool ok = ntok == 0 || mbar_wait(bar, 0);
   if (!__syncthreads_and(ok)) {  // the copy did not complete in time: report, wait once more, skip
     if (tid == 0 && a.status != nullptr) atomicExch(a.status, 1);
     if (!ok) mbar_wait(bar, 0);
     return;
   }
+  // exact limb sum l0 + l1 2^8 + l2 2^16 + l3 2^24 (|l| < 2^19) -> fp32 (one rounding) -> x 2^-S -> bf16
+  auto finish = [&](int l0, int l1, int l2, int l3, int t, float& hm) {
+    const long long tot = (long long)(l3 * 256 + l2) * 65536 + (long long)(l1 * 256 + l0);
+    const float f0 = __ll2float_rn(tot);
+    const float f = one_mul ? __fmul_rn(f0, inv2S) : scale_pow2(f0, -S_h);
+    uint16_t sb = f2bf_bits(f);
+    if (t < a.ns || t >= n - a.nl || t >= n) sb = 0xff80u;
+    if (t < a.Lmax) {
+      srow[t] = sb;
+      hm = fmaxf(hm, __uint_as_float((uint32_t)sb << 16));
+    }
+  };
 #pragma unroll
   for (int ti = 0; ti < kTilesPerCta; ++ti) {
     const int tile = t_begin + ti;
     const int t0 = tile * kTile;
-    float hmax[2] = {-INFINITY, -INFINITY};  // for heads fin_head[0], fin_head[1]
+    float hmax = -INFINITY;  // head tig, this warp's 32 tokens
     if (t0 < n && t0 < a.Lmax) {
 #pragma unroll
       for (int grp = 0; grp < 2; ++grp) {
         const int lt0 = ti * kTile + warp * 32 + grp * 16;  // chunk-local first token of the 16
-        const int ta = tok0 + lt0 + gid, tb8 = ta + 8;
+        const int ta = tok0 + lt0 + gid;
         // ldmatrix x4: matrices (rows 0-7 | 8-15) x (bytes 0-15 | 16-31) of the 16 x 32-byte tile
         uint32_t af[4];
         const int mi = lane >> 3, ri = lane & 7;
@@ -253,44 +269,19 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
         asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                      : "=r"(af[0]), "=r"(af[1]), "=r"(af[2]), "=r"(af[3])
                      : "r"(smem_u32(rowp)));
-#pragma unroll
-        for (int m = 0; m < 2; ++m) {
-          int d[4];
-          mma_s8(d, af, bf[m][0], bf[m][1]);
-          // exchange limb pairs with the partner lane (tig ^ 1) holding the other two limbs
-          int e[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) e[i] = __shfl_xor_sync(0xffffffffu, d[i], 1);
-          // limbs 0,1 live on even tig, limbs 2,3 on odd tig; even tig finalises token gid, odd gid+8
-          const bool odd = (tig & 1) != 0;
-          const int l0 = odd ? e[2] : d[0], l1 = odd ? e[3] : d[1];
-          const int l2 = odd ? d[2] : e[0], l3 = odd ? d[3] : e[1];
-          const int row = tig & 1;
-          const long long tot = (long long)l0 + ((long long)l1 << 8) + ((long long)l2 << 16) + ((long long)l3 << 24);
-          const int t = row ? tb8 : ta;
-          const float f = scale_pow2(__ll2float_rn(tot), -S_h[m]);
-          uint16_t sb = f2bf_bits(f);
-          if (t < a.ns || t >= n - a.nl || t >= n) sb = 0xff80u;
-          if (t < a.Lmax) {
-            a.scores[(int64_t)(kv * kG + fin_head[m]) * a.sw + t] = sb;
-            hmax[m] = fmaxf(hmax[m], __uint_as_float((uint32_t)sb << 16));
-          }
-        }
+        int d0[4], d1[4];
+        mma_s8(d0, af, bf[0][0], bf[0][1]);
+        mma_s8(d1, af, bf[1][0], bf[1][1]);
+        finish(d0[0], d0[1], d1[0], d1[1], ta, hmax);
+        finish(d0[2], d0[3], d1[2], d1[3], ta + 8, hmax);
       }
     }
-    // maximum of this warp's 32 tokens per head (a 32-token tile): lanes with equal tig>>1 hold
-    // head 2m + (tig>>1); written directly, no cross-warp reduction
+    // maximum of this warp's 32 tokens for head tig (a 32-token tile): reduce over gid
     const int wt = tile * (kTile / kMaxTile) + warp;  // 32-token tile index
-#pragma unroll
-    for (int m = 0; m < 2; ++m) {
-      float v = hmax[m];
-      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 1));
-      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
-      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
-      v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
-      if (wt < a.NT && (lane == 0 || lane == 2))
-        a.tmax[(int64_t)(kv * kG + 2 * m + (lane >> 1)) * a.tm_stride + wt] = v;
-    }
+    hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, 4));
+    hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, 8));
+    hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, 16));
+    if (wt < a.NT && gid == 0) a.tmax[(int64_t)(kv * kG + tig) * a.tm_stride + wt] = hmax;
   }
 }
 
