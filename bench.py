@@ -238,7 +238,15 @@ def stage_profile(m, Mth, gs, iters):
             tot += e0.elapsed_time(e1)
         return tot / iters
 
+    upd_keys = [k for k in ("codes", "asg", "nb", "Sk", "Sk2", "Sv", "reclist", "reccnt") if k in st]
+    upd_snap = {k: st[k].clone() for k in upd_keys}
+
+    def upd_restore():  # the index update appends the step's token: put the state back before each launch
+        for k in upd_keys:
+            st[k].copy_(upd_snap[k])
+
     ms = {
+        "index_update_kernel": timed(lambda: S.index_update(K, V, st, n_dev, q=qr, zq=m.zq), prep=upd_restore),
         "qgs_scan_kernel": timed(lambda: S.qgs_scan(st["codes"], m.zq, n_dev, ns, nl, m.scores, m.tmax, m.status)),
         "qgs_select_kernel": timed(lambda: S.qgs_select(m.scores, m.tmax, m.Lmax, n_dev, ns, nl, k_top, sel),
                                    prep=lambda: m.scores.copy_(scores_snap)),
@@ -254,6 +262,7 @@ def stage_profile(m, Mth, gs, iters):
     reads = int((m.exp_idx >= 0).sum().item()) + R * NS
     nt_tiles = (n + 31) // 32
     alg = {
+        "index_update_kernel": R * (D * 16 * 2 + C * 16 * 4 + 3 * D * 4 * 2 + D * 2) + Rkv * (D * 32 * 4 + 2 * D * 2),
         "qgs_scan_kernel": Rkv * n * 32,
         "qgs_select_kernel": R * (nt_tiles * 4 + NS * 4),
         "errorgate_waterfill_kernel": R * (2 * C * D * 4 + C * 4 + NS * (D * 2 + 4) + D * 2 + 3 * C * 4),

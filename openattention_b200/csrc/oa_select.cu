@@ -41,70 +41,79 @@ struct IndexArgs {
   int Lmax, C;
 };
 
+// One CTA per QUERY head r = kv*4 + g (so a batch's whole index update is resident at once): the
+// KV head's QGS basis U, this head's QGC projection W and centroids are staged together; warp 0
+// forms zq for this head, warp 1 (g == 0 only) the KV head's code of the new key, warp 2 the rank-16
+// projection zp; the four warps then score the centroids (ties -> lower cluster id) and the CTA
+// updates the cluster's pooled sums.  Every dot keeps its sequential fma order over d (or c).
+constexpr int kIuCentCache = 256;  // clusters whose centroids are staged in shared memory
+
 __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
-  const int kv = blockIdx.x;
+  extern __shared__ __align__(16) float iu_cent[];  // min(C, kIuCentCache) x 16
+  const int r = blockIdx.x;
+  const int kv = r / kG, g = r % kG;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int pos = __ldg(a.n_dev) - 1;
-  __shared__ float kf[kD], vf[kD], qf[kG][kD], zp[kG][kRC];
-  __shared__ __align__(16) float sU[kD * kRQ];             // this KV head's QGS basis
-  __shared__ __align__(16) __nv_bfloat16 sW[kG * kD * kRC];  // the 4 query heads' QGC projections
+  __shared__ float kf[kD], vf[kD], qf[kD], zp[kRC];
+  __shared__ __align__(16) float sU[kD * kRQ];              // this KV head's QGS basis
+  __shared__ __align__(16) __nv_bfloat16 sW[kD * kRC];      // this query head's QGC projection
+  __shared__ float s_bv[4];
+  __shared__ int s_bi[4];
   const bool have_tok = pos >= 0 && pos < a.Lmax;
+  const int C = a.C;
+  const int cstage = min(C, kIuCentCache);
+  const float* ce = a.cent + (int64_t)r * C * kRC;
   const float* Uk = a.U + (int64_t)kv * kD * kRQ;
   for (int i = tid; i < kD * kRQ / 4; i += 128)
     reinterpret_cast<float4*>(sU)[i] = __ldg(reinterpret_cast<const float4*>(Uk) + i);
-  for (int i = tid; i < kG * kD * kRC / 8; i += 128)
-    reinterpret_cast<uint4*>(sW)[i] = __ldg(reinterpret_cast<const uint4*>(a.W + (int64_t)kv * kG * kD * kRC) + i);
+  for (int i = tid; i < kD * kRC / 8; i += 128)
+    reinterpret_cast<uint4*>(sW)[i] = __ldg(reinterpret_cast<const uint4*>(a.W + (int64_t)r * kD * kRC) + i);
+  for (int i = tid; i < cstage * kRC / 4; i += 128)
+    reinterpret_cast<float4*>(iu_cent)[i] = __ldg(reinterpret_cast<const float4*>(ce) + i);
   if (have_tok) {
     kf[tid] = __bfloat162float(a.K[((int64_t)kv * a.Lmax + pos) * kD + tid]);
     vf[tid] = __bfloat162float(a.V[((int64_t)kv * a.Lmax + pos) * kD + tid]);
   }
-  if (a.q != nullptr) {
-#pragma unroll
-    for (int g = 0; g < kG; ++g) qf[g][tid] = __bfloat162float(a.q[(int64_t)(kv * kG + g) * a.q_stride + tid]);
-  }
+  if (a.q != nullptr) qf[tid] = __bfloat162float(a.q[(int64_t)r * a.q_stride + tid]);
   __syncthreads();
-  // query projection zq[r, j] = bf16((q . U[:, j]) * scale_j), d ascending
-  if (a.q != nullptr) {
-    const int g = tid >> 5, j = tid & 31;
-    float acc = 0.f;
+  if (warp == 0) {  // query projection zq[r, j] = bf16((q . U[:, j]) * scale_j), d ascending
+    if (a.q != nullptr) {
+      const int j = lane;
+      float acc = 0.f;
 #pragma unroll 8
-    for (int d = 0; d < kD; ++d) acc = __fmaf_rn(qf[g][d], sU[d * kRQ + j], acc);
-    a.zq[(int64_t)(kv * kG + g) * kRQ + j] = __float2bfloat16_rn(__fmul_rn(acc, __ldg(&a.scale[kv * kRQ + j])));
+      for (int d = 0; d < kD; ++d) acc = __fmaf_rn(qf[d], sU[d * kRQ + j], acc);
+      a.zq[(int64_t)r * kRQ + j] = __float2bfloat16_rn(__fmul_rn(acc, __ldg(&a.scale[kv * kRQ + j])));
+    }
+  } else if (warp == 1) {  // QGS code of the new key (per KV head: query head 0 of the group writes it)
+    if (have_tok && g == 0) {
+      const int j = lane;
+      float acc = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < kD; ++d) acc = __fmaf_rn(kf[d], sU[d * kRQ + j], acc);
+      float c = rintf(__fdiv_rn(acc, __ldg(&a.scale[kv * kRQ + j])));
+      c = fminf(fmaxf(c, -127.f), 127.f);
+      a.codes[((int64_t)kv * a.Lmax + pos) * kRQ + j] = (int8_t)c;
+    }
+  } else if (warp == 2) {  // rank-16 QGC projection: zp = bf16(k . W) - colmean
+    if (have_tok && lane < kRC) {
+      const int c = lane;
+      float acc = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < kD; ++d) acc = __fmaf_rn(kf[d], __bfloat162float(sW[d * kRC + c]), acc);
+      zp[c] = __fsub_rn(bf_round(acc), __ldg(&a.colmean[r * kRC + c]));
+    }
   }
   if (!have_tok) return;
-  // QGS code of the new key (per KV head)
-  if (tid < kRQ) {
-    const int j = tid;
-    float acc = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < kD; ++d) acc = __fmaf_rn(kf[d], sU[d * kRQ + j], acc);
-    float c = rintf(__fdiv_rn(acc, __ldg(&a.scale[kv * kRQ + j])));
-    c = fminf(fmaxf(c, -127.f), 127.f);
-    a.codes[((int64_t)kv * a.Lmax + pos) * kRQ + j] = (int8_t)c;
-  }
-  // rank-16 QGC projection per query head: zp = bf16(k . W) - colmean
-  if (tid < kG * kRC) {
-    const int g = tid >> 4, c = tid & 15;
-    const int r = kv * kG + g;
-    const __nv_bfloat16* Wr = sW + g * kD * kRC;
-    float acc = 0.f;
-#pragma unroll 8
-    for (int d = 0; d < kD; ++d) acc = __fmaf_rn(kf[d], __bfloat162float(Wr[d * kRC + c]), acc);
-    zp[g][c] = __fsub_rn(bf_round(acc), __ldg(&a.colmean[r * kRC + c]));
-  }
   __syncthreads();
-  // nearest centroid (warp g <-> query head g); ties -> lower cluster id
-  const int g = warp;
-  const int r = kv * kG + g;
-  const float* ce = a.cent + (int64_t)r * a.C * kRC;
+  // nearest centroid: thread i scores clusters i, i + 128, ...; ties -> lower cluster id
   float bestv = -INFINITY;
   int besti = 0x7fffffff;
-  for (int i = lane; i < a.C; i += 32) {
+  for (int i = tid; i < C; i += 128) {
     float dot = 0.f, nrm = 0.f;
 #pragma unroll
     for (int c = 0; c < kRC; ++c) {
-      const float x = __ldg(&ce[i * kRC + c]);
-      dot = __fmaf_rn(zp[g][c], x, dot);
+      const float x = i < cstage ? iu_cent[i * kRC + c] : __ldg(&ce[i * kRC + c]);
+      dot = __fmaf_rn(zp[c], x, dot);
       nrm = __fmaf_rn(x, x, nrm);
     }
     const float dist = __fsub_rn(dot, __fmul_rn(0.5f, nrm));
@@ -122,24 +131,35 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
       besti = oi;
     }
   }
-  const int cid = besti == 0x7fffffff ? 0 : besti;
-  float* sk = a.Sk + ((int64_t)r * a.C + cid) * kD;
-  float* sk2 = a.Sk2 + ((int64_t)r * a.C + cid) * kD;
-  float* sv = a.Sv + ((int64_t)r * a.C + cid) * kD;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int d = lane + 32 * i;
-    sk[d] = __fadd_rn(sk[d], kf[d]);
-    sk2[d] = __fadd_rn(sk2[d], __fmul_rn(kf[d], kf[d]));
-    sv[d] = __fadd_rn(sv[d], vf[d]);
-  }
   if (lane == 0) {
+    s_bv[warp] = bestv;
+    s_bi[warp] = besti;
+  }
+  __syncthreads();
+  bestv = s_bv[0];
+  besti = s_bi[0];
+#pragma unroll
+  for (int w = 1; w < 4; ++w) {
+    if (s_bv[w] > bestv || (s_bv[w] == bestv && s_bi[w] < besti)) {
+      bestv = s_bv[w];
+      besti = s_bi[w];
+    }
+  }
+  const int cid = besti == 0x7fffffff ? 0 : besti;
+  const int64_t row = (int64_t)r * C + cid;
+  {  // one round-to-nearest add per element: a reduction without a return is the same value, no wait
+    const int d = tid;
+    atomicAdd(&a.Sk[row * kD + d], kf[d]);
+    atomicAdd(&a.Sk2[row * kD + d], __fmul_rn(kf[d], kf[d]));
+    atomicAdd(&a.Sv[row * kD + d], vf[d]);
+  }
+  if (tid == 0) {
     a.asg[(int64_t)r * a.Lmax + pos] = cid;
-    a.nb[(int64_t)r * a.C + cid] = __fadd_rn(a.nb[(int64_t)r * a.C + cid], 1.f);
+    atomicAdd(&a.nb[row], 1.f);
     if (a.reclist != nullptr) {
-      const int cnt = a.reccnt[(int64_t)r * a.C + cid];
-      if (cnt < a.rmax) a.reclist[((int64_t)r * a.C + cid) * a.rmax + cnt] = pos;
-      a.reccnt[(int64_t)r * a.C + cid] = cnt + 1;
+      const int cnt = a.reccnt[row];
+      if (cnt < a.rmax) a.reclist[row * a.rmax + cnt] = pos;
+      a.reccnt[row] = cnt + 1;
     }
   }
 }
@@ -510,7 +530,9 @@ extern "C" int oa_index_update(const void* K, const void* V, int64_t B, int64_t 
               static_cast<const __nv_bfloat16*>(W), colmean, cent, asg, nb, Sk, Sk2, Sv, reclist, reccnt, rmax,
               static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<__nv_bfloat16*>(zq), n_dev,
               (int)Lmax, (int)C};
-  index_update_kernel<<<(unsigned)(B * kHKV), 128, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  const size_t smem = (size_t)std::min<int64_t>(C, kIuCentCache) * kRC * sizeof(float);
+  OA_REQUIRE(oa_aligned16(cent) && oa_aligned16(U) && oa_aligned16(W), "%s: U / W / cent must be 16-byte aligned", fn);
+  index_update_kernel<<<(unsigned)(B * kHQ), 128, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }
 
