@@ -392,6 +392,93 @@ __device__ __forceinline__ void warp_radix_select(int m, int q, int* hist, Get g
   T = ok ? prefix : 0u;
 }
 
+// ---- threshold + sort selection of the k largest unique 64-bit words held by a warp.  A word packs
+// (key << 32) | (0xffffffff - index), so "larger" means larger key, ties to the lower index.  The
+// k-th largest of the 32 lane maxima is a lower bound T0 of the answer (at least k words reach it);
+// the words >= T0 are compacted (at most 64, else the caller falls back to the radix select) and
+// sorted by a 64-element bitonic network in registers.
+__device__ __forceinline__ uint64_t shfl64(uint64_t v, int src) {
+  const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)v, src);
+  const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(v >> 32), src);
+  return ((uint64_t)hi << 32) | lo;
+}
+__device__ __forceinline__ uint64_t shfl64_xor(uint64_t v, int m) {
+  const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, m);
+  const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), m);
+  return ((uint64_t)hi << 32) | lo;
+}
+// descending bitonic sort of the 32 words v (one per lane)
+__device__ __forceinline__ uint64_t bitonic32_desc(uint64_t v) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j >= 1; j >>= 1) {
+      const uint64_t o = shfl64_xor(v, j);
+      const int l = lane ^ j;
+      const bool keep_max = ((lane & k) == 0) == (lane < l);
+      v = keep_max ? (o > v ? o : v) : (o < v ? o : v);
+    }
+  }
+  return v;
+}
+// descending bitonic sort of 64 words: element e = lane + 32 h lives in v[h] of lane e & 31
+__device__ __forceinline__ void bitonic64_desc(uint64_t (&v)[2]) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll
+  for (int k = 2; k <= 64; k <<= 1) {
+#pragma unroll
+    for (int j = k >> 1; j >= 1; j >>= 1) {
+      if (j == 32) {  // partners in the same lane
+        const bool keep_max = (lane & k) == 0;  // element lane (< lane + 32)
+        const uint64_t a = v[0], b = v[1];
+        v[0] = keep_max ? (a > b ? a : b) : (a < b ? a : b);
+        v[1] = keep_max ? (a > b ? b : a) : (a < b ? b : a);
+      } else {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int e = lane + 32 * h;
+          const uint64_t o = shfl64_xor(v[h], j);
+          const bool keep_max = ((e & k) == 0) == (e < (e ^ j));
+          v[h] = keep_max ? (o > v[h] ? o : v[h]) : (o < v[h] ? o : v[h]);
+        }
+      }
+    }
+  }
+}
+// Top k (k <= 32) of the m words word(i), i < m (0 = no word).  On success, sorted[0..1] hold the
+// 64 largest survivors in descending order (element e = lane + 32 h) and kth the k-th largest.
+template <typename Word>
+__device__ __forceinline__ bool warp_topk_sorted(int m, int k, Word word, uint64_t* sbuf, uint64_t (&sorted)[2],
+                                                 uint64_t& kth) {
+  const int lane = threadIdx.x & 31;
+  const unsigned lt = (1u << lane) - 1u;
+  if (k < 1 || k > 32) return false;
+  uint64_t lm = 0ull;
+  for (int i = lane; i < m; i += 32) {
+    const uint64_t w = word(i);
+    lm = w > lm ? w : lm;
+  }
+  const uint64_t T0 = shfl64(bitonic32_desc(lm), k - 1);
+  if (T0 == 0ull) return false;  // fewer than k words
+  int cnt = 0;
+  for (int i0 = 0; i0 < m; i0 += 32) {
+    const int i = i0 + lane;
+    const uint64_t w = i < m ? word(i) : 0ull;
+    const unsigned b = __ballot_sync(0xffffffffu, w >= T0 && w != 0ull);
+    if (w >= T0 && w != 0ull && cnt + __popc(b & lt) < 64) sbuf[cnt + __popc(b & lt)] = w;
+    cnt += __popc(b);
+  }
+  if (cnt > 64) return false;
+  __syncwarp();
+  sorted[0] = lane < cnt ? sbuf[lane] : 0ull;
+  sorted[1] = lane + 32 < cnt ? sbuf[lane + 32] : 0ull;
+  __syncwarp();
+  bitonic64_desc(sorted);
+  kth = shfl64(k > 32 ? sorted[1] : sorted[0], (k - 1) & 31);
+  return true;
+}
+
 __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const SelectArgs a) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.x * kSelWarps + warp;
@@ -399,6 +486,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   __shared__ int s_tiles[kSelWarps][kMaxKT2];
   __shared__ int s_pos[kSelWarps][64];
   __shared__ uint32_t s_key[kSelWarps][64];
+  __shared__ uint64_t s_w64[kSelWarps][64];
   extern __shared__ __align__(16) unsigned char sel_smem[];
   // per warp: tile keys (NT uint32), then candidate keys (kt2_max * 256 uint16)
   uint32_t* tkey = reinterpret_cast<uint32_t*>(sel_smem) + (size_t)warp * a.NT_pad;
@@ -414,7 +502,19 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   uint16_t* srw = a.scores + (int64_t)r * a.sw;
   for (int i = lane; i < ntv; i += 32) tkey[i] = fkey(tm[i]);
   __syncwarp();
-  // (1) tiles
+  // (1) tiles: threshold + sort when it applies, else the radix select
+  uint64_t srt[2], kth;
+  auto tword = [&](int i) -> uint64_t { return ((uint64_t)tkey[i] << 32) | (uint64_t)(0xffffffffu - (uint32_t)i); };
+  if (warp_topk_sorted(ntv, kt2, tword, s_w64[warp], srt, kth)) {
+    int taken = 0;
+    for (int i0 = 0; i0 < ntv; i0 += 32) {  // the kt2 tiles with word >= kth, in ascending tile order
+      const int i = i0 + lane;
+      const bool take = i < ntv && tword(i) >= kth;
+      const unsigned bt = __ballot_sync(0xffffffffu, take);
+      if (take) tiles[taken + __popc(bt & ((1u << lane) - 1u))] = i;
+      taken += __popc(bt);
+    }
+  } else {
   uint32_t Tt;
   int above_t;
   warp_radix_select<32>(ntv, kt2, hist, [&](int i, bool& v, uint32_t& k) { v = true; k = tkey[i]; }, Tt, above_t);
@@ -432,6 +532,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
       taken += __popc(bt);
       ties += __popc(beq);
     }
+  }
   }
   __syncwarp();
   // (2) candidate keys of the chosen tiles (ascending tile order) staged with 16-byte loads;
@@ -452,6 +553,25 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
     k = ckey[i];
     v = k != 0u;
   };
+  // candidate i is tile tiles[i >> 5], offset i & 31: ascending i is ascending position
+  auto cword = [&](int i) -> uint64_t {
+    const uint32_t k = ckey[i];
+    return k ? ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - (uint32_t)i) : 0ull;
+  };
+  int32_t* outp = a.sel + (int64_t)r * (a.ns + a.nl + a.k_top);
+  if (warp_topk_sorted(m, a.k_top, cword, s_w64[warp], srt, kth)) {
+    // the k winners, already in rank order (score desc, position asc)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int e = lane + 32 * h;
+      if (e < a.k_top) {
+        const int i = (int)(0xffffffffu - (uint32_t)srt[h]);
+        s_pos[warp][e] = tiles[i >> 5] * kMaxTile + (i & (kMaxTile - 1));
+      }
+    }
+    __syncwarp();
+    for (int j = lane; j < a.k_top; j += 32) outp[a.ns + a.nl + j] = s_pos[warp][j];
+  } else {
   uint32_t T;
   int above;
   warp_radix_select<16>(m, a.k_top, hist, cand, T, above);
@@ -483,7 +603,6 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   }
   __syncwarp();
   // (3) rank order (score desc, position asc)
-  int32_t* out = a.sel + (int64_t)r * (a.ns + a.nl + a.k_top);
   for (int j = lane; j < a.k_top; j += 32) {
     const uint32_t kj = s_key[warp][j];
     const int pj = s_pos[warp][j];
@@ -493,7 +612,8 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
       const int pi = s_pos[warp][i];
       rank += (ki > kj || (ki == kj && pi < pj)) ? 1 : 0;
     }
-    out[a.ns + a.nl + rank] = pj;
+    outp[a.ns + a.nl + rank] = pj;
+  }
   }
   __syncwarp();
   for (int j = lane; j < a.k_top; j += 32) {
@@ -502,7 +622,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   }
   for (int i = lane; i < a.ns + a.nl; i += 32) {
     const int t = i < a.ns ? i : n - a.nl + (i - a.ns);
-    out[i] = t;
+    outp[i] = t;
     if (t >= 0 && t < a.Lmax) srw[t] = 0xff80u;
   }
 }

@@ -1,0 +1,92 @@
+"""The QGS row top-k (qgs_select) and the within-cluster top-q (topq) through the C ABI against the
+oracle on crafted score rows: random scores; all-equal scores (every choice is a tie, decided by the
+lower position); and skewed rows whose large values sit in the tiles and in-tile offsets that one
+half of a warp's lanes read, so the kernel's threshold pre-filter overflows and its radix select
+runs.  k from 1 to 40 (above 32 the radix select always runs).  Bit-exact."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import cases
+import oracle as O
+from helpers import state_from_fixture, to_gpu_state, to_np
+from openattention_b200 import selection as S
+from openattention_b200.geometry import HQ
+
+pytestmark = pytest.mark.gpu
+NEG = 0xFF80
+
+
+def _bits(v):
+    return O.bits(torch.from_numpy(np.ascontiguousarray(v, np.float32)).to(torch.bfloat16))
+
+
+def _rows(kind, R, n, seed):
+    rng = np.random.default_rng(seed)
+    if kind == "random":
+        v = rng.standard_normal((R, n)).astype(np.float32) * 3
+    elif kind == "equal":
+        v = np.full((R, n), 1.5, np.float32)
+    else:  # skewed: tiles t % 32 < 16 and in-tile offsets < 16 hold the large values
+        v = rng.standard_normal((R, n)).astype(np.float32) * 0.1
+        t = np.arange(n)
+        hot = ((t // 32) % 32 < 16) & (t % 32 < 16)
+        v[:, hot] += 10 + rng.standard_normal((R, int(hot.sum()))).astype(np.float32)
+    return _bits(v)
+
+
+@pytest.mark.parametrize("kind", ["random", "equal", "skewed"])
+@pytest.mark.parametrize("k_top", [1, 9, 31, 40])
+def test_select_matches_oracle(kind, k_top):
+    R, n, ns, nl, Lmax = 64, 4101, 3, 3, 4160
+    SW = S.padded_len(Lmax)
+    NT = (Lmax + 31) // 32
+    s = np.full((R, SW), NEG, np.uint16)
+    s[:, :n] = _rows(kind, R, n, 7 + k_top)
+    s[:, :ns] = NEG
+    s[:, n - nl:n] = NEG
+    tmax = O.bf16_to_f32(s[:, :NT * 32].reshape(R, NT, 32)).max(axis=2).astype(np.float32)
+    ref = s.copy()
+    sel_ref = O.select(ref, n, ns, nl, k_top)
+    scores = O.from_bits(s).cuda()
+    sel = torch.empty(R, ns + nl + k_top, dtype=torch.int32, device="cuda")
+    n_dev = torch.tensor([n], dtype=torch.int32, device="cuda")
+    S.qgs_select(scores, torch.from_numpy(tmax).cuda(), Lmax, n_dev, ns, nl, k_top, sel)
+    torch.cuda.synchronize()
+    assert np.array_equal(sel.cpu().numpy(), sel_ref)
+    assert np.array_equal(to_np(scores), ref)
+
+
+@pytest.mark.parametrize("kind", ["random", "equal"])
+def test_topq_matches_oracle_with_ties(golden_dir, kind):
+    """Top-q over a fixture's CSR lists with crafted scores and quotas (up to 4 per cluster)."""
+    x = cases.decode_inputs("decode_c0")
+    z = np.load(os.path.join(golden_dir, "decode_c0.npz"))
+    st_np, K, V = state_from_fixture(x, z)
+    B, n0, Lmax = x["B"], x["n0"], x["Lmax"]
+    C = st_np["nb"].shape[-1]
+    E, R = 216, B * HQ
+    n = n0  # no generated tokens
+    SW = S.padded_len(Lmax)
+    s = np.full((R, SW), NEG, np.uint16)
+    s[:, :n] = _rows(kind, R, n, 11)
+    clen = st_np["clen"].reshape(R, C)
+    quota = np.zeros((R, C), np.float32)
+    for r in range(R):
+        left = E
+        for c in np.random.default_rng(r).permutation(C):
+            q = min(4, int(clen[r, c]), left)
+            quota[r, c] = q
+            left -= q
+    exp_ref = O.topq(s, st_np["asg"].reshape(R, -1), quota, n, E)
+    st = to_gpu_state(st_np)
+    exp_idx = torch.empty(R, E, dtype=torch.int32, device="cuda")
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    S.topq(O.from_bits(s).cuda(), st, torch.from_numpy(quota).cuda(), E,
+           torch.tensor([n], dtype=torch.int32, device="cuda"), torch.tensor([n0], dtype=torch.int32, device="cuda"),
+           exp_idx, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert np.array_equal(exp_idx.cpu().numpy(), exp_ref)
