@@ -282,6 +282,7 @@ def cpu_baseline_sample(m, Mth, qs, nks, nvs, budget_s=12.0):
     work; reported per bs32 layer-step (x32)."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    threads = use_all_host_threads(O)
     st_gpu = m.st[0]
     st = {}
     for k, v in st_gpu.items():
@@ -306,9 +307,9 @@ def cpu_baseline_sample(m, Mth, qs, nks, nvs, budget_s=12.0):
         times.append(time.perf_counter() - t0)
         steps += 1
     per_req = statistics.median(times)
-    return {"value": per_req * 1e6 * B_PER_GPU, "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+    return {"value": per_req * 1e6 * B_PER_GPU, "unit": UNIT, "cores": threads, "kind": "port",
             "sample": f"{steps} decode steps of 1 request (n~{N_CTX}, 1% read), median x {B_PER_GPU} requests; "
-                      f"oracle/oa_oracle.c with OpenMP on {os.cpu_count()} threads"}
+                      f"oracle/oa_oracle.c with OpenMP on {threads} threads"}
 
 
 def run_ours(a):
@@ -442,12 +443,19 @@ def run_ours(a):
 
 
 # ------------------------------------------------------------------ reference arm (CPU)
+def use_all_host_threads(O):
+    """The CPU legs use every host core (torchrun sets OMP_NUM_THREADS=1 per rank).  Returns the
+    thread count in effect."""
+    return O.set_threads(os.cpu_count() or 1)
+
+
 def run_reference(a):
     rank, world, local = dist_env()
     if rank != 0:
         return None
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
+    threads = use_all_host_threads(O)
     from openattention_b200 import synth
     from openattention_b200.geometry import HQ, budget
     C, E = budget(RHO)
@@ -484,7 +492,7 @@ def run_reference(a):
         if s >= a.warmup:
             times.append(time.perf_counter() - t0)
     per = statistics.median(times) / B_s * B_PER_GPU * 1e6
-    cores = os.cpu_count()
+    cores = threads
     sample = (f"{a.steps} timed decode steps of {B_s} request(s) at n={N_CTX}, 1% read (C={C}, E={E}); median "
               f"scaled x{B_PER_GPU // B_s} to bs32; build {t_build:.1f} s untimed")
     return {"metric": METRIC, "value": round(per, 1), "unit": UNIT, "n_gpus": world, "steps": a.steps,

@@ -51,6 +51,15 @@ def lib():
     return _lib
 
 
+def set_threads(n: int) -> int:
+    """OpenMP threads of the oracle's parallel loops (its runtime may already be initialised by the
+    host process, so the environment variable alone is not enough).  Returns the count in effect."""
+    L = lib()
+    L.omp_set_num_threads(ctypes.c_int(max(1, int(n))))
+    L.omp_get_max_threads.restype = ctypes.c_int
+    return int(L.omp_get_max_threads())
+
+
 def _p(a):
     return ctypes.c_void_p(0) if a is None else a.ctypes.data_as(ctypes.c_void_p)
 
