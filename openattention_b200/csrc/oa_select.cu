@@ -11,6 +11,7 @@
 // limb partial sums recombine into the exact int64 dot product, which is rounded once to fp32 and
 // once to bf16.  The result does not depend on summation order.
 #include "oa_common.cuh"
+#include "oa_warp.cuh"
 #include "../../include/openattention_b200.h"
 
 namespace oa {
@@ -390,93 +391,6 @@ __device__ __forceinline__ void warp_radix_select(int m, int q, int* hist, Get g
     pmask |= 0xffu << shift;
   }
   T = ok ? prefix : 0u;
-}
-
-// ---- threshold + sort selection of the k largest unique 64-bit words held by a warp.  A word packs
-// (key << 32) | (0xffffffff - index), so "larger" means larger key, ties to the lower index.  The
-// k-th largest of the 32 lane maxima is a lower bound T0 of the answer (at least k words reach it);
-// the words >= T0 are compacted (at most 64, else the caller falls back to the radix select) and
-// sorted by a 64-element bitonic network in registers.
-__device__ __forceinline__ uint64_t shfl64(uint64_t v, int src) {
-  const uint32_t lo = __shfl_sync(0xffffffffu, (uint32_t)v, src);
-  const uint32_t hi = __shfl_sync(0xffffffffu, (uint32_t)(v >> 32), src);
-  return ((uint64_t)hi << 32) | lo;
-}
-__device__ __forceinline__ uint64_t shfl64_xor(uint64_t v, int m) {
-  const uint32_t lo = __shfl_xor_sync(0xffffffffu, (uint32_t)v, m);
-  const uint32_t hi = __shfl_xor_sync(0xffffffffu, (uint32_t)(v >> 32), m);
-  return ((uint64_t)hi << 32) | lo;
-}
-// descending bitonic sort of the 32 words v (one per lane)
-__device__ __forceinline__ uint64_t bitonic32_desc(uint64_t v) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int k = 2; k <= 32; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j >= 1; j >>= 1) {
-      const uint64_t o = shfl64_xor(v, j);
-      const int l = lane ^ j;
-      const bool keep_max = ((lane & k) == 0) == (lane < l);
-      v = keep_max ? (o > v ? o : v) : (o < v ? o : v);
-    }
-  }
-  return v;
-}
-// descending bitonic sort of 64 words: element e = lane + 32 h lives in v[h] of lane e & 31
-__device__ __forceinline__ void bitonic64_desc(uint64_t (&v)[2]) {
-  const int lane = threadIdx.x & 31;
-#pragma unroll
-  for (int k = 2; k <= 64; k <<= 1) {
-#pragma unroll
-    for (int j = k >> 1; j >= 1; j >>= 1) {
-      if (j == 32) {  // partners in the same lane
-        const bool keep_max = (lane & k) == 0;  // element lane (< lane + 32)
-        const uint64_t a = v[0], b = v[1];
-        v[0] = keep_max ? (a > b ? a : b) : (a < b ? a : b);
-        v[1] = keep_max ? (a > b ? b : a) : (a < b ? b : a);
-      } else {
-#pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          const int e = lane + 32 * h;
-          const uint64_t o = shfl64_xor(v[h], j);
-          const bool keep_max = ((e & k) == 0) == (e < (e ^ j));
-          v[h] = keep_max ? (o > v[h] ? o : v[h]) : (o < v[h] ? o : v[h]);
-        }
-      }
-    }
-  }
-}
-// Top k (k <= 32) of the m words word(i), i < m (0 = no word).  On success, sorted[0..1] hold the
-// 64 largest survivors in descending order (element e = lane + 32 h) and kth the k-th largest.
-template <typename Word>
-__device__ __forceinline__ bool warp_topk_sorted(int m, int k, Word word, uint64_t* sbuf, uint64_t (&sorted)[2],
-                                                 uint64_t& kth) {
-  const int lane = threadIdx.x & 31;
-  const unsigned lt = (1u << lane) - 1u;
-  if (k < 1 || k > 32) return false;
-  uint64_t lm = 0ull;
-  for (int i = lane; i < m; i += 32) {
-    const uint64_t w = word(i);
-    lm = w > lm ? w : lm;
-  }
-  const uint64_t T0 = shfl64(bitonic32_desc(lm), k - 1);
-  if (T0 == 0ull) return false;  // fewer than k words
-  int cnt = 0;
-  for (int i0 = 0; i0 < m; i0 += 32) {
-    const int i = i0 + lane;
-    const uint64_t w = i < m ? word(i) : 0ull;
-    const unsigned b = __ballot_sync(0xffffffffu, w >= T0 && w != 0ull);
-    if (w >= T0 && w != 0ull && cnt + __popc(b & lt) < 64) sbuf[cnt + __popc(b & lt)] = w;
-    cnt += __popc(b);
-  }
-  if (cnt > 64) return false;
-  __syncwarp();
-  sorted[0] = lane < cnt ? sbuf[lane] : 0ull;
-  sorted[1] = lane + 32 < cnt ? sbuf[lane + 32] : 0ull;
-  __syncwarp();
-  bitonic64_desc(sorted);
-  kth = shfl64(k > 32 ? sorted[1] : sorted[0], (k - 1) & 31);
-  return true;
 }
 
 __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const SelectArgs a) {
