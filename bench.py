@@ -1,7 +1,8 @@
 #!/usr/bin/env python3
 """Decode-attention-stage benchmark of the OpenAttention deployed path on B200 (BASELINE config c2).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B] [--ctx N]
+    python bench.py --sweep [--sweep-b 1,32] [--sweep-n 8192,131072]   (latency sweep, one line per point)
 
 Workload per GPU: B=32 requests, 32K-token bf16 KV caches (seeded synthetic, see
 openattention_b200/synth.py), 1% read (C=64, E=216), ONE layer's decode step: index update + QGS
@@ -442,6 +443,84 @@ def run_ours(a):
     return res
 
 
+# ------------------------------------------------------------------ latency sweep (config c3)
+SWEEP_B = (1, 4, 16, 32, 64)
+SWEEP_N = (8192, 16384, 32768, 65536, 131072)
+SWEEP_RHO = (0.01, 0.05)
+
+
+def sweep_point(dev, B, n0, rho, steps, warmup):
+    """One point of the latency sweep: one request of n0 tokens is built and replicated B times (the
+    per-request work does not depend on which request it is), then `steps` graph-replayed decode
+    steps are timed with CUDA events (inputs larger than L2 from B = 4 on; at B = 1 the step
+    reads about 16 MB per step and the number is a latency)."""
+    from openattention_b200 import method as Mth
+    from openattention_b200 import synth
+    from openattention_b200.geometry import HQ
+    total = warmup + steps + 4
+    Lmax = n0 + total + 16
+    K1, V1, mus = synth.kv_torch(41, 1, n0, Lmax, dev)
+    K = K1.expand(B, -1, -1, -1).contiguous()
+    V = V1.expand(B, -1, -1, -1).contiguous()
+    del K1, V1
+    Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40] * B
+    m = Mth.OursB200(types.SimpleNamespace(rho=rho), B, Lmax, dev, layers=1)
+    g = torch.Generator(device=dev)
+    g.manual_seed(43)
+    qpre = torch.zeros(1, HQ, n0, 128, dtype=torch.bfloat16, device=dev)
+    qpre[:, :, n0 - 64:] = torch.randn(1, HQ, 64, 128, generator=g, device=dev).to(torch.bfloat16)
+    m.build(0, 0, qpre, n0)
+    del qpre
+    for k, v in m.st[0].items():
+        if k in ("reclist", "reccnt"):
+            v.zero_()
+        v[1:].copy_(v[0:1].expand_as(v[1:]))
+    gs = GraphStep(m, Mth, n0, dev)
+    qs = torch.randn(total, B, HQ, 1, 128, generator=g, device=dev).to(torch.bfloat16)
+    nk, nv = synth.new_tokens_torch(45, mus.expand(B, *mus.shape[1:]).contiguous(), n0)
+    for s in range(warmup):
+        gs.q_in.copy_(qs[s])
+        gs.k_in.copy_(nk)
+        gs.v_in.copy_(nv)
+        gs.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for s in range(steps):
+        gs.q_in.copy_(qs[warmup + s])
+        gs.k_in.copy_(nk)
+        gs.v_in.copy_(nv)
+        gs.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    R, Rkv, C, E = B * HQ, B * 8, m.C, m.E
+    n = int(Mth.C.n_dev.item())
+    from openattention_b200.geometry import step_split
+    ns, nl, k_top = step_split(gs.n_host, rho, C, E)
+    NS = ns + nl + k_top
+    reads = int((m.exp_idx >= 0).sum().item()) + R * NS
+    alg = (Rkv * n * 32 + 3 * R * C * 128 * 4 + reads * 512 + R * C * 4 + R * (NS + E) * 4 + 2 * R * 256
+           + R * (128 * 16 * 2 + C * 16 * 4) + Rkv * 128 * 32 * 4)
+    del gs, m, K, V
+    torch.cuda.empty_cache()
+    return {"sweep": "c3", "B": B, "n": n0, "rho": rho, "C": C, "E": E, "us_per_step": round(ms * 1e3, 2),
+            "alg_bytes": alg, "achieved_gbs": round(alg / (ms * 1e-3) / 1e9, 1),
+            "frac": round(alg / (ms * 1e-3) / 1e9 / peaks()[0], 4)}
+
+
+def run_sweep(a):
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    Bs = [int(x) for x in a.sweep_b.split(",")] if a.sweep_b else SWEEP_B
+    Ns = [int(x) for x in a.sweep_n.split(",")] if a.sweep_n else SWEEP_N
+    for rho in SWEEP_RHO:
+        for n0 in Ns:
+            for B in Bs:
+                print(json.dumps(sweep_point(dev, B, n0, rho, a.steps, a.warmup)), flush=True)
+    return None
+
+
 # ------------------------------------------------------------------ reference arm (CPU)
 def use_all_host_threads(O):
     """The CPU legs use every host core (torchrun sets OMP_NUM_THREADS=1 per rank).  Returns the
@@ -507,18 +586,28 @@ def run_reference(a):
 
 
 def main():
-    global B_PER_GPU
+    global B_PER_GPU, N_CTX
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--sweep", action="store_true",
+                    help="latency sweep of the decode step over batch x context x read (one JSON line per point)")
+    ap.add_argument("--sweep-b", default="", help="comma list of batches for --sweep")
+    ap.add_argument("--sweep-n", default="", help="comma list of contexts for --sweep")
+    ap.add_argument("--ctx", type=int, default=N_CTX,
+                    help="context length (default 32768, the benchmark config; others only for profiling)")
     ap.add_argument("--batch", type=int, default=B_PER_GPU,
                     help="requests per GPU (default 32, the benchmark config; smaller only for profiling)")
     a = ap.parse_args()
     B_PER_GPU = a.batch
+    N_CTX = a.ctx
     if a.warmup < 3:
         a.warmup = 3
+    if a.sweep:
+        run_sweep(a)
+        return
     res = run_reference(a) if a.impl == "reference" else run_ours(a)
     if res is not None:
         print(json.dumps(res), flush=True)

@@ -280,3 +280,46 @@ def test_decode_32k_steps_bit_exact(rho):
     if C == 64:
         assert big > 512, f"largest cluster {big}: the wider register paths must be reached"
     assert int(m.status.item()) == 0
+
+
+@pytest.mark.parametrize("B,n0,rho", [(1, 131072, 0.05), (2, 65536, 0.01), (4, 8192, 0.05)])
+def test_decode_sweep_shapes_bit_exact(B, n0, rho):
+    """Extreme points of the latency sweep (contexts 8K..128K, 1% and 5% read): a GPU-built state,
+    then decode steps checked against the oracle.  At 128K the score row no longer fits shared memory
+    (top-q reads its keys from global memory); at 5% the read lists are long (E = 1335, C = 192)."""
+    from openattention_b200 import synth
+    dev = torch.device("cuda")
+    steps = 3
+    Lmax = n0 + steps + 8
+    K, V, mus = synth.kv_torch(31 + B, B, n0, Lmax, dev)
+    Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40] * B
+    m = _method(B, Lmax, rho)
+    C, E, R = m.C, m.E, B * HQ
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    qpre = torch.zeros(1, HQ, n0, D, dtype=torch.bfloat16, device=dev)
+    qpre[:, :, n0 - 64:] = torch.randn(1, HQ, 64, D, generator=g, device=dev).to(torch.bfloat16)
+    for b in range(B):
+        m.build(0, b, qpre, n0)
+    Mth.C.n_dev = None
+    Mth.C.n0_dev = torch.tensor([n0], dtype=torch.int32, device=dev)
+    st_np = {k: (O.bits(v) if v.dtype == torch.bfloat16 else v.cpu().numpy()).copy() for k, v in m.st[0].items()}
+    Kn, Vn = O.bits(K).copy(), O.bits(V).copy()
+    out = torch.empty(R, D, dtype=torch.float32, device=dev)
+    for s in range(steps):
+        n = n0 + s + 1
+        nk, nv = synth.new_tokens_torch(700 + s, mus, n - 1)
+        K[:, :, n - 1], V[:, :, n - 1] = nk, nv
+        Kn[:, :, n - 1], Vn[:, :, n - 1] = O.bits(nk), O.bits(nv)
+        q = torch.randn(B, HQ, 1, D, generator=g, device=dev).to(torch.bfloat16)
+        qr, sel = m.select(0, q, n, residual=False)
+        S.residual_flash(qr, K, V, m.st[0], sel, m.exp_idx, m.nt, m.quota, out, status=m.status)
+        torch.cuda.synchronize()
+        o = O.decode_step(st_np, O.bits(q.reshape(R, D)), Kn, Vn, n, rho, C, E)
+        _eq(f"step{s}.sel", sel, o["sel"])
+        _eq(f"step{s}.quota", m.quota, o["quota"])
+        _eq(f"step{s}.exp_idx", m.exp_idx, o["exp_idx"])
+        got = out.cpu().double().numpy()
+        assert np.abs(got - o["out"]).max() <= 2e-3
+        assert np.linalg.norm(got - o["out"]) <= 1e-3 * np.linalg.norm(o["out"])
+    assert int(m.status.item()) == 0
