@@ -1377,7 +1377,8 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
   for (int c = tid; c < C; c += kPF) {
     const float nr = __fsub_rn(a.nt[rowC + c], S.w[c]);
     S.inv[c] = nr > 0.5f ? __fdiv_rn(1.f, fmaxf(nr, 1.f)) : 0.f;
-    S.zc[c] = nr > 0.5f ? ln_f(fmaxf(nr, 1.f)) * kLog2e : -INFINITY;  // ln n' term, completed below
+    // log2 n' (the output is held to the estimator's tolerance, not to the proxies' bits)
+    S.zc[c] = nr > 0.5f ? __log2f(fmaxf(nr, 1.f)) : -INFINITY;  // completed below
   }
   __syncthreads();
   const __nv_bfloat16* Kr = a.K + (int64_t)kv * a.Lmax * kD + hl * 8;
@@ -1416,18 +1417,17 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
     }
   }
   __syncthreads();
-  // ---- proxy logits: q.dk_c summed over the cluster's read tokens in a fixed order
-  for (int c = warp; c < C; c += kPF / 32) {
-    if (!(S.inv[c] > 0.f)) continue;  // warp-uniform
+  // ---- proxy logits: one thread per cluster sums q.dk_c over the cluster's read tokens in a fixed
+  //      order (selected tokens in list order, then its slot segment)
+  for (int c = tid; c < C; c += kPF) {
+    if (!(S.inv[c] > 0.f)) continue;
     float part = 0.f;
-    for (int j = lane; j < NS; j += 32)
+    for (int j = 0; j < NS; ++j)
       if (S.cl[j] == c) part += S.z[j];
     const int e0 = NS + S.base[c], e1 = NS + min(S.base[c + 1], a.E);
-    for (int j = e0 + lane; j < e1; j += 32)
+    for (int j = e0; j < e1; ++j)
       if (S.tok[j] >= 0) part += S.z[j];
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
-    if (lane == 0) S.zc[c] = fmaf(__fmul_rn(__fsub_rn(S.qsk[c], part), S.inv[c]), a.qk_scale, S.zc[c]);
+    S.zc[c] = fmaf(__fmul_rn(__fsub_rn(S.qsk[c], part), S.inv[c]), a.qk_scale, S.zc[c]);
   }
   __syncthreads();
   // ---- softmax normaliser: max over token and proxy logits, then weights
