@@ -252,10 +252,10 @@ def stage_profile(m, Mth, gs, iters):
         "qgs_select_kernel": timed(lambda: S.qgs_select(m.scores, m.tmax, m.Lmax, n_dev, ns, nl, k_top, sel),
                                    prep=lambda: m.scores.copy_(scores_snap)),
         "errorgate_waterfill_kernel": timed(lambda: S.errorgate_waterfill(qr, K, st, sel, E, m.score, m.nt, m.quota,
-                                                                          m.status)),
+                                                                          m.status, zdot=m.zdot)),
         "topq_stream_kernel": timed(lambda: S.topq(m.scores, st, m.quota, E, n_dev, n0_dev, m.exp_idx, m.status)),
         "proxy_flash_kernel": timed(lambda: S.residual_flash(qr, K, V, st, sel, m.exp_idx, m.nt, m.quota, m.out,
-                                                                status=m.status)),
+                                                                status=m.status, zdot=m.zdot)),
     }
     # data-dependent byte counts of this step
     quota = m.quota.view(B, HQ, C)
@@ -266,9 +266,9 @@ def stage_profile(m, Mth, gs, iters):
         "index_update_kernel": R * (D * 16 * 2 + C * 16 * 4 + 3 * D * 4 * 2 + D * 2) + Rkv * (D * 32 * 4 + 2 * D * 2),
         "qgs_scan_kernel": Rkv * n * 32,
         "qgs_select_kernel": R * (nt_tiles * 4 + NS * 4),
-        "errorgate_waterfill_kernel": R * (2 * C * D * 4 + C * 4 + NS * (D * 2 + 4) + D * 2 + 3 * C * 4),
+        "errorgate_waterfill_kernel": R * (2 * C * D * 4 + C * 4 + NS * (D * 2 + 4) + D * 2 + 4 * C * 4),
         "topq_stream_kernel": members * 6 + R * (2 * C * 4 + E * 4),
-        "proxy_flash_kernel": reads * 2 * D * 2 + R * (2 * C * D * 4 + 2 * C * 4 + (NS + E) * 4 + 2 * D * 2),
+        "proxy_flash_kernel": reads * 2 * D * 2 + R * (C * D * 4 + 3 * C * 4 + (NS + E) * 4 + 2 * D * 2),
     }
     # the whole step's algorithmic bytes: codes, the three fp32 sum arrays once, the read rows, the small
     # per-row arrays, the index-update operands and the chosen clusters' member lists

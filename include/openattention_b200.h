@@ -144,13 +144,15 @@ int oa_qgs_select(void* scores, int64_t score_stride, const float* tile_max, int
 /* ErrorGate (wl1) + hierarchical water-filling per row: tail statistics (pooled sums minus the
  * selected tokens), score = zbar + ln n + s2/2 + ln erf(sqrt(s2/2)), quotas q_b = min(n_b,
  * floor(lambda w_b)) plus leftover whole tokens to the best-scoring clusters with room.
- * Outputs score, nt (tail counts) and quota, each (B*32, C) fp32.  Replaces _k_errorgate +
- * _k_waterfill (inference/ours_fused.py:122-216).  C <= 256, n_sel <= 512.  status (may be NULL):
- * device int32 set to 2 if a bulk copy of the pooled sums did not complete in the bounded wait. */
+ * Outputs score, nt (tail counts) and quota, each (B*32, C) fp32; zdot (may be NULL): the unscaled
+ * dot q . kbar_b of each cluster's tail mean (the value zbar is formed from), which
+ * oa_residual_flash can use instead of re-reading Sk.  Replaces _k_errorgate + _k_waterfill
+ * (inference/ours_fused.py:122-216).  C <= 256, n_sel <= 512.  Sk and Sk2 16-byte aligned.
+ * status (may be NULL): device int32, unused by this entry (kept for a uniform stage signature). */
 int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64_t B, int64_t Lmax, int64_t C,
                            const int32_t* asg, const int32_t* sel, int64_t n_sel, const float* Sk, const float* Sk2,
-                           const float* nb, float E, float* score, float* nt, float* quota, int32_t* status,
-                           void* stream);
+                           const float* nb, float E, float* score, float* nt, float* quota, float* zdot,
+                           int32_t* status, void* stream);
 
 /* Within-cluster top-q: for each cluster with quota q > 0, its q best members by QGS score (the
  * selected tokens are already -inf), ties -> lower position, written to exp_idx (R, E) int32 at the
@@ -174,17 +176,22 @@ int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C
                 const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar, float* log_n,
                 int32_t* status, void* stream);
 
-/* Residual proxies and OpenAttention.flash in one pass (per-query-head proxies, the deployed
- * combination of oa_residual + oa_flash_qhead_proxies): the read tokens' K/V rows are gathered once
- * and used both for the pooled-sum subtraction and for the online softmax; the bf16-rounded proxies
- * are attended from on-chip memory.  kbar / vbar / log_n outputs may be NULL (then not written).
- * Inputs as oa_residual; out (B*32, 128) bf16 or fp32 (out_dtype) with row stride out_stride.
- * status: as oa_errorgate_waterfill (value 5). */
+/* Residual proxies and OpenAttention.flash in one kernel (per-query-head proxies: the deployed
+ * combination of oa_residual + oa_flash_qhead_proxies).  Inputs as oa_residual; out (B*32, 128)
+ * bf16 or fp32 (out_dtype) with row stride out_stride.
+ *  - kbar, vbar and log_n all NULL (the deployed step): the proxies are folded into the flash pass.
+ *    For a live cluster, q . kbar'_b = (q . Sk_b - sum of its read tokens' q . k) / n'_b needs only
+ *    scalar sums of the token dots, and the value side is sum_t (p_t - w_b(t)) v_t + sum_b w_b Sv_b
+ *    with w_b = p_b / n'_b.  The proxies are the fp32 estimator's (un-rounded).  zdot (may be NULL):
+ *    oa_errorgate_waterfill's zdot for this step; then q . Sk_b is taken from it and Sk is not read.
+ *  - kbar / vbar (and optionally log_n) given: the bf16 proxies are formed exactly as oa_residual
+ *    forms them (bit-identical), written, and attended; zdot is ignored.
+ * status (may be NULL): device int32, unused by this entry. */
 int oa_residual_flash(const void* q, int64_t q_stride, const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C,
                       const int32_t* asg, const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E,
-                      const float* Sk, const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar,
-                      float* log_n, void* out, int64_t out_stride, int out_dtype, float sm_scale, int32_t* status,
-                      void* stream);
+                      const float* Sk, const float* Sv, const float* nt, const float* quota, const float* zdot,
+                      void* kbar, void* vbar, float* log_n, void* out, int64_t out_stride, int out_dtype,
+                      float sm_scale, int32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
  * Per-request build (prefill).  Each call works on ONE request: K, V (8, Lmax, 128) bf16 with the

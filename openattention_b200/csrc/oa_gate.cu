@@ -46,6 +46,7 @@ struct GateArgs {
   float* score;
   float* nt;
   float* quota;
+  float* zdot;  // may be null
   int32_t* status;
 };
 
@@ -356,6 +357,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
     a.quota[rC + c] = __fadd_rn(S.qb[c], add);
     a.nt[rC + c] = S.nt[c];
     a.score[rC + c] = S.score[c];
+    if (a.zdot != nullptr) a.zdot[rC + c] = S.zd[c];
   }
 }
 
@@ -1008,6 +1010,7 @@ struct ResidArgs {
   const float* Sv;
   const float* nt;
   const float* quota;
+  const float* zdot;    // may be null; proxy_flash_kernel then reads Sk
   __nv_bfloat16* kbar;  // may be null (then not written)
   __nv_bfloat16* vbar;
   float* logn;
@@ -1400,7 +1403,12 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
     }
   }
   const float* Skr = a.Sk + rowC * kD + hl * 8;
-  for (int c0 = hw; c0 < C; c0 += kPFHalf * 4) {
+  if (a.zdot != nullptr) {
+    // q . (Sk_b - selected tokens) = zdot_b * n_t(b): the tail mean's dot from the ErrorGate pass
+    for (int c = tid; c < C; c += kPF)
+      if (S.inv[c] > 0.f) S.qsk[c] = __fmul_rn(a.zdot[rowC + c], a.nt[rowC + c]);
+  }
+  for (int c0 = hw; a.zdot == nullptr && c0 < C; c0 += kPFHalf * 4) {
     float4 x[4], y[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
@@ -1422,8 +1430,9 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
   for (int c = tid; c < C; c += kPF) {
     if (!(S.inv[c] > 0.f)) continue;
     float part = 0.f;
-    for (int j = 0; j < NS; ++j)
-      if (S.cl[j] == c) part += S.z[j];
+    if (a.zdot == nullptr)  // with zdot the selected tokens are already out of the tail mean
+      for (int j = 0; j < NS; ++j)
+        if (S.cl[j] == c) part += S.z[j];
     const int e0 = NS + S.base[c], e1 = NS + min(S.base[c + 1], a.E);
     for (int j = e0; j < e1; ++j)
       if (S.tok[j] >= 0) part += S.z[j];
@@ -1532,7 +1541,7 @@ using namespace oa;
 extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64_t B, int64_t Lmax,
                                       int64_t C, const int32_t* asg, const int32_t* sel, int64_t n_sel,
                                       const float* Sk, const float* Sk2, const float* nb, float E, float* score,
-                                      float* nt, float* quota, int32_t* status, void* stream) {
+                                      float* nt, float* quota, float* zdot, int32_t* status, void* stream) {
   const char* fn = "oa_errorgate_waterfill";
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= kMaxC, "%s: need 0 < C <= %d (C=%lld)", fn, kMaxC, (long long)C);
   OA_REQUIRE(n_sel > 0 && n_sel <= 512, "%s: n_sel=%lld outside [1, 512]", fn, (long long)n_sel);
@@ -1540,7 +1549,7 @@ extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const voi
   OA_REQUIRE(E >= 0.f, "%s: negative budget", fn);
   OA_REQUIRE(oa_aligned16(Sk) && oa_aligned16(Sk2), "%s: Sk / Sk2 must be 16-byte aligned", fn);
   GateArgs a{static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(K), (int)Lmax, (int)C,
-             (int)n_sel, asg, sel, Sk, Sk2, nb, E, score, nt, quota, status};
+             (int)n_sel, asg, sel, Sk, Sk2, nb, E, score, nt, quota, zdot, status};
   const size_t smem = eg_smem_bytes((int)C, (int)n_sel);
   errorgate_waterfill_kernel<<<(unsigned)(B * kHQ), kEgThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
@@ -1597,7 +1606,7 @@ extern "C" int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax
              fn);
   OA_REQUIRE(oa_aligned16(K) && oa_aligned16(V), "%s: K / V must be 16-byte aligned", fn);
   ResidArgs a{nullptr, 0, static_cast<const __nv_bfloat16*>(K), static_cast<const __nv_bfloat16*>(V), (int)Lmax,
-              (int)C, (int)n_sel, (int)E, asg, sel, exp_idx, Sk, Sv, nt, quota, static_cast<__nv_bfloat16*>(kbar),
+              (int)C, (int)n_sel, (int)E, asg, sel, exp_idx, Sk, Sv, nt, quota, nullptr, static_cast<__nv_bfloat16*>(kbar),
               static_cast<__nv_bfloat16*>(vbar), logn, nullptr, 0, 0, 0.f, status};
   residual_kernel<false><<<(unsigned)(B * kHQ), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
@@ -1606,7 +1615,7 @@ extern "C" int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax
 extern "C" int oa_residual_flash(const void* q, int64_t q_stride, const void* K, const void* V, int64_t B, int64_t Lmax,
                                  int64_t C, const int32_t* asg, const int32_t* sel, int64_t n_sel,
                                  const int32_t* exp_idx, int64_t E, const float* Sk, const float* Sv, const float* nt,
-                                 const float* quota, void* kbar, void* vbar, float* logn, void* out,
+                                 const float* quota, const float* zdot, void* kbar, void* vbar, float* logn, void* out,
                                  int64_t out_stride, int out_dtype, float sm_scale, int32_t* status, void* stream) {
   const char* fn = "oa_residual_flash";
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
@@ -1617,7 +1626,7 @@ extern "C" int oa_residual_flash(const void* q, int64_t q_stride, const void* K,
   OA_REQUIRE(oa_aligned16(K) && oa_aligned16(V), "%s: K / V must be 16-byte aligned", fn);
   ResidArgs a{static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(K),
               static_cast<const __nv_bfloat16*>(V), (int)Lmax, (int)C, (int)n_sel, (int)E, asg, sel, exp_idx, Sk, Sv,
-              nt, quota, static_cast<__nv_bfloat16*>(kbar), static_cast<__nv_bfloat16*>(vbar), logn, out,
+              nt, quota, zdot, static_cast<__nv_bfloat16*>(kbar), static_cast<__nv_bfloat16*>(vbar), logn, out,
               out_stride, out_dtype == OA_F32 ? 1 : 0, sm_scale * kLog2e, status};
   if (kbar == nullptr && logn == nullptr) {
     OA_REQUIRE(oa_aligned16(q) && q_stride % 8 == 0, "%s: q rows must be 16-byte aligned", fn);

@@ -159,6 +159,7 @@ class OursB200:
         self.tmax = torch.zeros(R, self.NT, dtype=torch.float32, device=dev)
         self.score = torch.zeros(R, Cn, device=dev)
         self.nt = torch.zeros(R, Cn, device=dev)
+        self.zdot = torch.zeros(R, Cn, device=dev)  # ErrorGate's tail-mean dots, reused by the fused flash
         self.quota = torch.zeros(R, Cn, device=dev)
         self.exp_idx = torch.full((R, E), -1, dtype=torch.int32, device=dev)
         self.kbar = torch.zeros(R, Cn, D, dtype=torch.bfloat16, device=dev)
@@ -240,7 +241,7 @@ class OursB200:
         S.index_update(K, V, st, n_dev, q=qr, zq=self.zq)
         S.qgs_scan(st["codes"], self.zq, n_dev, ns, nl, self.scores, self.tmax, self.status)
         S.qgs_select(self.scores, self.tmax, Lmax, n_dev, ns, nl, k_top, sel)
-        S.errorgate_waterfill(qr, K, st, sel, self.E, self.score, self.nt, self.quota, self.status)
+        S.errorgate_waterfill(qr, K, st, sel, self.E, self.score, self.nt, self.quota, self.status, zdot=self.zdot)
         n0_dev = C.n0_dev if C.n0_dev is not None else self._n0_dev
         S.topq(self.scores, st, self.quota, self.E, n_dev, n0_dev, self.exp_idx, self.status)
         if residual:
@@ -259,7 +260,7 @@ class OursB200:
         keep = self.keep_proxies
         S.residual_flash(qr, C.K[l], C.V[l], self.st[l], sel, self.exp_idx, self.nt, self.quota, self.out,
                          kbar=self.kbar if keep else None, vbar=self.vbar if keep else None,
-                         logn=self.logn if keep else None, status=self.status)
+                         logn=self.logn if keep else None, status=self.status, zdot=self.zdot)
         return self.out.view(self.B, HQ, 1, D)
 
     def attend(self, l, qr, sel, exp_idx, kbar_r, vbar_r, logn):

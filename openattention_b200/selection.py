@@ -61,16 +61,17 @@ def qgs_select(scores, tile_max, Lmax, n_dev, ns, nl, k_top, sel):
               _ptr(n_dev), int(ns), int(nl), int(k_top), _ptr(sel), _stream(scores))
 
 
-def errorgate_waterfill(q, K, st, sel, E, score, nt, quota, status=None):
+def errorgate_waterfill(q, K, st, sel, E, score, nt, quota, status=None, zdot=None):
+    """zdot (optional, (R, C) fp32): receives q . kbar of each cluster's tail mean, for residual_flash."""
     B, _, Lmax, _ = K.shape
     C = st["nb"].shape[-1]
     R = B * HQ
-    for nm, t in (("score", score), ("nt", nt), ("quota", quota)):
+    for nm, t in (("score", score), ("nt", nt), ("quota", quota), ("zdot", zdot)):
         _need(nm, t, torch.float32, (R, C))
     _need("sel", sel, torch.int32)
     _lib.call("oa_errorgate_waterfill", _ptr(q), q.stride(0), _ptr(K), B, Lmax, C, _ptr(st["asg"]), _ptr(sel),
               sel.shape[1], _ptr(st["Sk"]), _ptr(st["Sk2"]), _ptr(st["nb"]), float(E), _ptr(score), _ptr(nt),
-              _ptr(quota), _ptr(status), _stream(K))
+              _ptr(quota), _ptr(zdot), _ptr(status), _stream(K))
 
 
 def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx, status=None):
@@ -98,18 +99,20 @@ def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn, status=None):
 
 
 def residual_flash(q, K, V, st, sel, exp_idx, nt, quota, out, kbar=None, vbar=None, logn=None, sm_scale=128 ** -0.5,
-                   status=None):
-    """Residual proxies + OpenAttention.flash in one kernel; out (B*32, D) bf16 or fp32."""
+                   status=None, zdot=None):
+    """Residual proxies + OpenAttention.flash in one kernel; out (B*32, D) bf16 or fp32.  zdot: the
+    step's errorgate_waterfill zdot output (optional; saves the Sk read)."""
     B, _, Lmax, _ = K.shape
     C = st["nb"].shape[-1]
     R = B * HQ
     if out.shape != (R, D) or out.stride(1) != 1 or out.dtype not in (torch.bfloat16, torch.float32):
         raise RuntimeError("out must be (B*32, 128) bf16 or fp32 with a contiguous last dim")
     code = _lib.OA_F32 if out.dtype == torch.float32 else _lib.OA_BF16
+    _need("zdot", zdot, torch.float32, (R, C))
     _lib.call("oa_residual_flash", _ptr(q), q.stride(0), _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["asg"]), _ptr(sel),
               sel.shape[1], _ptr(exp_idx), exp_idx.shape[1], _ptr(st["Sk"]), _ptr(st["Sv"]), _ptr(nt), _ptr(quota),
-              _ptr(kbar), _ptr(vbar), _ptr(logn), _ptr(out), out.stride(0), code, float(sm_scale), _ptr(status),
-              _stream(K))
+              _ptr(zdot), _ptr(kbar), _ptr(vbar), _ptr(logn), _ptr(out), out.stride(0), code, float(sm_scale),
+              _ptr(status), _stream(K))
 
 
 def padded_len(Lmax: int) -> int:

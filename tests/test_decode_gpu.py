@@ -119,6 +119,9 @@ def test_fused_residual_flash(name, golden_dir):
         o_ = torch.empty(R, D, dtype=dt, device="cuda")
         S.residual_flash(qr, Mth.C.K[0], Mth.C.V[0], m.st[0], sel, m.exp_idx, m.nt, m.quota, o_, status=m.status)
         outs.append(o_)
+    out_z = torch.empty(R, D, dtype=torch.float32, device="cuda")  # the deployed form: Sk dots from ErrorGate
+    S.residual_flash(qr, Mth.C.K[0], Mth.C.V[0], m.st[0], sel, m.exp_idx, m.nt, m.quota, out_z, status=m.status,
+                     zdot=m.zdot)
     torch.cuda.synchronize()
     o = O.decode_step(st_np, O.bits(q.reshape(R, D)), K, V, n, rho, C, E)
     _eq("exp_idx", m.exp_idx, o["exp_idx"])
@@ -140,6 +143,7 @@ def test_fused_residual_flash(name, golden_dir):
                            o["sel"], o["exp_idx"], Skr, Svr, nr)
     close(outs[0], est)
     close(outs[0], o["out"])
+    close(out_z, est)
     assert torch.equal(outs[0], outs[1])
     g16 = outs[2].float().cpu()
     r16 = outs[0].cpu().to(torch.bfloat16).float()
@@ -266,7 +270,7 @@ def test_decode_32k_steps_bit_exact(rho):
         Kn[:, :, n - 1], Vn[:, :, n - 1] = O.bits(nk), O.bits(nv)
         q = torch.randn(B, HQ, 1, D, generator=g, device=dev).to(torch.bfloat16)
         qr, sel = m.select(0, q, n, residual=False)
-        S.residual_flash(qr, K, V, m.st[0], sel, m.exp_idx, m.nt, m.quota, out, status=m.status)
+        S.residual_flash(qr, K, V, m.st[0], sel, m.exp_idx, m.nt, m.quota, out, status=m.status, zdot=m.zdot)
         torch.cuda.synchronize()
         o = O.decode_step(st_np, O.bits(q.reshape(R, D)), Kn, Vn, n, rho, C, E)
         _eq(f"step{s}.sel", sel, o["sel"])
@@ -313,7 +317,7 @@ def test_decode_sweep_shapes_bit_exact(B, n0, rho):
         Kn[:, :, n - 1], Vn[:, :, n - 1] = O.bits(nk), O.bits(nv)
         q = torch.randn(B, HQ, 1, D, generator=g, device=dev).to(torch.bfloat16)
         qr, sel = m.select(0, q, n, residual=False)
-        S.residual_flash(qr, K, V, m.st[0], sel, m.exp_idx, m.nt, m.quota, out, status=m.status)
+        S.residual_flash(qr, K, V, m.st[0], sel, m.exp_idx, m.nt, m.quota, out, status=m.status, zdot=m.zdot)
         torch.cuda.synchronize()
         o = O.decode_step(st_np, O.bits(q.reshape(R, D)), Kn, Vn, n, rho, C, E)
         _eq(f"step{s}.sel", sel, o["sel"])
