@@ -558,6 +558,48 @@ def run_sweep(a):
     return None
 
 
+# ------------------------------------------------------------------ end-to-end model decode (config c4)
+def run_model_e2e(a):
+    """Config c4: a random-initialised Llama-3.1-8B architecture with the OpenAttention path as its
+    attention; dense prefill of a uniformly random prompt (plus the index build of every layer), then
+    `--decode-steps` greedy decode steps replayed as one CUDA graph per step.  Reports ms per decode
+    step (per token of each request) and the aggregate tokens/s."""
+    from openattention_b200 import llama as L
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    cfg = L.LlamaConfig()
+    B, T, steps = B_PER_GPU, a.prompt, a.decode_steps
+    model = L.RandomLlama(cfg, B, T + steps + a.warmup + 16, dev, rho=RHO, seed=1)
+    g = torch.Generator(device=dev)
+    g.manual_seed(2)
+    prompt = torch.randint(0, cfg.vocab, (B, T), generator=g, device=dev)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    first = model.prefill(prompt)
+    torch.cuda.synchronize()
+    t_prefill = time.perf_counter() - t0
+    model.start_decode(T, first)
+    model.capture()
+    for _ in range(a.warmup):
+        model.step_graph()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        model.step_graph()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    return {"metric": "ms/token e2e (c4: random-init Llama-3.1-8B, OpenAttention 1% decode)", "value": round(ms, 4),
+            "unit": "ms/token", "n_gpus": 1, "steps": steps, "warmup": a.warmup, "higher_is_better": False,
+            "tokens_per_s": round(B * 1000.0 / ms, 1), "dtype": "bf16", "data": "synthetic (uniform random prompt)",
+            "prefill_incl_build_s": round(t_prefill, 2),
+            "config": {"workload": "c4 end-to-end decode", "model": "Llama-3.1-8B architecture, random init",
+                       "global_batch": B, "prompt": T, "decode_steps": steps, "rho": RHO,
+                       "parallelism": "single GPU (batch replicas per GPU)"},
+            "status": int(model.method.status.item())}
+
+
 # ------------------------------------------------------------------ reference arm (CPU)
 def use_all_host_threads(O):
     """The CPU legs use every host core (torchrun sets OMP_NUM_THREADS=1 per rank).  Returns the
@@ -629,6 +671,10 @@ def main():
     ap.add_argument("--steps", type=int, default=500)
     ap.add_argument("--warmup", type=int, default=20)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--model-e2e", action="store_true",
+                    help="config c4: end-to-end decode of a random-init Llama-3.1-8B (ms/token); --batch sets B")
+    ap.add_argument("--prompt", type=int, default=30000, help="prompt length for --model-e2e")
+    ap.add_argument("--decode-steps", type=int, default=256, help="decode steps for --model-e2e")
     ap.add_argument("--sweep", action="store_true",
                     help="latency sweep of the decode step over batch x context x read (one JSON line per point)")
     ap.add_argument("--sweep-b", default="", help="comma list of batches for --sweep")
@@ -644,6 +690,9 @@ def main():
         a.warmup = 3
     if a.sweep:
         run_sweep(a)
+        return
+    if a.model_e2e:
+        print(json.dumps(run_model_e2e(a)), flush=True)
         return
     res = run_reference(a) if a.impl == "reference" else run_ours(a)
     if res is not None:
