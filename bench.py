@@ -164,14 +164,16 @@ class GraphStep:
     With copy_out the graph also copies the attention output into a buffer of its own (so a host
     read of one step can overlap the next step, which rewrites the method's output buffer)."""
 
-    def __init__(self, m, Mth, n0, dev, copy_out=False):
+    def __init__(self, m, Mth, n0, dev, copy_out=False, fresh=True):
         from openattention_b200.geometry import HQ
         B = m.B
         self.m, self.Mth = m, Mth
         self.q_in = torch.zeros(B, HQ, 1, 128, dtype=torch.bfloat16, device=dev)
         self.k_in = torch.zeros(B, 8, 128, dtype=torch.bfloat16, device=dev)
         self.v_in = torch.zeros(B, 8, 128, dtype=torch.bfloat16, device=dev)
-        if getattr(Mth.C, "kv_idx", None) is None or Mth.C.n_dev is None:  # position counters, shared by all graphs
+        # position counters: new ones for a new workload (fresh), else the ones of the graphs already
+        # captured for this workload, which all advance the same counters
+        if fresh or getattr(Mth.C, "kv_idx", None) is None or Mth.C.n_dev is None:
             Mth.C.n_dev = torch.full((1,), n0, dtype=torch.int32, device=dev)      # n before the step
             Mth.C.kv_idx = torch.full((1,), n0 - 1, dtype=torch.int64, device=dev)
             Mth.C.n0_dev = torch.full((1,), n0, dtype=torch.int32, device=dev)
@@ -263,7 +265,8 @@ def stage_profile(m, Mth, gs, iters):
                                    prep=lambda: m.scores.copy_(scores_snap)),
         "errorgate_waterfill_kernel": timed(lambda: S.errorgate_waterfill(qr, K, st, sel, E, m.score, m.nt, m.quota,
                                                                           m.status, zdot=m.zdot)),
-        "topq_stream_kernel": timed(lambda: S.topq(m.scores, st, m.quota, E, n_dev, n0_dev, m.exp_idx, m.status)),
+        "topq_stream_kernel": timed(lambda: S.topq(m.scores, st, m.quota, E, n_dev, n0_dev, m.exp_idx, m.status,
+                                                     workspace=m.topq_ws)),
         "proxy_flash_kernel": timed(lambda: S.residual_flash(qr, K, V, st, sel, m.exp_idx, m.nt, m.quota, m.out,
                                                                 status=m.status, zdot=m.zdot)),
     }
@@ -319,7 +322,7 @@ def cpu_baseline_sample(m, Mth, qs, nks, nvs, budget_s=12.0):
         steps += 1
     per_req = statistics.median(times)
     return {"value": per_req * 1e6 * B_PER_GPU, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{steps} decode steps of 1 request (n~{N_CTX}, 1% read), median x {B_PER_GPU} requests; "
+            "sample": f"{steps} decode steps of 1 request (n~{N_CTX}, rho={RHO:g}), median x {B_PER_GPU} requests; "
                       f"oracle/oa_oracle.c with OpenMP on {threads} threads"}
 
 
@@ -391,7 +394,7 @@ def run_ours(a):
     hv = nvs.cpu().pin_memory()
     hout = torch.empty(max(a.steps, a.warmup), B_PER_GPU, HQ, 1, 128, dtype=torch.bfloat16).pin_memory()
     n_now0, kv_now0 = Mth.C.n_dev.clone(), Mth.C.kv_idx.clone()
-    gsp = [GraphStep(m, Mth, n0, dev, copy_out=True) for _ in range(2)]
+    gsp = [GraphStep(m, Mth, n0, dev, copy_out=True, fresh=False) for _ in range(2)]
     Mth.C.n_dev.copy_(n_now0)
     Mth.C.kv_idx.copy_(kv_now0)
     cs = torch.cuda.Stream(dev)
@@ -454,7 +457,7 @@ def run_ours(a):
             "metric": METRIC, "value": round(ms * 1e3 / world, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": round(ms, 5), "higher_is_better": False, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded clustered RoPE keys, N(0,1) values/queries)",
-            "config": {"workload": f"c2 decode-attn-stage: B={B_PER_GPU} requests/GPU, n={N_CTX}+steps, rho=1% "
+            "config": {"workload": f"c2 decode-attn-stage: B={B_PER_GPU} requests/GPU, n={N_CTX}+steps, rho={RHO:g} "
                                    f"(C={m.C}, E={m.E}), one layer step as one CUDA graph",
                        "global_batch": B_PER_GPU * world, "seq_len": N_CTX,
                        "parallelism": f"request-sharded x{world} (no data-path collective)",
@@ -657,7 +660,7 @@ def run_reference(a):
             "warmup": a.warmup, "ms_per_step": round(per / 1e3, 4), "higher_is_better": False, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded clustered RoPE keys)",
             "impl": "reference",
-            "config": {"workload": f"c2 decode-attn-stage: B={B_PER_GPU} requests, n={N_CTX}, rho=1% (C={C}, E={E}), "
+            "config": {"workload": f"c2 decode-attn-stage: B={B_PER_GPU} requests, n={N_CTX}, rho={RHO:g} (C={C}, E={E}), "
                                    "one layer step", "global_batch": B_PER_GPU, "seq_len": N_CTX,
                        "parallelism": "host CPU"},
             "cpu_baseline": {"value": round(per, 1), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
@@ -665,7 +668,7 @@ def run_reference(a):
 
 
 def main():
-    global B_PER_GPU, N_CTX
+    global B_PER_GPU, N_CTX, RHO
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=500)
@@ -683,9 +686,12 @@ def main():
                     help="context length (default 32768, the benchmark config; others only for profiling)")
     ap.add_argument("--batch", type=int, default=B_PER_GPU,
                     help="requests per GPU (default 32, the benchmark config; smaller only for profiling)")
+    ap.add_argument("--rho", type=float, default=RHO,
+                    help="read fraction (default 0.01, the benchmark config; 0.03 / 0.05 only for profiling)")
     a = ap.parse_args()
     B_PER_GPU = a.batch
     N_CTX = a.ctx
+    RHO = a.rho
     if a.warmup < 3:
         a.warmup = 3
     if a.sweep:

@@ -159,12 +159,19 @@ int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64
  * cluster's offset sum_{c'<c} q_c' in ascending position; -1 pads.  Candidates are the cluster's CSR
  * members (positions < n0) and its generated tokens: reclist (may be NULL) while it holds them all
  * (reccnt <= rmax), else positions in [n0, n) with asg == c.  C <= 256.  status (may be NULL): set to
- * 4 if the bulk copy of the score row did not complete in the bounded wait.
+ * 4 if a bulk copy of the score row did not complete in the bounded wait.
+ * workspace (may be NULL): oa_topq_workspace_bytes(R, Lmax, E) bytes, 16-byte aligned, used for rows
+ * too long for the shared-memory kernel (their member keys are permuted into it); without it such
+ * rows read their keys from global memory, which is much slower.
  * Replaces _k_topq_d2 (inference/ours_graph.py:93-166). */
 int oa_topq(const void* scores, int64_t score_stride, int64_t R, int64_t Lmax, int64_t C, const int32_t* mem,
             const int32_t* cstart, const int32_t* clen, const int32_t* asg, const int32_t* reclist,
             const int32_t* reccnt, int rmax, const float* quota, int64_t E, const int32_t* n_dev,
-            const int32_t* n0_dev, int32_t* exp_idx, int32_t* status, void* stream);
+            const int32_t* n0_dev, int32_t* exp_idx, int32_t* status, void* workspace, size_t workspace_bytes,
+            void* stream);
+
+/* Bytes of workspace oa_topq uses for these sizes (0 when its rows fit the shared-memory kernel). */
+size_t oa_topq_workspace_bytes(int64_t R, int64_t Lmax, int64_t E);
 
 /* Residual proxies: per (row, cluster) the pooled sums minus every token read (sel in order, then
  * the cluster's exp segment), n' = nt - quota, kbar' / vbar' = bf16(sums / max(n', 1)) (R, C, 128),

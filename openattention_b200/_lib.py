@@ -34,7 +34,8 @@ SIGNATURES = {
     "oa_qgs_scan": (I32, [P, P, I64, I64, P, I32, I32, P, I64, P, I64, P, P]),
     "oa_qgs_select": (I32, [P, I64, P, I64, I64, I64, P, I32, I32, I32, P, P]),
     "oa_errorgate_waterfill": (I32, [P, I64, P, I64, I64, I64, P, P, I64, P, P, P, F32, P, P, P, P, P, P]),
-    "oa_topq": (I32, [P, I64, I64, I64, I64, P, P, P, P, P, P, I32, P, I64, P, P, P, P, P]),
+    "oa_topq": (I32, [P, I64, I64, I64, I64, P, P, P, P, P, P, I32, P, I64, P, P, P, P, P, SZ, P]),
+    "oa_topq_workspace_bytes": (SZ, [I64, I64, I64]),
     "oa_residual": (I32, [P, P, I64, I64, I64, P, P, I64, P, I64, P, P, P, P, P, P, P, P, P]),
     "oa_residual_flash": (I32, [P, I64, P, P, I64, I64, I64, P, P, I64, P, I64, P, P, P, P, P, P, P, P, P, I64,
                                 I32, F32, P, P]),

@@ -22,6 +22,17 @@ int oa_check_launch(const char* what) {
   return OA_OK;
 }
 
+int oa_smem_opt_in(const void* kernel, size_t dyn, const char* what) {
+  cudaFuncAttributes fa;
+  cudaError_t e = cudaFuncGetAttributes(&fa, kernel);
+  if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  if (dyn + fa.sharedSizeBytes > 48 * 1024) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
+    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+  }
+  return OA_OK;
+}
+
 extern "C" const char* oa_version(void) { return "openattention_b200 0.1.0 (sm_100a)"; }
 
 extern "C" const char* oa_last_error_string(void) { return g_err; }

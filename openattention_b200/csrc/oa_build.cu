@@ -337,10 +337,7 @@ extern "C" int oa_kmeans_assign(const float* zP, int64_t T, int64_t C, const flo
   OA_REQUIRE(T > 0 && C > 0 && C <= 1024 && asg_stride >= T, "%s: bad sizes", fn);
   OA_REQUIRE(zP && cent && asg && oa_aligned16(zP), "%s: null or misaligned pointer", fn);
   const size_t smem = sizeof(float) * (size_t)C * (kRC + 1);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kmeans_assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-  }
+  if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(kmeans_assign_kernel), smem, fn)) return rc;
   kmeans_assign_kernel<<<dim3((unsigned)((T + kBT - 1) / kBT), kHQ), kBT, smem, S(stream)>>>(
       zP, (int)T, (int)C, cent, asg, asg_stride);
   return oa_check_launch(fn);

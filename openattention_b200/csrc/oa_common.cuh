@@ -98,6 +98,9 @@ enum {
 
 int oa_fail(int code, const char* fmt, ...);
 int oa_check_launch(const char* what);
+// Raise a kernel's dynamic shared-memory limit when its static arrays plus `dyn` bytes pass the
+// 48 KB default (the opt-in counts the static part too).  Returns an OA status.
+int oa_smem_opt_in(const void* kernel, size_t dyn, const char* what);
 
 #define OA_REQUIRE(cond, ...)                      \
   do {                                             \

@@ -13,6 +13,7 @@
 // accumulated in double from the end.
 #include "oa_common.cuh"
 #include "oa_math.cuh"
+#include "oa_warp.cuh"
 #include "../../include/openattention_b200.h"
 
 namespace oa {
@@ -981,6 +982,313 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
   if (prev_r >= 0) winners_out(prev_r, prev_cnt);
 }
 
+// ------------------------------------------------------------------------ top-q, long rows
+// For rows whose score row does not fit shared memory (beyond about 49K positions) top-q runs in two
+// kernels over a caller workspace of R x ckw 16-bit keys:
+//   topq_permute_kernel: one CTA per row stages the score row in chunks of kPmChunk positions (bulk
+//     copies); for each chunk, warps take clusters and key the run of the cluster's members whose
+//     positions fall in the chunk (member lists are ascending within a cluster, so each run starts
+//     where the previous chunk's ended), writing the keys into the workspace in CSR order; the
+//     member list is read once;
+//   topq_ck_kernel: one CTA per row; warps take the clusters with q > 0 and select from the
+//     cluster's contiguous keys in the workspace (register path as topq_stream_kernel, radix path
+//     for larger clusters), with generated tokens keyed from the score row.
+constexpr int kPmThreads = 1024;
+constexpr int kPmChunk = 65536;  // positions staged per pass
+constexpr int kPmU = 8;            // 32-member groups a warp loads at once
+constexpr int kCkThreads = 256;
+constexpr int kCkWarps = kCkThreads / 32;
+constexpr int kCkWin = 4096;  // member keys a warp stages in shared memory per window
+constexpr int kCkWinSlots = kCkWin + 16 + 64;  // + alignment slack of the 16-byte loads + 64 generated keys
+
+__global__ void __launch_bounds__(kPmThreads) topq_permute_kernel(const TopqArgs a, uint16_t* ck, int64_t ckw) {
+  extern __shared__ __align__(128) uint16_t pm_spill[];  // kPmChunk positions
+  __shared__ int s_lo[kMaxC];  // per cluster: its first member not keyed yet
+  __shared__ int s_next;
+  __shared__ __align__(8) uint64_t mbar;
+  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  const int C = a.C;
+  const int n = __ldg(a.n_dev), n0 = __ldg(a.n0_dev);
+  const int npos = min(min(n, n0), a.Lmax);  // member lists hold positions < n0
+  const int64_t rC = (int64_t)r * C;
+  const uint16_t* sr = a.scores + (int64_t)r * a.sw;
+  const int32_t* mrow = a.mem + (int64_t)r * a.Lmax;
+  uint16_t* ckr = ck + (int64_t)r * ckw;
+  const uint32_t bar = smem_u32(&mbar);
+  for (int c = tid; c < C; c += kPmThreads) s_lo[c] = 0;
+  if (tid == 0) {
+    s_next = 0;
+    mbar_init(bar);
+  }
+  __syncthreads();
+  int it = 0;
+  for (int P0 = 0; P0 < npos; P0 += kPmChunk, ++it) {
+    const int P1 = min(npos, P0 + kPmChunk);
+    const uint32_t nbytes = (uint32_t)(((P1 - P0) + 7) & ~7) * 2u;
+    if (tid == 0) {
+      if (it > 0) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      bulk_load(pm_spill, sr + P0, nbytes, bar);
+    }
+    const bool ok = mbar_wait(bar, (uint32_t)(it & 1));
+    if (!__syncthreads_and(ok)) {
+      if (tid == 0 && a.status != nullptr) atomicExch(a.status, 4);
+      if (!ok) mbar_wait(bar, (uint32_t)(it & 1));
+      return;
+    }
+    // A cluster's members are in ascending position order, so its members inside [P0, P1) are the
+    // run that starts at s_lo[c]: warps take clusters and walk their runs kPmU x 32 members at a time.
+    while (true) {
+      int c = 0;
+      if (lane == 0) c = atomicAdd(&s_next, 1);
+      c = __shfl_sync(0xffffffffu, c, 0);
+      if (c >= C) break;
+      const int cs = a.cstart[rC + c], nmem = a.clen[rC + c];
+      int lo = s_lo[c];
+      while (lo < nmem) {
+        int t[kPmU];
+#pragma unroll
+        for (int u = 0; u < kPmU; ++u) {
+          const int i = lo + 32 * u + lane;
+          t[u] = i < nmem ? __ldg(mrow + cs + i) : 0x7fffffff;
+        }
+        int taken = 0;
+#pragma unroll
+        for (int u = 0; u < kPmU; ++u) {
+          // the run starts at the first position >= P0; the lower bound is checked all the same
+          const bool in = (unsigned)(t[u] - P0) < (unsigned)(P1 - P0);
+          if (in) ckr[cs + lo + 32 * u + lane] = (uint16_t)ukey16(pm_spill[t[u] - P0]);
+          taken += __popc(__ballot_sync(0xffffffffu, in));
+        }
+        lo += taken;
+        if (taken < 32 * kPmU) break;
+      }
+      if (lane == 0) s_lo[c] = lo;
+    }
+    __syncthreads();  // the staging buffer is refilled by the next pass
+    if (tid == 0) s_next = 0;
+  }
+}
+
+__global__ void __launch_bounds__(kCkThreads) topq_ck_kernel(const TopqArgs a, const uint16_t* ck, int64_t ckw) {
+  __shared__ int s_base[kMaxC + 1];
+  __shared__ int s_q[kMaxC];
+  __shared__ int s_next;
+  __shared__ int s_win[kCkWarps][32];
+  __shared__ int s_hist[kCkWarps][256];
+  __shared__ uint64_t s_w64[kCkWarps][64];
+  extern __shared__ __align__(16) uint16_t ck_win[];  // per warp kCkWinSlots keys
+  const int r = blockIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned lt = (1u << lane) - 1u;
+  const int C = a.C;
+  const int n = __ldg(a.n_dev), n0 = __ldg(a.n0_dev);
+  const int nsp = min(n, a.Lmax);
+  const int64_t rC = (int64_t)r * C;
+  const uint16_t* ckr = ck + (int64_t)r * ckw;
+  const int32_t* mrow = a.mem + (int64_t)r * a.Lmax;
+  const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
+  int32_t* out = a.exp + (int64_t)r * a.E;
+  for (int c = tid; c < C; c += kCkThreads) s_q[c] = (int)a.quota[rC + c];
+  if (tid == 0) s_next = 0;
+  __syncthreads();
+  if (tid == 0) {
+    int run = 0;
+    for (int c = 0; c < C; ++c) {
+      s_base[c] = run;
+      run += s_q[c];
+    }
+    s_base[C] = run;
+  }
+  __syncthreads();
+  for (int i = s_base[C] + tid; i < a.E; i += kCkThreads) out[i] = -1;
+  // member keys from the workspace (kb = 0); generated tokens keyed from the score row
+  const TsRow w{ckr, nullptr, a.scores + (int64_t)r * a.sw, mrow, n0, nsp, 0, 0};
+  int* hist = s_hist[warp];
+  uint16_t* wk = ck_win + (size_t)warp * kCkWinSlots;
+  while (true) {
+    int c = 0;
+    if (lane == 0) {
+      do {
+        c = atomicAdd(&s_next, 1);
+      } while (c < C && s_q[c] <= 0);
+    }
+    c = __shfl_sync(0xffffffffu, c, 0);
+    if (c >= C) break;
+    const int q = s_q[c], base = s_base[c];
+    const int cs = a.cstart[rC + c], nmem = a.clen[rC + c];
+    const int cnt = a.reclist ? a.reccnt[rC + c] : 0x7fffffff;
+    const bool use_list = a.reclist != nullptr && cnt <= a.rmax;
+    const int32_t* rec = use_list ? a.reclist + (rC + c) * a.rmax : nullptr;
+    const int ngen = use_list ? cnt : 0;
+    if (use_list && q <= kSmallQ && ngen <= 64 && nmem + 3 <= 1024) {
+      const int span = nmem + 3;
+      int* win = s_win[warp];
+      if (span <= 256)
+        topq_keys_regs<8>(w, cs, nmem, rec, ngen, q, win, 32, lane);
+      else if (span <= 512)
+        topq_keys_regs<16>(w, cs, nmem, rec, ngen, q, win, 32, lane);
+      else
+        topq_keys_regs<32>(w, cs, nmem, rec, ngen, q, win, 32, lane);
+      __syncwarp();
+      if (lane < q && base + lane < a.E) {
+        const int e = win[lane];
+        out[base + lane] = e >= 0 ? mrow[e] : -e - 1;
+      }
+      __syncwarp();
+      continue;
+    }
+    const int ngen_scan = max(0, n - n0);
+    auto pos_of = [&](int idx) -> int {
+      if (idx < nmem) return mrow[cs + idx];
+      return use_list ? rec[idx - nmem] : n0 + (idx - nmem);
+    };
+    // a cluster that fits the window is staged once: its member keys with 16-byte loads (all in
+    // flight at once), then up to 64 listed generated tokens' keys after them
+    const bool staged = nmem <= kCkWin;
+    const bool gen_staged = staged && use_list && ngen <= 64;
+    const int so = cs & 7;  // wk[so + i] = key of member i
+    if (staged) {
+      const int nv = (so + nmem + 7) >> 3;  // ends at most at Lmax rounded up to 8 = the row stride
+      __syncwarp();
+#pragma unroll 4
+      for (int j = lane; j < nv; j += 32)
+        reinterpret_cast<int4*>(wk)[j] = __ldg(reinterpret_cast<const int4*>(ckr + (cs - so)) + j);
+      __syncwarp();
+      if (gen_staged)
+        for (int j = lane; j < ngen; j += 32) wk[so + nmem + j] = (uint16_t)ts_key_at(w, rec[j]);
+      __syncwarp();
+    }
+    // threshold + sort: the k-th largest lane maximum bounds the answer from below (warp_topk_sorted)
+    if (gen_staged && q <= 32) {
+      uint64_t srt[2], kth;
+      auto word = [&](int i) -> uint64_t {
+        return ((uint64_t)wk[so + i] << 32) | (uint64_t)(0xffffffffu - (uint32_t)i);
+      };
+      if (warp_topk_sorted(nmem + ngen, q, word, s_w64[warp], srt, kth)) {
+        // lanes < q hold the winners in key order; each finds its slot by list index (= position order)
+        const int idx = (int)(0xffffffffu - (uint32_t)srt[0]);
+        int rank = 0;
+        for (int j = 0; j < q; ++j) rank += __shfl_sync(0xffffffffu, idx, j) < idx ? 1 : 0;
+        if (lane < q && base + rank < a.E) out[base + rank] = pos_of(idx);
+        __syncwarp();
+        continue;
+      }
+    }
+    // radix path over (list index, key): members' keys, then generated tokens
+    auto for_each = [&](auto&& f) {
+      if (staged) {
+        for (int i0 = 0; i0 < nmem; i0 += 32) {
+          const int i = i0 + lane;
+          const bool v = i < nmem;
+          f(v, i, v ? (uint32_t)wk[so + i] : 0u);
+        }
+      } else {
+        // members in windows of kCkWin keys, each staged with 16-byte loads
+        for (int w0 = 0; w0 < nmem; w0 += kCkWin) {
+          const int wn = min(kCkWin, nmem - w0);
+          const int g0 = cs + w0, a0 = g0 & ~7, o = g0 - a0;
+          const int nv = (o + wn + 7) >> 3;
+          __syncwarp();
+#pragma unroll 4
+          for (int j = lane; j < nv; j += 32)
+            reinterpret_cast<int4*>(wk)[j] = __ldg(reinterpret_cast<const int4*>(ckr + a0) + j);
+          __syncwarp();
+          for (int i0 = 0; i0 < wn; i0 += 32) {
+            const int i = i0 + lane;
+            const bool v = i < wn;
+            f(v, w0 + i, v ? (uint32_t)wk[o + i] : 0u);
+          }
+        }
+      }
+      if (gen_staged) {
+        for (int i0 = 0; i0 < ngen; i0 += 32) {
+          const int i = i0 + lane;
+          const bool v = i < ngen;
+          f(v, nmem + i, v ? (uint32_t)wk[so + nmem + i] : 0u);
+        }
+      } else if (use_list) {
+        for (int i0 = 0; i0 < cnt; i0 += 32) {
+          const int i = i0 + lane;
+          const bool v = i < cnt;
+          f(v, nmem + i, v ? ts_key_at(w, rec[i]) : 0u);
+        }
+      } else {
+        for (int i0 = 0; i0 < ngen_scan; i0 += 32) {
+          const int t = n0 + i0 + lane;
+          const bool v = (i0 + lane < ngen_scan) && asg_r[t] == c;
+          f(v, nmem + i0 + lane, v ? ts_key_at(w, t) : 0u);
+        }
+      }
+    };
+    int above = 0, hi = 0, lo = 0;
+    bool all = false;
+    for (int pass = 0; pass < 2 && !all; ++pass) {
+      for (int b = lane; b < 256; b += 32) hist[b] = 0;
+      __syncwarp();
+      for_each([&](bool v, int, uint32_t k) {
+        // lanes with the same bin add once (a cluster's keys share few high bytes)
+        const bool part = v && (pass == 0 || (int)(k >> 8) == hi);
+        const int bin = part ? (int)(pass == 0 ? (k >> 8) : (k & 255)) : -1;
+        const unsigned peers = __match_any_sync(0xffffffffu, bin);
+        if (part && __ffs(peers) - 1 == lane) atomicAdd(&hist[bin], __popc(peers));
+      });
+      __syncwarp();
+      int cnt8[8], sum = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        cnt8[i] = hist[255 - 8 * lane - i];
+        sum += cnt8[i];
+      }
+      int incl = sum;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += x;
+      }
+      const int excl = incl - sum;
+      const int need = q - above;
+      int fb = -1, fa = 0;
+      if (excl < need && incl >= need) {
+        int run = excl;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (fb < 0 && run + cnt8[i] >= need) {
+            fb = 255 - 8 * lane - i;
+            fa = run;
+          }
+          run += cnt8[i];
+        }
+      }
+      const unsigned who = __ballot_sync(0xffffffffu, fb >= 0);
+      if (who == 0u) {
+        all = true;
+      } else {
+        const int src = __ffs(who) - 1;
+        const int d = __shfl_sync(0xffffffffu, fb, src);
+        above += __shfl_sync(0xffffffffu, fa, src);
+        if (pass == 0) hi = d;
+        else lo = d;
+      }
+      __syncwarp();
+    }
+    const uint32_t T = all ? 0u : (((uint32_t)hi << 8) | (uint32_t)lo);
+    const int need_eq = all ? 0 : q - above;
+    int taken = 0, ties = 0;
+    for_each([&](bool v, int idx, uint32_t k) {
+      const bool gt = v && k > T;
+      const bool eq = v && k == T;
+      const unsigned beq = __ballot_sync(0xffffffffu, eq);
+      const bool take = gt || (eq && ties + __popc(beq & lt) < need_eq);
+      const unsigned bt = __ballot_sync(0xffffffffu, take);
+      const int slot = taken + __popc(bt & lt);
+      if (take && slot < q && base + slot < a.E) out[base + slot] = pos_of(idx);
+      taken += __popc(bt);
+      ties += __popc(beq);
+    });
+    __syncwarp();
+  }
+}
+
 // ------------------------------------------------------------------------ residual proxies (+ flash)
 // One CTA (8 warps) per row; warp w owns the clusters c = c0 + w + 8k (k < 8) of each 64-cluster
 // chunk and keeps their running sums Sk - sum k, Sv - sum v in registers (lane <-> dims lane + 32i).
@@ -1551,47 +1859,79 @@ extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const voi
   GateArgs a{static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(K), (int)Lmax, (int)C,
              (int)n_sel, asg, sel, Sk, Sk2, nb, E, score, nt, quota, zdot, status};
   const size_t smem = eg_smem_bytes((int)C, (int)n_sel);
+  if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(errorgate_waterfill_kernel), smem, fn)) return rc;
   errorgate_waterfill_kernel<<<(unsigned)(B * kHQ), kEgThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
+}
+
+namespace oa {
+namespace {
+size_t ts_smem_bytes(int64_t Lmax, int64_t E) {  // shared memory of topq_stream_kernel for one row
+  const size_t spill_bytes = (size_t)((Lmax + 7) & ~7ll) * 2;
+  const int key_cap = (int)(((Lmax + 7) & ~7ll) + 1040);  // list slack of the register path
+  return spill_bytes + (size_t)(key_cap + kTsGenCap) * 2 + (size_t)E * 4;
+}
+bool ts_fits(int64_t Lmax, int64_t E) { return ts_smem_bytes(Lmax, E) <= 196 * 1024; }
+int64_t ck_stride(int64_t Lmax) { return (Lmax + 7) & ~7ll; }
+}  // namespace
+}  // namespace oa
+
+extern "C" size_t oa_topq_workspace_bytes(int64_t R, int64_t Lmax, int64_t E) {
+  if (R <= 0 || Lmax <= 0 || oa::ts_fits(Lmax, E)) return 0;
+  return (size_t)(R * oa::ck_stride(Lmax) + 1024) * sizeof(uint16_t);
 }
 
 extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int64_t Lmax, int64_t C,
                        const int32_t* mem, const int32_t* cstart, const int32_t* clen, const int32_t* asg,
                        const int32_t* reclist, const int32_t* reccnt, int rmax, const float* quota, int64_t E,
                        const int32_t* n_dev, const int32_t* n0_dev, int32_t* exp_idx, int32_t* status,
-                       void* stream) {
+                       void* workspace, size_t workspace_bytes, void* stream) {
   const char* fn = "oa_topq";
   OA_REQUIRE(R > 0 && Lmax > 0 && Lmax < (1 << 30) && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
   OA_REQUIRE(score_stride >= ((Lmax + 7) & ~7ll) && score_stride % 8 == 0 && oa_aligned16(scores),
              "%s: score rows must be 16-byte aligned and hold Lmax rounded up to 8", fn);
   OA_REQUIRE(scores && mem && cstart && clen && asg && quota && n_dev && n0_dev && exp_idx, "%s: null pointer", fn);
   OA_REQUIRE(reclist == nullptr || (reccnt != nullptr && rmax > 0), "%s: reclist needs reccnt and rmax", fn);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t spill_bytes = (size_t)((Lmax + 7) & ~7ll) * 2;
-  {  // persistent streamed-key kernel when the score row, the member keys and the generated keys fit
+  if (ts_fits(Lmax, E)) {  // persistent streamed-key kernel: score row, member keys and generated keys fit
     const int key_cap = (int)(((Lmax + 7) & ~7ll) + 1040);  // list slack of the register path
-    const size_t smem_ts = spill_bytes + (size_t)(key_cap + kTsGenCap) * 2 + (size_t)E * 4;
-    if (smem_ts <= 196 * 1024) {
-      int dev = 0, sms = 148;
-      cudaGetDevice(&dev);
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, 1, mem, cstart,
-                 clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};
-      cudaError_t e =
-          cudaFuncSetAttribute(topq_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_ts);
-      if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-      const int grid = (int)std::min<int64_t>(R, sms);
-      topq_stream_kernel<<<grid, kTsThreads, smem_ts, static_cast<cudaStream_t>(stream)>>>(
-          a, (int)R, (int)spill_bytes, key_cap);
-      return oa_check_launch(fn);
-    }
+    const size_t smem_ts = ts_smem_bytes(Lmax, E);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, 1, mem, cstart,
+               clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};
+    cudaError_t e = cudaFuncSetAttribute(topq_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_ts);
+    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+    const int grid = (int)std::min<int64_t>(R, sms);
+    topq_stream_kernel<<<grid, kTsThreads, smem_ts, st>>>(a, (int)R, (int)spill_bytes, key_cap);
+    return oa_check_launch(fn);
+  }
+  TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, 0, mem, cstart,
+             clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};
+  if (workspace != nullptr && workspace_bytes >= oa_topq_workspace_bytes(R, Lmax, E)) {
+    // long rows: keys permuted into CSR order in the workspace, then selected from contiguous keys
+    OA_REQUIRE(oa_aligned16(workspace), "%s: workspace must be 16-byte aligned", fn);
+    uint16_t* ck = static_cast<uint16_t*>(workspace);
+    const int64_t ckw = ck_stride(Lmax);
+    const size_t smem = (size_t)kPmChunk * 2;
+    cudaError_t e = cudaFuncSetAttribute(topq_permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+    topq_permute_kernel<<<(unsigned)R, kPmThreads, smem, st>>>(a, ck, ckw);
+    int rc = oa_check_launch(fn);
+    if (rc != OA_OK) return rc;
+    const size_t smem_ck = (size_t)kCkWarps * kCkWinSlots * sizeof(uint16_t);
+    if (int rc2 = oa_smem_opt_in(reinterpret_cast<const void*>(topq_ck_kernel), smem_ck, fn)) return rc2;
+    topq_ck_kernel<<<(unsigned)R, kCkThreads, smem_ck, st>>>(a, ck, ckw);
+    return oa_check_launch(fn);
   }
   const bool in_smem = spill_bytes <= 160 * 1024;  // larger rows read their keys from global memory
-  TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, in_smem ? 1 : 0,
-             mem, cstart, clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};
+  a.smem_keys = in_smem ? 1 : 0;
   const size_t smem = in_smem ? spill_bytes : 16;
   cudaError_t e = cudaFuncSetAttribute(topq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-  topq_kernel<<<(unsigned)R, kTqThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  topq_kernel<<<(unsigned)R, kTqThreads, smem, st>>>(a);
   return oa_check_launch(fn);
 }
 
@@ -1632,6 +1972,7 @@ extern "C" int oa_residual_flash(const void* q, int64_t q_stride, const void* K,
     OA_REQUIRE(oa_aligned16(q) && q_stride % 8 == 0, "%s: q rows must be 16-byte aligned", fn);
     OA_REQUIRE(oa_aligned16(Sk) && oa_aligned16(Sv), "%s: Sk / Sv must be 16-byte aligned", fn);
     const size_t smem = proxy_flash_smem((int)(n_sel + E), (int)C);
+    if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(proxy_flash_kernel), smem, fn)) return rc;
     proxy_flash_kernel<<<(unsigned)(B * kHQ), kPF, smem, static_cast<cudaStream_t>(stream)>>>(a);
   } else {
     residual_kernel<true><<<(unsigned)(B * kHQ), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);

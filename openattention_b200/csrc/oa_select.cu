@@ -566,6 +566,7 @@ extern "C" int oa_index_update(const void* K, const void* V, int64_t B, int64_t 
               (int)Lmax, (int)C};
   const size_t smem = (size_t)std::min<int64_t>(C, kIuCentCache) * kRC * sizeof(float);
   OA_REQUIRE(oa_aligned16(cent) && oa_aligned16(U) && oa_aligned16(W), "%s: U / W / cent must be 16-byte aligned", fn);
+  if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(index_update_kernel), smem, fn)) return rc;
   index_update_kernel<<<(unsigned)(B * kHQ), 128, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }
@@ -605,10 +606,7 @@ extern "C" int oa_qgs_select(void* scores, int64_t score_stride, const float* ti
                NT, (int)Lmax, sel, NT_pad, kt2_max};
   const size_t smem = (size_t)kSelWarps * (NT_pad * 4 + (size_t)kt2_max * kMaxTile * 2);
   OA_REQUIRE(smem <= 200 * 1024, "%s: Lmax=%lld and k_top=%d need too much shared memory", fn, (long long)Lmax, k_top);
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(qgs_select_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-  }
+  if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(qgs_select_kernel), smem, fn)) return rc;
   qgs_select_kernel<<<(unsigned)((R + kSelWarps - 1) / kSelWarps), kSelWarps * 32, smem,
                       static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);

@@ -162,6 +162,7 @@ class OursB200:
         self.zdot = torch.zeros(R, Cn, device=dev)  # ErrorGate's tail-mean dots, reused by the fused flash
         self.quota = torch.zeros(R, Cn, device=dev)
         self.exp_idx = torch.full((R, E), -1, dtype=torch.int32, device=dev)
+        self.topq_ws = S.topq_workspace(R, Lmax, E, dev)  # only for rows too long for shared memory
         self.kbar = torch.zeros(R, Cn, D, dtype=torch.bfloat16, device=dev)
         self.vbar = torch.zeros(R, Cn, D, dtype=torch.bfloat16, device=dev)
         self.logn = torch.zeros(R, Cn, device=dev)
@@ -243,7 +244,7 @@ class OursB200:
         S.qgs_select(self.scores, self.tmax, Lmax, n_dev, ns, nl, k_top, sel)
         S.errorgate_waterfill(qr, K, st, sel, self.E, self.score, self.nt, self.quota, self.status, zdot=self.zdot)
         n0_dev = C.n0_dev if C.n0_dev is not None else self._n0_dev
-        S.topq(self.scores, st, self.quota, self.E, n_dev, n0_dev, self.exp_idx, self.status)
+        S.topq(self.scores, st, self.quota, self.E, n_dev, n0_dev, self.exp_idx, self.status, workspace=self.topq_ws)
         if residual:
             S.residual(K, V, st, sel, self.exp_idx, self.nt, self.quota, self.kbar, self.vbar, self.logn,
                        self.status)

@@ -74,7 +74,13 @@ def errorgate_waterfill(q, K, st, sel, E, score, nt, quota, status=None, zdot=No
               _ptr(quota), _ptr(zdot), _ptr(status), _stream(K))
 
 
-def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx, status=None):
+def topq_workspace(R: int, Lmax: int, E: int, device) -> torch.Tensor | None:
+    """The workspace oa_topq uses for rows too long for its shared-memory kernel (None when not needed)."""
+    nbytes = _lib.load().oa_topq_workspace_bytes(R, Lmax, E)
+    return torch.empty(nbytes, dtype=torch.uint8, device=device) if nbytes else None
+
+
+def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx, status=None, workspace=None):
     R = scores.shape[0]
     B, _, Lmax = st["asg"].shape
     C = st["nb"].shape[-1]
@@ -83,7 +89,7 @@ def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx, status=None):
     _lib.call("oa_topq", _ptr(scores), scores.stride(0), R, Lmax, C, _ptr(st["mem"]), _ptr(st["cstart"]),
               _ptr(st["clen"]), _ptr(st["asg"]), _ptr(rec), _ptr(st.get("reccnt")),
               0 if rec is None else rec.shape[-1], _ptr(quota), E, _ptr(n_dev), _ptr(n0_dev), _ptr(exp_idx),
-              _ptr(status), _stream(scores))
+              _ptr(status), _ptr(workspace), 0 if workspace is None else workspace.numel(), _stream(scores))
 
 
 def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn, status=None):

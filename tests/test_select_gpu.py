@@ -40,7 +40,18 @@ def _rows(kind, R, n, seed):
 @pytest.mark.parametrize("kind", ["random", "equal", "skewed"])
 @pytest.mark.parametrize("k_top", [1, 9, 31, 40])
 def test_select_matches_oracle(kind, k_top):
-    R, n, ns, nl, Lmax = 64, 4101, 3, 3, 4160
+    _check_select(kind, k_top, 64, 4101, 4160)
+
+
+@pytest.mark.parametrize("n,Lmax,k_top", [(65536, 65600, 20), (131072, 131104, 40)])
+def test_select_long_rows_matches_oracle(n, Lmax, k_top):
+    """Rows of 64K and 128K positions: the per-warp tile keys then take tens of KB of shared memory,
+    which together with the kernel's static arrays passes the 48 KB default."""
+    _check_select("random", k_top, 8, n, Lmax)
+
+
+def _check_select(kind, k_top, R, n, Lmax):
+    ns, nl = 3, 3
     SW = S.padded_len(Lmax)
     NT = (Lmax + 31) // 32
     s = np.full((R, SW), NEG, np.uint16)
@@ -87,6 +98,48 @@ def test_topq_matches_oracle_with_ties(golden_dir, kind):
     S.topq(O.from_bits(s).cuda(), st, torch.from_numpy(quota).cuda(), E,
            torch.tensor([n], dtype=torch.int32, device="cuda"), torch.tensor([n0], dtype=torch.int32, device="cuda"),
            exp_idx, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert np.array_equal(exp_idx.cpu().numpy(), exp_ref)
+
+
+@pytest.mark.parametrize("use_ws", [True, False])
+def test_topq_long_rows_matches_oracle(use_ws):
+    """Rows too long for the shared-memory top-q (64K positions): with the workspace (keys permuted into
+    CSR order, then selected from contiguous keys) and without it (keys read from global memory)."""
+    import types
+    from openattention_b200 import method as Mth
+    from openattention_b200 import synth
+    dev = torch.device("cuda")
+    B, n0, rho = 1, 65536, 0.01
+    Lmax = n0 + 8
+    K, V, _ = synth.kv_torch(51, B, n0, Lmax, dev)
+    Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40]
+    m = Mth.OursB200(types.SimpleNamespace(rho=rho), B, Lmax, dev, layers=1)
+    g = torch.Generator(device=dev)
+    g.manual_seed(52)
+    qpre = torch.zeros(1, HQ, n0, 128, dtype=torch.bfloat16, device=dev)
+    qpre[:, :, n0 - 64:] = torch.randn(1, HQ, 64, 128, generator=g, device=dev).to(torch.bfloat16)
+    m.build(0, 0, qpre, n0)
+    R, C, E = B * HQ, m.C, m.E
+    st = m.st[0]
+    clen = st["clen"].view(R, C).cpu().numpy()
+    quota = np.zeros((R, C), np.float32)
+    for r in range(R):
+        left = E
+        for c in np.random.default_rng(60 + r).permutation(C):
+            q = min(int(np.random.default_rng(r * 97 + c).integers(0, 40)), int(clen[r, c]), left)
+            quota[r, c] = q
+            left -= q
+    s = np.full((R, S.padded_len(Lmax)), NEG, np.uint16)
+    s[:, :n0] = _rows("random", R, n0, 61)
+    exp_ref = O.topq(s, st["asg"].view(R, -1).cpu().numpy(), quota, n0, E)
+    ws = S.topq_workspace(R, Lmax, E, dev) if use_ws else None
+    assert (ws is not None) == use_ws
+    exp_idx = torch.empty(R, E, dtype=torch.int32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    S.topq(O.from_bits(s).cuda(), st, torch.from_numpy(quota).cuda(), E, torch.tensor([n0], dtype=torch.int32,
+           device=dev), torch.tensor([n0], dtype=torch.int32, device=dev), exp_idx, status, workspace=ws)
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     assert np.array_equal(exp_idx.cpu().numpy(), exp_ref)
