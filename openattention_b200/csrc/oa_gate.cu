@@ -14,6 +14,7 @@
 #include "oa_common.cuh"
 #include "oa_math.cuh"
 #include "oa_warp.cuh"
+#include "oa_warp.cuh"
 #include "../../include/openattention_b200.h"
 
 namespace oa {
@@ -741,6 +742,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
   __shared__ __align__(8) uint64_t mbar;
   __shared__ int s_base_[2][kMaxC + 1];  // row metadata, double-buffered: the next row's loads while
   __shared__ int s_q_[2][kMaxC], s_cs_[2][kMaxC], s_cl_[2][kMaxC], s_rcnt_[2][kMaxC];  // this row runs
+  __shared__ int s_ord_[2][kMaxC];  // the order in which warps take the clusters
   __shared__ int s_next;
   __shared__ int s_hist[kTsWarps][256];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -777,6 +779,26 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
       ex += s_q_[set][c];
     }
     if (lane == 31) s_base_[set][C] = incl;
+    // Largest clusters first (C <= 64), so that the last clusters taken are short ones and the
+    // warps reach the end-of-row barrier together; clusters with q = 0 go last.
+    if (C <= 64) {
+      uint64_t wv[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = lane + 32 * h;
+        uint32_t work = 0u;
+        if (c < C && s_q_[set][c] > 0) work = 1u + (uint32_t)s_cl_[set][c] + (uint32_t)min(s_rcnt_[set][c], 4096);
+        wv[h] = c < C ? ((uint64_t)work << 32) | (uint64_t)(0xffffffffu - (uint32_t)c) : 0ull;
+      }
+      bitonic64_desc(wv);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int e = lane + 32 * h;
+        if (e < C) s_ord_[set][e] = (int)(0xffffffffu - (uint32_t)wv[h]);
+      }
+    } else {
+      for (int c = lane; c < C; c += 32) s_ord_[set][c] = c;
+    }
   };
   auto winners_out = [&](int row, int cnt) {  // CSR slots / generated positions -> positions
     int32_t* pout = a.exp + (int64_t)row * a.E;
@@ -862,11 +884,14 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
     TsRow w{s_key + mo, s_gkey, a.scores + (int64_t)r * a.sw, mrow, n0, nsp, gcount, mo};
     int* hist = s_hist[warp];
     const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
+    const int* s_ord = s_ord_[cur];
     while (true) {
-      int c = 0;
+      int c = C;
       if (lane == 0) {
+        int i;
         do {
-          c = atomicAdd(&s_next, 1);
+          i = atomicAdd(&s_next, 1);
+          c = i < C ? s_ord[i] : C;
         } while (c < C && s_q[c] <= 0);
       }
       c = __shfl_sync(0xffffffffu, c, 0);
