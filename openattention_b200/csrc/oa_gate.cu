@@ -144,12 +144,29 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
     S.selt[j] = v ? t : -1;
     S.selc[j] = v ? a.asg[(int64_t)r * a.Lmax + t] : -1;
   }
-  for (int e = tid; e < min(NS, kEgSelCache) * 16; e += kEgThreads) {
-    const int j = e >> 4, part = e & 15;
-    const int t = a.sel[(int64_t)r * NS + j];
-    if (t >= 0 && t < a.Lmax)
-      *reinterpret_cast<uint4*>(S.selk + j * kD + part * 8) =
-          __ldg(reinterpret_cast<const uint4*>(Kr + (int64_t)t * kD + part * 8));
+  {  // K rows of the selected tokens: a thread's indices first, then all its row loads, then the stores
+    constexpr int kSU = 4;
+    const int ne = min(NS, kEgSelCache) * 16;
+    for (int e0 = tid; e0 < ne; e0 += kEgThreads * kSU) {
+      int t[kSU];
+#pragma unroll
+      for (int u = 0; u < kSU; ++u) {
+        const int e = e0 + kEgThreads * u;
+        t[u] = e < ne ? a.sel[(int64_t)r * NS + (e >> 4)] : -1;
+      }
+      uint4 x[kSU];
+#pragma unroll
+      for (int u = 0; u < kSU; ++u) {
+        const int e = e0 + kEgThreads * u;
+        x[u] = (t[u] >= 0 && t[u] < a.Lmax) ? __ldg(reinterpret_cast<const uint4*>(Kr + (int64_t)t[u] * kD + (e & 15) * 8))
+                                            : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < kSU; ++u) {
+        const int e = e0 + kEgThreads * u;
+        if (t[u] >= 0 && t[u] < a.Lmax) *reinterpret_cast<uint4*>(S.selk + (e >> 4) * kD + (e & 15) * 8) = x[u];
+      }
+    }
   }
   __syncthreads();
   float qv[4], q2[4];

@@ -65,17 +65,38 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
   const int cstage = min(C, kIuCentCache);
   const float* ce = a.cent + (int64_t)r * C * kRC;
   const float* Uk = a.U + (int64_t)kv * kD * kRQ;
-  for (int i = tid; i < kD * kRQ / 4; i += 128)
-    reinterpret_cast<float4*>(sU)[i] = __ldg(reinterpret_cast<const float4*>(Uk) + i);
-  for (int i = tid; i < kD * kRC / 8; i += 128)
-    reinterpret_cast<uint4*>(sW)[i] = __ldg(reinterpret_cast<const uint4*>(a.W + (int64_t)r * kD * kRC) + i);
-  for (int i = tid; i < cstage * kRC / 4; i += 128)
-    reinterpret_cast<float4*>(iu_cent)[i] = __ldg(reinterpret_cast<const float4*>(ce) + i);
+  // Every thread issues all of its loads (U, W, centroids, the new K / V element, q) before it stores
+  // any of them, so the staging costs one memory round trip.
+  constexpr int kUV = kD * kRQ / 4 / 128;  // float4 of U per thread (8)
+  constexpr int kWV = kD * kRC / 8 / 128;  // uint4 of W per thread (2)
+  constexpr int kCV = kIuCentCache * kRC / 4 / 128;  // float4 of centroids per thread, at most (8)
+  const int ncv = cstage * kRC / 4;
+  float4 ub[kUV], cb[kCV];
+  uint4 wb[kWV];
+#pragma unroll
+  for (int u = 0; u < kUV; ++u) ub[u] = __ldg(reinterpret_cast<const float4*>(Uk) + tid + 128 * u);
+#pragma unroll
+  for (int u = 0; u < kWV; ++u)
+    wb[u] = __ldg(reinterpret_cast<const uint4*>(a.W + (int64_t)r * kD * kRC) + tid + 128 * u);
+#pragma unroll
+  for (int u = 0; u < kCV; ++u)
+    cb[u] = tid + 128 * u < ncv ? __ldg(reinterpret_cast<const float4*>(ce) + tid + 128 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+  __nv_bfloat16 kb = __float2bfloat16_rn(0.f), vb = kb, qb = kb;
   if (have_tok) {
-    kf[tid] = __bfloat162float(a.K[((int64_t)kv * a.Lmax + pos) * kD + tid]);
-    vf[tid] = __bfloat162float(a.V[((int64_t)kv * a.Lmax + pos) * kD + tid]);
+    kb = a.K[((int64_t)kv * a.Lmax + pos) * kD + tid];
+    vb = a.V[((int64_t)kv * a.Lmax + pos) * kD + tid];
   }
-  if (a.q != nullptr) qf[tid] = __bfloat162float(a.q[(int64_t)r * a.q_stride + tid]);
+  if (a.q != nullptr) qb = a.q[(int64_t)r * a.q_stride + tid];
+#pragma unroll
+  for (int u = 0; u < kUV; ++u) reinterpret_cast<float4*>(sU)[tid + 128 * u] = ub[u];
+#pragma unroll
+  for (int u = 0; u < kWV; ++u) reinterpret_cast<uint4*>(sW)[tid + 128 * u] = wb[u];
+#pragma unroll
+  for (int u = 0; u < kCV; ++u)
+    if (tid + 128 * u < ncv) reinterpret_cast<float4*>(iu_cent)[tid + 128 * u] = cb[u];
+  kf[tid] = __bfloat162float(kb);
+  vf[tid] = __bfloat162float(vb);
+  qf[tid] = __bfloat162float(qb);
   __syncthreads();
   if (warp == 0) {  // query projection zq[r, j] = bf16((q . U[:, j]) * scale_j), d ascending
     if (a.q != nullptr) {
