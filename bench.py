@@ -216,7 +216,8 @@ class GraphStep:
 
 def stage_profile(m, Mth, gs, iters):
     """Each kernel of the step timed alone on the current stream: CUDA events around single launches,
-    L2 flushed (a 256 MB write) before each, mean over `iters`; with its algorithmic bytes per launch
+    L2 flushed (a 256 MB write) before each and the GPU kept busy while the host enqueues the launch
+    (so host launch overhead is not timed), mean over `iters`; with its algorithmic bytes per launch
     (unique bytes the stage must move: inputs read once, outputs written once, no on-chip intermediates)."""
     from openattention_b200 import selection as S
     from openattention_b200.geometry import D, HKV, HQ, step_split
@@ -243,6 +244,9 @@ def stage_profile(m, Mth, gs, iters):
             if prep:
                 prep()
             flush.zero_()
+            # a bounded spin (about 0.2 ms) keeps the GPU busy while the host enqueues the launch, so
+            # the events time the kernel and not the host's launch overhead
+            torch.cuda._sleep(400_000)
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             fn()

@@ -1944,8 +1944,7 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, 1, mem, cstart,
                clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};
-    cudaError_t e = cudaFuncSetAttribute(topq_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_ts);
-    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+    if (int rc0 = oa_smem_opt_in(reinterpret_cast<const void*>(topq_stream_kernel), smem_ts, fn)) return rc0;
     const int grid = (int)std::min<int64_t>(R, sms);
     topq_stream_kernel<<<grid, kTsThreads, smem_ts, st>>>(a, (int)R, (int)spill_bytes, key_cap);
     return oa_check_launch(fn);
@@ -1958,8 +1957,7 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
     uint16_t* ck = static_cast<uint16_t*>(workspace);
     const int64_t ckw = ck_stride(Lmax);
     const size_t smem = (size_t)kPmChunk * 2;
-    cudaError_t e = cudaFuncSetAttribute(topq_permute_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+    if (int rc0 = oa_smem_opt_in(reinterpret_cast<const void*>(topq_permute_kernel), smem, fn)) return rc0;
     topq_permute_kernel<<<(unsigned)R, kPmThreads, smem, st>>>(a, ck, ckw);
     int rc = oa_check_launch(fn);
     if (rc != OA_OK) return rc;
@@ -1971,8 +1969,7 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
   const bool in_smem = spill_bytes <= 160 * 1024;  // larger rows read their keys from global memory
   a.smem_keys = in_smem ? 1 : 0;
   const size_t smem = in_smem ? spill_bytes : 16;
-  cudaError_t e = cudaFuncSetAttribute(topq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
+  if (int rc0 = oa_smem_opt_in(reinterpret_cast<const void*>(topq_kernel), smem, fn)) return rc0;
   topq_kernel<<<(unsigned)R, kTqThreads, smem, st>>>(a);
   return oa_check_launch(fn);
 }
