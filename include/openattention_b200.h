@@ -126,6 +126,16 @@ int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64
                     int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv, int32_t* reclist, int32_t* reccnt,
                     int rmax, const void* q, int64_t q_stride, void* zq, const int32_t* n_dev, void* stream);
 
+/* Runner helper with no counterpart in the reference (its decode loop does this with two index
+ * copies and two counter increments): appends one token per request to the K/V caches in one
+ * launch.  k_new, v_new (B, 8, 128) bf16 contiguous are written at position p = n_dev[0] + offset
+ * of K, V (B, 8, Lmax, 128) (nothing is written when p is outside [0, Lmax)); then, if advance,
+ * n_dev[0] becomes n_dev[0] + 1 and, if kv_idx is not NULL, kv_idx[0] (int64) the old n_dev[0].
+ * A decode step that appends before the index update uses offset 0 and advance 1; a layer loop
+ * that advanced the counters already uses offset -1 and advance 0. */
+int oa_append_kv(void* K, void* V, int64_t B, int64_t Lmax, const void* k_new, const void* v_new, int32_t* n_dev,
+                 int offset, int advance, int64_t* kv_idx, void* stream);
+
 /* QGS scan: scores (B*32, score_stride) bf16 = exact int8 dot products of codes and zq, rounded to
  * fp32 then bf16, -inf for t < ns and t >= n - nl; tile_max (B*32, tile_max_stride) fp32 = maximum
  * of each 32-token tile (tile_max_stride >= ceil(Lmax / 32)).  Replaces _k_qgs_scan_tm (inference/graph_runner.py:100-120).

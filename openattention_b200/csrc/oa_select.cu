@@ -562,6 +562,32 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   }
 }
 
+// ------------------------------------------------------------------------ token append (runner helper)
+// One CTA: the new token's K and V rows of every (request, KV head) are written at position
+// n + offset (n = n_dev[0] as read at the start); then, with `advance`, n_dev[0] = n + 1 and
+// kv_idx[0] = n.  A single CTA so that every row is written before the counters change.
+constexpr int kApThreads = 1024;
+__global__ void __launch_bounds__(kApThreads) append_kv_kernel(__nv_bfloat16* K, __nv_bfloat16* V, int rows, int Lmax,
+                                                             const __nv_bfloat16* k_new, const __nv_bfloat16* v_new,
+                                                             int32_t* n_dev, int offset, int advance, int64_t* kv_idx) {
+  const int n = *n_dev;
+  const int p = n + offset;
+  if (p >= 0 && p < Lmax) {
+    const int vec = rows * kD / 8;  // 16-byte vectors per tensor
+    for (int i = threadIdx.x; i < 2 * vec; i += kApThreads) {
+      const int t = i < vec ? 0 : 1, j = i - t * vec;
+      const int row = j / (kD / 8), part = j - row * (kD / 8);
+      const uint4 x = reinterpret_cast<const uint4*>(t ? v_new : k_new)[j];
+      reinterpret_cast<uint4*>((t ? V : K) + ((int64_t)row * Lmax + p) * kD)[part] = x;
+    }
+  }
+  __syncthreads();
+  if (advance && threadIdx.x == 0) {
+    *n_dev = n + 1;
+    if (kv_idx != nullptr) *kv_idx = n;
+  }
+}
+
 }  // namespace
 }  // namespace oa
 
@@ -589,6 +615,20 @@ extern "C" int oa_index_update(const void* K, const void* V, int64_t B, int64_t 
   OA_REQUIRE(oa_aligned16(cent) && oa_aligned16(U) && oa_aligned16(W), "%s: U / W / cent must be 16-byte aligned", fn);
   if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(index_update_kernel), smem, fn)) return rc;
   index_update_kernel<<<(unsigned)(B * kHQ), 128, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  return oa_check_launch(fn);
+}
+
+extern "C" int oa_append_kv(void* K, void* V, int64_t B, int64_t Lmax, const void* k_new, const void* v_new,
+                            int32_t* n_dev, int offset, int advance, int64_t* kv_idx, void* stream) {
+  const char* fn = "oa_append_kv";
+  OA_REQUIRE(B > 0 && Lmax > 0 && Lmax < (1ll << 31) && B * kHKV * kD / 8 * 2 < (1ll << 31), "%s: bad sizes", fn);
+  OA_REQUIRE(K && V && k_new && v_new && n_dev, "%s: null pointer", fn);
+  OA_REQUIRE(oa_aligned16(K) && oa_aligned16(V) && oa_aligned16(k_new) && oa_aligned16(v_new),
+             "%s: K, V, k_new and v_new must be 16-byte aligned", fn);
+  append_kv_kernel<<<1, kApThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<__nv_bfloat16*>(K), static_cast<__nv_bfloat16*>(V), (int)(B * kHKV), (int)Lmax,
+      static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new), n_dev, offset,
+      advance ? 1 : 0, kv_idx);
   return oa_check_launch(fn);
 }
 

@@ -22,6 +22,7 @@ import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from . import method as Mth
+from . import selection as S
 from .geometry import D, HKV, HQ, llama31_inv_freq
 
 
@@ -143,8 +144,8 @@ class RandomLlama:
             q = self._rope(qkv[:, :HQ * D].view(B, HQ, D), cos, sin)
             k = self._rope(qkv[:, HQ * D:(HQ + HKV) * D].view(B, HKV, D), cos, sin)
             v = qkv[:, (HQ + HKV) * D:].view(B, HKV, D)
-            self.K[l].index_copy_(2, C.kv_idx, k.unsqueeze(2))
-            self.V[l].index_copy_(2, C.kv_idx, v.unsqueeze(2))
+            # this layer's new K/V rows at position n - 1 (the counters advanced at the step's start)
+            S.append_kv(self.K[l], self.V[l], k.contiguous(), v.contiguous(), C.n_dev, offset=-1, advance=False)
             o = self.method.decode(l, q.view(B, HQ, 1, D), n_host)         # (B, 32, 1, D)
             x = x + o.reshape(B, HQ * D) @ self.wo[l]
             x = x + self._mlp(self._rms(x, self.ln2[l]), l)

@@ -25,6 +25,21 @@ def _need(name, t, dtype, shape=None):
         raise RuntimeError(f"{name}: shape {tuple(t.shape)} != {tuple(shape)}")
 
 
+def append_kv(K, V, k_new, v_new, n_dev, offset=0, advance=True, kv_idx=None):
+    """Writes the new token's K/V rows (B, 8, 128) at position n_dev + offset of the caches (B, 8, Lmax,
+    128) in one launch; with advance, n_dev += 1 and kv_idx (int64, optional) = the old n_dev."""
+    B, _, Lmax, _ = K.shape
+    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("V", V, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("k_new", k_new, torch.bfloat16, (B, HKV, D))
+    _need("v_new", v_new, torch.bfloat16, (B, HKV, D))
+    _need("n_dev", n_dev, torch.int32, (1,))
+    if kv_idx is not None:
+        _need("kv_idx", kv_idx, torch.int64, (1,))
+    _lib.call("oa_append_kv", _ptr(K), _ptr(V), B, Lmax, _ptr(k_new), _ptr(v_new), _ptr(n_dev), int(offset),
+              1 if advance else 0, _ptr(kv_idx), _stream(K))
+
+
 def index_update(K, V, st, n_dev, q=None, zq=None):
     """New token at n-1 joins the index; with q (B*32, D) also writes zq (B*32, 32) bf16."""
     B, _, Lmax, _ = K.shape

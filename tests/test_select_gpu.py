@@ -143,3 +143,28 @@ def test_topq_long_rows_matches_oracle(use_ws):
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     assert np.array_equal(exp_idx.cpu().numpy(), exp_ref)
+
+
+@pytest.mark.parametrize("offset,advance", [(0, True), (-1, False)])
+def test_append_kv_matches_index_copy(offset, advance):
+    """The runner helper writes the new token's K/V rows where two index copies would, and advances
+    the counters as the decode loop's increments do."""
+    dev = torch.device("cuda")
+    B, Lmax, n = 3, 200, 57
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    K = torch.randn(B, 8, Lmax, 128, generator=g, device=dev).to(torch.bfloat16)
+    V = torch.randn(B, 8, Lmax, 128, generator=g, device=dev).to(torch.bfloat16)
+    kn = torch.randn(B, 8, 128, generator=g, device=dev).to(torch.bfloat16)
+    vn = torch.randn(B, 8, 128, generator=g, device=dev).to(torch.bfloat16)
+    Kr, Vr = K.clone(), V.clone()
+    n_dev = torch.tensor([n], dtype=torch.int32, device=dev)
+    kv_idx = torch.tensor([n - 1], dtype=torch.int64, device=dev)
+    S.append_kv(K, V, kn, vn, n_dev, offset=offset, advance=advance, kv_idx=kv_idx)
+    p = n + offset
+    Kr[:, :, p] = kn
+    Vr[:, :, p] = vn
+    torch.cuda.synchronize()
+    assert torch.equal(K, Kr) and torch.equal(V, Vr)
+    assert int(n_dev.item()) == (n + 1 if advance else n)
+    assert int(kv_idx.item()) == (n if advance else n - 1)
