@@ -574,11 +574,24 @@ __global__ void __launch_bounds__(kApThreads) append_kv_kernel(__nv_bfloat16* K,
   const int p = n + offset;
   if (p >= 0 && p < Lmax) {
     const int vec = rows * kD / 8;  // 16-byte vectors per tensor
-    for (int i = threadIdx.x; i < 2 * vec; i += kApThreads) {
-      const int t = i < vec ? 0 : 1, j = i - t * vec;
-      const int row = j / (kD / 8), part = j - row * (kD / 8);
-      const uint4 x = reinterpret_cast<const uint4*>(t ? v_new : k_new)[j];
-      reinterpret_cast<uint4*>((t ? V : K) + ((int64_t)row * Lmax + p) * kD)[part] = x;
+    constexpr int kU = 8;           // loads a thread issues before its stores
+    for (int i0 = threadIdx.x; i0 < 2 * vec; i0 += kApThreads * kU) {
+      uint4 x[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int i = i0 + kApThreads * u;
+        const int t = i < vec ? 0 : 1, j = i - t * vec;
+        x[u] = i < 2 * vec ? reinterpret_cast<const uint4*>(t ? v_new : k_new)[j] : make_uint4(0u, 0u, 0u, 0u);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int i = i0 + kApThreads * u;
+        if (i < 2 * vec) {
+          const int t = i < vec ? 0 : 1, j = i - t * vec;
+          const int row = j / (kD / 8), part = j - row * (kD / 8);
+          reinterpret_cast<uint4*>((t ? V : K) + ((int64_t)row * Lmax + p) * kD)[part] = x[u];
+        }
+      }
     }
   }
   __syncthreads();
