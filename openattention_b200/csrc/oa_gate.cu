@@ -749,8 +749,11 @@ __device__ __forceinline__ void topq_keys_regs(const TsRow& w, int cs, int nmem,
   if (lane < q && my_idx != 0x7fffffff && rank < lim) win[rank] = ts_enc(my_idx, cs, nmem, rec);
 }
 
+// parts > 1 (fewer rows than SMs): work item w is row w / parts, clusters [p C / parts, (p+1) C / parts)
+// of it for p = w % parts; each item's CTA stages the whole score row but keys and selects only its
+// clusters' members (their CSR range), so a row's work is spread over `parts` SMs.
 __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqArgs a, int R, int spill_cap,
-                                                                    int key_cap) {
+                                                                    int key_cap, int parts) {
   extern __shared__ __align__(128) unsigned char ts_smem[];
   uint16_t* s_spill = reinterpret_cast<uint16_t*>(ts_smem);
   uint16_t* s_key = reinterpret_cast<uint16_t*>(ts_smem + spill_cap);
@@ -817,25 +820,29 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
       for (int c = lane; c < C; c += 32) s_ord_[set][c] = c;
     }
   };
-  auto winners_out = [&](int row, int cnt) {  // CSR slots / generated positions -> positions
+  auto winners_out = [&](int row, int lo, int hi) {  // CSR slots / generated positions -> positions
     int32_t* pout = a.exp + (int64_t)row * a.E;
     const int32_t* pm = a.mem + (int64_t)row * a.Lmax;
-    for (int i = tid; i < cnt; i += kTsThreads) {
+    for (int i = lo + tid; i < hi; i += kTsThreads) {
       const int e = s_win[i];
       pout[i] = e >= 0 ? pm[e] : -e - 1;
     }
   };
+  const int W = R * parts;  // work items
   if (tid == 0) {
     mbar_init(bar);
-    if (nbytes) bulk_load(s_spill, a.scores + (int64_t)blockIdx.x * a.sw, nbytes, bar);
+    if (nbytes) bulk_load(s_spill, a.scores + (int64_t)(blockIdx.x / parts) * a.sw, nbytes, bar);
   }
-  load_meta(blockIdx.x, 0);
+  load_meta(blockIdx.x / parts, 0);
   __syncthreads();
   if (warp == 0) prefix(0);
   const unsigned lt = (1u << lane) - 1u;
-  int it = 0, cur = 0, prev_r = -1, prev_cnt = 0;
-  for (int r = blockIdx.x; r < R; r += gridDim.x, ++it, cur ^= 1) {
-    const int nr = r + (int)gridDim.x;
+  int it = 0, cur = 0, prev_r = -1, prev_lo = 0, prev_hi = 0;
+  for (int wi = blockIdx.x; wi < W; wi += gridDim.x, ++it, cur ^= 1) {
+    const int r = wi / parts, part = wi - r * parts;
+    const int nwi = wi + (int)gridDim.x;
+    const int nr = nwi < W ? nwi / parts : R;  // the next item's row (R: none)
+    const int c_lo = part * C / parts, c_hi = (part + 1) * C / parts;
     const int64_t rC = (int64_t)r * C;
     const int* s_q = s_q_[cur];
     const int* s_cs = s_cs_[cur];
@@ -849,20 +856,21 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
       return;
     }
     // overlapping phase 1: the previous row's winner positions, the next row's metadata, this row's pads
-    if (prev_r >= 0) winners_out(prev_r, prev_cnt);
+    if (prev_r >= 0) winners_out(prev_r, prev_lo, prev_hi);
     if (nr < R) load_meta(nr, cur ^ 1);
     int32_t* out = a.exp + (int64_t)r * a.E;
-    for (int i = s_base[C] + tid; i < a.E; i += kTsThreads) out[i] = -1;
+    if (part == 0)
+      for (int i = s_base[C] + tid; i < a.E; i += kTsThreads) out[i] = -1;
     if (tid == 0) s_next = 0;
     // ---- phase 1: member keys in CSR order (key slot = member index + mo, so every 16-byte vector of
     // the member list becomes one 8-byte store of four keys), generated-position keys
-    const int total = s_cs[C - 1] + s_cl[C - 1];
+    const int m_lo = s_cs[c_lo], m_hi = s_cs[c_hi - 1] + s_cl[c_hi - 1];  // this item's members
     const int32_t* mrow = a.mem + (int64_t)r * a.Lmax;
     const int mo = (int)((reinterpret_cast<uintptr_t>(mrow) & 15u) >> 2);
     const int32_t* m0 = mrow - mo;
-    const int nvec = (total + mo + 3) >> 2;
+    const int nvec = (m_hi + mo + 3) >> 2;
     const uint32_t lim = (uint32_t)(spill_cap / 2 - 1);  // list entries are positions; clamp keeps reads inside
-    for (int v0 = tid; v0 < nvec; v0 += kTsThreads * kTsU) {
+    for (int v0 = ((m_lo + mo) >> 2) + tid; v0 < nvec; v0 += kTsThreads * kTsU) {
       int4 x[kTsU];
 #pragma unroll
       for (int u = 0; u < kTsU; ++u) {
@@ -909,7 +917,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
         do {
           i = atomicAdd(&s_next, 1);
           c = i < C ? s_ord[i] : C;
-        } while (c < C && s_q[c] <= 0);
+        } while (c < C && (s_q[c] <= 0 || c < c_lo || c >= c_hi));
       }
       c = __shfl_sync(0xffffffffu, c, 0);
       if (c >= C) break;
@@ -1019,9 +1027,10 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
     }
     __syncthreads();  // winners complete; keys and the cluster counter are reused by the next row
     prev_r = r;
-    prev_cnt = min(s_base[C], a.E);
+    prev_lo = min(s_base[c_lo], a.E);
+    prev_hi = min(s_base[c_hi], a.E);
   }
-  if (prev_r >= 0) winners_out(prev_r, prev_cnt);
+  if (prev_r >= 0) winners_out(prev_r, prev_lo, prev_hi);
 }
 
 // ------------------------------------------------------------------------ top-q, long rows
@@ -1945,8 +1954,10 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
     TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, 1, mem, cstart,
                clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};
     if (int rc0 = oa_smem_opt_in(reinterpret_cast<const void*>(topq_stream_kernel), smem_ts, fn)) return rc0;
-    const int grid = (int)std::min<int64_t>(R, sms);
-    topq_stream_kernel<<<grid, kTsThreads, smem_ts, st>>>(a, (int)R, (int)spill_bytes, key_cap);
+    // fewer rows than SMs: split each row's clusters over up to 4 CTAs
+    const int parts = (int)std::max<int64_t>(1, std::min<int64_t>({4, sms / R, C}));
+    const int grid = (int)std::min<int64_t>(R * parts, sms);
+    topq_stream_kernel<<<grid, kTsThreads, smem_ts, st>>>(a, (int)R, (int)spill_bytes, key_cap, parts);
     return oa_check_launch(fn);
   }
   TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, 0, mem, cstart,
