@@ -126,6 +126,17 @@ int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64
                     int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv, int32_t* reclist, int32_t* reccnt,
                     int rmax, const void* q, int64_t q_stride, void* zq, const int32_t* n_dev, void* stream);
 
+/* oa_index_update with the new token's K/V write fused in (the "fused KV-write + index update" step
+ * that precedes the path on every layer; the reference writes the cache in its attention hook,
+ * graph_runner.py:479-480, then runs _k_index_update_d2, ours_graph.py:43-90): k_new, v_new (B, 8, 128)
+ * bf16 contiguous are the new token's rows; they are written into K, V at position n_dev[0] - 1 and
+ * the index is updated from them, in one launch.  Other arguments as oa_index_update. */
+int oa_index_update_append(void* K, void* V, int64_t B, int64_t Lmax, int64_t C, const void* k_new, const void* v_new,
+                           int8_t* codes, const float* U, const float* scale, const void* W, const float* colmean,
+                           const float* cent, int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv,
+                           int32_t* reclist, int32_t* reccnt, int rmax, const void* q, int64_t q_stride, void* zq,
+                           const int32_t* n_dev, void* stream);
+
 /* Runner helper with no counterpart in the reference (its decode loop does this with two index
  * copies and two counter increments): appends one token per request to the K/V caches in one
  * launch.  k_new, v_new (B, 8, 128) bf16 contiguous are written at position p = n_dev[0] + offset

@@ -32,6 +32,8 @@ SIGNATURES = {
                                              I64, I32, I64, I64, I64, I64, F32, I32, P]),
     "oa_index_update": (I32, [P, P, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, P, I64, P, P, P]),
     "oa_append_kv": (I32, [P, P, I64, I64, P, P, P, I32, I32, P, P]),
+    "oa_index_update_append": (I32, [P, P, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, P,
+                                     I64, P, P, P]),
     "oa_qgs_scan": (I32, [P, P, I64, I64, P, I32, I32, P, I64, P, I64, P, P]),
     "oa_qgs_select": (I32, [P, I64, P, I64, I64, I64, P, I32, I32, I32, P, P]),
     "oa_errorgate_waterfill": (I32, [P, I64, P, I64, I64, I64, P, P, I64, P, P, P, F32, P, P, P, P, P, P]),

@@ -40,6 +40,10 @@ struct IndexArgs {
   __nv_bfloat16* zq;
   const int32_t* n_dev;
   int Lmax, C;
+  // optional: the new token's K / V rows (B*8, 128) bf16; the key and value are taken from here and
+  // the first query head's CTA of each KV head writes them into K / V at position n - 1
+  const __nv_bfloat16* k_new;
+  const __nv_bfloat16* v_new;
 };
 
 // One CTA per QUERY head r = kv*4 + g (so a batch's whole index update is resident at once): the
@@ -83,8 +87,17 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
     cb[u] = tid + 128 * u < ncv ? __ldg(reinterpret_cast<const float4*>(ce) + tid + 128 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
   __nv_bfloat16 kb = __float2bfloat16_rn(0.f), vb = kb, qb = kb;
   if (have_tok) {
-    kb = a.K[((int64_t)kv * a.Lmax + pos) * kD + tid];
-    vb = a.V[((int64_t)kv * a.Lmax + pos) * kD + tid];
+    if (a.k_new != nullptr) {
+      kb = a.k_new[(int64_t)kv * kD + tid];
+      vb = a.v_new[(int64_t)kv * kD + tid];
+      if (g == 0) {  // the cache write of the fused append (read again only by later kernels)
+        const_cast<__nv_bfloat16*>(a.K)[((int64_t)kv * a.Lmax + pos) * kD + tid] = kb;
+        const_cast<__nv_bfloat16*>(a.V)[((int64_t)kv * a.Lmax + pos) * kD + tid] = vb;
+      }
+    } else {
+      kb = a.K[((int64_t)kv * a.Lmax + pos) * kD + tid];
+      vb = a.V[((int64_t)kv * a.Lmax + pos) * kD + tid];
+    }
   }
   if (a.q != nullptr) qb = a.q[(int64_t)r * a.q_stride + tid];
 #pragma unroll
@@ -607,12 +620,12 @@ __global__ void __launch_bounds__(kApThreads) append_kv_kernel(__nv_bfloat16* K,
 // ------------------------------------------------------------------------ C ABI
 using namespace oa;
 
-extern "C" int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, int8_t* codes,
-                               const float* U, const float* scale, const void* W, const float* colmean,
-                               const float* cent, int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv,
-                               int32_t* reclist, int32_t* reccnt, int rmax, const void* q, int64_t q_stride,
-                               void* zq, const int32_t* n_dev, void* stream) {
-  const char* fn = "oa_index_update";
+namespace {
+int index_update_entry(const char* fn, void* K, void* V, int64_t B, int64_t Lmax, int64_t C, int8_t* codes,
+                       const float* U, const float* scale, const void* W, const float* colmean, const float* cent,
+                       int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv, int32_t* reclist, int32_t* reccnt,
+                       int rmax, const void* q, int64_t q_stride, void* zq, const int32_t* n_dev, const void* k_new,
+                       const void* v_new, void* stream) {
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= 4096, "%s: bad sizes B=%lld Lmax=%lld C=%lld", fn, (long long)B,
              (long long)Lmax, (long long)C);
   OA_REQUIRE(Lmax < (1ll << 31) / 1, "%s: Lmax too large", fn);
@@ -620,15 +633,39 @@ extern "C" int oa_index_update(const void* K, const void* V, int64_t B, int64_t 
              "%s: null pointer", fn);
   OA_REQUIRE(q == nullptr || zq != nullptr, "%s: q given without zq", fn);
   OA_REQUIRE(reclist == nullptr || (reccnt != nullptr && rmax > 0), "%s: reclist needs reccnt and rmax > 0", fn);
+  OA_REQUIRE((k_new == nullptr) == (v_new == nullptr), "%s: k_new and v_new are given together", fn);
   IndexArgs a{static_cast<const __nv_bfloat16*>(K), static_cast<const __nv_bfloat16*>(V), codes, U, scale,
               static_cast<const __nv_bfloat16*>(W), colmean, cent, asg, nb, Sk, Sk2, Sv, reclist, reccnt, rmax,
               static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<__nv_bfloat16*>(zq), n_dev,
-              (int)Lmax, (int)C};
+              (int)Lmax, (int)C, static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new)};
   const size_t smem = (size_t)std::min<int64_t>(C, kIuCentCache) * kRC * sizeof(float);
   OA_REQUIRE(oa_aligned16(cent) && oa_aligned16(U) && oa_aligned16(W), "%s: U / W / cent must be 16-byte aligned", fn);
   if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(index_update_kernel), smem, fn)) return rc;
   index_update_kernel<<<(unsigned)(B * kHQ), 128, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
+}
+}  // namespace
+
+extern "C" int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, int8_t* codes,
+                               const float* U, const float* scale, const void* W, const float* colmean,
+                               const float* cent, int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv,
+                               int32_t* reclist, int32_t* reccnt, int rmax, const void* q, int64_t q_stride,
+                               void* zq, const int32_t* n_dev, void* stream) {
+  return index_update_entry("oa_index_update", const_cast<void*>(K), const_cast<void*>(V), B, Lmax, C, codes, U,
+                            scale, W, colmean, cent, asg, nb, Sk, Sk2, Sv, reclist, reccnt, rmax, q, q_stride, zq,
+                            n_dev, nullptr, nullptr, stream);
+}
+
+extern "C" int oa_index_update_append(void* K, void* V, int64_t B, int64_t Lmax, int64_t C, const void* k_new,
+                                      const void* v_new, int8_t* codes, const float* U, const float* scale,
+                                      const void* W, const float* colmean, const float* cent, int32_t* asg, float* nb,
+                                      float* Sk, float* Sk2, float* Sv, int32_t* reclist, int32_t* reccnt, int rmax,
+                                      const void* q, int64_t q_stride, void* zq, const int32_t* n_dev,
+                                      void* stream) {
+  const char* fn = "oa_index_update_append";
+  OA_REQUIRE(k_new && v_new, "%s: null k_new / v_new", fn);
+  return index_update_entry(fn, K, V, B, Lmax, C, codes, U, scale, W, colmean, cent, asg, nb, Sk, Sk2, Sv, reclist,
+                            reccnt, rmax, q, q_stride, zq, n_dev, k_new, v_new, stream);
 }
 
 extern "C" int oa_append_kv(void* K, void* V, int64_t B, int64_t Lmax, const void* k_new, const void* v_new,

@@ -22,7 +22,6 @@ import torch.nn.functional as F
 from torch.nn.attention import SDPBackend, sdpa_kernel
 
 from . import method as Mth
-from . import selection as S
 from .geometry import D, HKV, HQ, llama31_inv_freq
 
 
@@ -144,9 +143,9 @@ class RandomLlama:
             q = self._rope(qkv[:, :HQ * D].view(B, HQ, D), cos, sin)
             k = self._rope(qkv[:, HQ * D:(HQ + HKV) * D].view(B, HKV, D), cos, sin)
             v = qkv[:, (HQ + HKV) * D:].view(B, HKV, D)
-            # this layer's new K/V rows at position n - 1 (the counters advanced at the step's start)
-            S.append_kv(self.K[l], self.V[l], k.contiguous(), v.contiguous(), C.n_dev, offset=-1, advance=False)
-            o = self.method.decode(l, q.view(B, HQ, 1, D), n_host)         # (B, 32, 1, D)
+            # this layer's new K/V rows are written at position n - 1 (the counters advanced at the step's
+            # start) by the index update's launch
+            o = self.method.decode(l, q.view(B, HQ, 1, D), n_host, k_new=k.contiguous(), v_new=v.contiguous())
             x = x + o.reshape(B, HQ * D) @ self.wo[l]
             x = x + self._mlp(self._rms(x, self.ln2[l]), l)
         logits = self._rms(x, self.norm) @ self.lm_head

@@ -228,7 +228,7 @@ class OursB200:
             self._sel[NS] = torch.zeros(self.R, NS, dtype=torch.int32, device=self.dev)
         return self._sel[NS]
 
-    def select(self, l, q, n, residual=True):
+    def select(self, l, q, n, residual=True, k_new=None, v_new=None):
         """Stages 1-5 of the step: index update + zq, QGS scan + top-k, ErrorGate + water-filling,
         within-cluster top-q and (residual=True) the residual proxies.  Returns (q rows, sel)."""
         st, Lmax = self.st[l], self.Lmax
@@ -239,7 +239,7 @@ class OursB200:
         if not qr.is_contiguous():
             qr = qr.contiguous()
         sel = self._sel_buf(ns + nl + k_top)
-        S.index_update(K, V, st, n_dev, q=qr, zq=self.zq)
+        S.index_update(K, V, st, n_dev, q=qr, zq=self.zq, k_new=k_new, v_new=v_new)
         S.qgs_scan(st["codes"], self.zq, n_dev, ns, nl, self.scores, self.tmax, self.status)
         S.qgs_select(self.scores, self.tmax, Lmax, n_dev, ns, nl, k_top, sel)
         S.errorgate_waterfill(qr, K, st, sel, self.E, self.score, self.nt, self.quota, self.status, zdot=self.zdot)
@@ -253,11 +253,14 @@ class OursB200:
         self.read_frac = (ns + nl + k_top + self.E + 1.5 * self.C) / n
         return qr, sel
 
-    def decode(self, l, q, n):
+    def decode(self, l, q, n, k_new=None, v_new=None):
+        """The reference's decode(l, q, n) (the new token's K/V already in C.K[l] / C.V[l] at n - 1).  With
+        k_new, v_new (B, 8, 128) bf16 the caller leaves that write to the index update, which does it in
+        the same launch (oa_index_update_append)."""
         if not self.FUSED:
-            qr, sel = self.select(l, q, n)
+            qr, sel = self.select(l, q, n, k_new=k_new, v_new=v_new)
             return self.attend(l, qr, sel, self.exp_idx, self.kbar, self.vbar, self.logn)
-        qr, sel = self.select(l, q, n, residual=False)
+        qr, sel = self.select(l, q, n, residual=False, k_new=k_new, v_new=v_new)
         keep = self.keep_proxies
         S.residual_flash(qr, C.K[l], C.V[l], self.st[l], sel, self.exp_idx, self.nt, self.quota, self.out,
                          kbar=self.kbar if keep else None, vbar=self.vbar if keep else None,

@@ -40,8 +40,9 @@ def append_kv(K, V, k_new, v_new, n_dev, offset=0, advance=True, kv_idx=None):
               1 if advance else 0, _ptr(kv_idx), _stream(K))
 
 
-def index_update(K, V, st, n_dev, q=None, zq=None):
-    """New token at n-1 joins the index; with q (B*32, D) also writes zq (B*32, 32) bf16."""
+def index_update(K, V, st, n_dev, q=None, zq=None, k_new=None, v_new=None):
+    """New token at n-1 joins the index; with q (B*32, D) also writes zq (B*32, 32) bf16.  With k_new,
+    v_new (B, 8, 128) the token's rows are written into K, V at n-1 by the same launch."""
     B, _, Lmax, _ = K.shape
     C = st["nb"].shape[-1]
     _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
@@ -52,11 +53,16 @@ def index_update(K, V, st, n_dev, q=None, zq=None):
             raise RuntimeError("q must be (B*32, 128) bf16 with a contiguous last dim")
         _need("zq", zq, torch.bfloat16, (B * HQ, RQ))
     rec = st.get("reclist")
-    _lib.call("oa_index_update", _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["codes"]), _ptr(st["U"]), _ptr(st["scale"]),
-              _ptr(st["W"]), _ptr(st["colmean"]), _ptr(st["cent"]), _ptr(st["asg"]), _ptr(st["nb"]),
-              _ptr(st["Sk"]), _ptr(st["Sk2"]), _ptr(st["Sv"]), _ptr(rec), _ptr(st.get("reccnt")),
-              0 if rec is None else rec.shape[-1], _ptr(q), 0 if q is None else q.stride(0), _ptr(zq), _ptr(n_dev),
-              _stream(K))
+    rmax = 0 if rec is None else rec.shape[-1]
+    tail = (_ptr(st["codes"]), _ptr(st["U"]), _ptr(st["scale"]), _ptr(st["W"]), _ptr(st["colmean"]), _ptr(st["cent"]),
+            _ptr(st["asg"]), _ptr(st["nb"]), _ptr(st["Sk"]), _ptr(st["Sk2"]), _ptr(st["Sv"]), _ptr(rec),
+            _ptr(st.get("reccnt")), rmax, _ptr(q), 0 if q is None else q.stride(0), _ptr(zq), _ptr(n_dev), _stream(K))
+    if k_new is None:
+        _lib.call("oa_index_update", _ptr(K), _ptr(V), B, Lmax, C, *tail)
+        return
+    _need("k_new", k_new, torch.bfloat16, (B, HKV, D))
+    _need("v_new", v_new, torch.bfloat16, (B, HKV, D))
+    _lib.call("oa_index_update_append", _ptr(K), _ptr(V), B, Lmax, C, _ptr(k_new), _ptr(v_new), *tail)
 
 
 def qgs_scan(codes, zq, n_dev, ns, nl, scores, tile_max, status=None):

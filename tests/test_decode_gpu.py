@@ -235,6 +235,53 @@ def test_decode_graph_replay_matches_eager():
     assert torch.equal(outs["eager"], outs["graph"])
 
 
+def test_decode_with_fused_kv_append_matches_written_cache():
+    """decode(l, q, n, k_new, v_new): the index update's launch writes the new token's K/V rows; the
+    caches, the index state and the outputs equal those of the reference contract (rows written
+    first, then decode), over several steps."""
+    from openattention_b200 import synth
+    B, n0, steps, rho = 2, 2048, 3, 0.01
+    Lmax = n0 + steps + 8
+    dev = "cuda"
+    K = torch.zeros(B, 8, Lmax, D, dtype=torch.bfloat16, device=dev)
+    V = torch.zeros_like(K)
+    for b in range(B):
+        Kb, Vb, mu = synth.kv_numpy(7 + b, n0, Lmax)
+        K[b], V[b] = Kb.to(dev), Vb.to(dev)
+    qpre = synth.queries_numpy(8, HQ * n0).view(1, HQ, n0, D).to(dev)
+    res = {}
+    for mode in ("written", "fused"):
+        Kc, Vc = K.clone(), V.clone()
+        Mth.C.K, Mth.C.V, Mth.C.qlen = [Kc], [Vc], [40] * B
+        Mth.C.n_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        Mth.C.n0_dev = torch.full((1,), n0, dtype=torch.int32, device=dev)
+        m = _method(B, Lmax, rho)
+        for b in range(B):
+            m.build(0, b, qpre, n0)
+        outs = []
+        for s in range(steps):
+            n = n0 + s + 1
+            g = torch.Generator(device=dev)
+            g.manual_seed(300 + s)
+            kn = torch.randn(B, 8, D, generator=g, device=dev).to(torch.bfloat16)
+            vn = torch.randn(B, 8, D, generator=g, device=dev).to(torch.bfloat16)
+            q = torch.randn(B, HQ, 1, D, generator=g, device=dev).to(torch.bfloat16)
+            Mth.C.n_dev.fill_(n)
+            if mode == "written":
+                Kc[:, :, n - 1], Vc[:, :, n - 1] = kn, vn
+                o = m.decode(0, q, n)
+            else:
+                o = m.decode(0, q, n, k_new=kn, v_new=vn)
+            outs.append(o.clone())
+        torch.cuda.synchronize()
+        res[mode] = (torch.stack(outs), Kc, Vc, {k: v.clone() for k, v in m.st[0].items()})
+    a, b = res["written"], res["fused"]
+    assert torch.equal(a[0], b[0])
+    assert torch.equal(a[1], b[1]) and torch.equal(a[2], b[2])
+    for k in a[3]:
+        assert torch.equal(a[3][k], b[3][k]), k
+
+
 @pytest.mark.parametrize("rho", [0.01, 0.03])
 def test_decode_32k_steps_bit_exact(rho):
     """The GPU-built state of one 32K-token request, then decode steps checked against the oracle:
