@@ -105,6 +105,7 @@ class RandomLlama:
         nxt = torch.empty(B, dtype=torch.long, device=self.dev)
         for b in range(B):
             x = self.embed[tokens[b]]                                      # (T, H)
+            pending = None  # the previous layer's build, finished once this layer's work is enqueued
             for l in range(self.cfg.layers):
                 h = self._rms(x, self.ln1[l])
                 qkv = h @ self.wqkv[l]
@@ -123,7 +124,11 @@ class RandomLlama:
                 for t0 in range(0, T, chunk):                            # MLP in row chunks (activation memory)
                     t1 = min(T, t0 + chunk)
                     x[t0:t1] = x[t0:t1] + self._mlp(self._rms(x[t0:t1], self.ln2[l]), l)
-                self.method.build(l, b, q.unsqueeze(0), T)
+                finish = self.method.build_async(l, b, q.unsqueeze(0), T)
+                if pending is not None:
+                    pending()
+                pending = finish
+            pending()
             logits = self._rms(x[-1:], self.norm) @ self.lm_head
             nxt[b] = logits.float().argmax(-1)[0]
         return nxt

@@ -96,10 +96,22 @@ def query_metric(Mpre_l, inv_freq, scaling, q, T, Qn, win=WIN, P=PQ):
 
 def basis_from_metric(M: torch.Tensor):
     """U (8, D, 32): top-32 eigenvectors of each KV head's mean metric; W (32, D, 16) bf16 =
-    top-16 eigenvectors scaled by sqrt(max(eigenvalue, 0)) (inference/methods_eager.py:520-528)."""
-    _, Ukv = torch.linalg.eigh(M.view(HKV, G, D, D).mean(1))
+    top-16 eigenvectors scaled by sqrt(max(eigenvalue, 0)) (inference/methods_eager.py:520-528).
+
+    The 40 symmetric 128 x 128 eigen-decompositions run on the host (batched LAPACK, about 2.6 MB
+    each way): the device solver takes the matrices one at a time and costs about 90 ms per layer.
+    An eigenvector is defined up to its sign; a flipped column of U changes zq and the codes together
+    (their products, the scores, do not change), and a flipped column of W changes the projected keys
+    and the centroids together, so the selection is the same."""
+    U, W = basis_from_host_metric(M.detach().to("cpu", torch.float32))
+    return U.to(M.device), W.to(M.device)
+
+
+def basis_from_host_metric(Mh: torch.Tensor):
+    """basis_from_metric on a host copy of M (32, D, D) fp32; returns host tensors."""
+    _, Ukv = torch.linalg.eigh(Mh.view(HKV, G, D, D).mean(1))
+    ev, Uq = torch.linalg.eigh(Mh)
     U = Ukv[..., -RQ:].contiguous()
-    ev, Uq = torch.linalg.eigh(M)
     W = (Uq[..., -RC:] * ev[..., -RC:].clamp(min=0).sqrt().unsqueeze(-2)).to(torch.bfloat16).contiguous()
     return U, W
 
@@ -182,12 +194,25 @@ class OursB200:
     def build(self, l, b, q, T):
         """Index of layer l, batch row b after the prefill wrote C.K[l][b, :, :T], C.V[l][b, :, :T];
         q: (1, 32, T, D) prefill queries (the last C.qlen[b] rows are the question)."""
-        st = self.st[l]
-        K1, V1 = C.K[l][b], C.V[l][b]
+        self.build_async(l, b, q, T)()
+
+    def build_async(self, l, b, q, T):
+        """build() in two halves.  Now: the query metric on the device and its copy to pinned host memory
+        (q is not used after this returns).  The returned callable: the host eigen-decomposition, then
+        the device build.  A prefill loop calls it after enqueueing its next layer, so the host half
+        overlaps device work."""
         Qn = C.qlen[b] if C.qlen else 40
         M = query_metric(self.Mpre[l], self.inv_freq, self.scaling, q, T, Qn)
-        U, W = basis_from_metric(M)
-        self.build_from_basis(l, b, U, W, T)
+        Mh = torch.empty(M.shape, dtype=torch.float32, pin_memory=True)
+        Mh.copy_(M, non_blocking=True)
+        done = torch.cuda.Event()
+        done.record()
+
+        def finish():
+            done.synchronize()
+            U, W = basis_from_host_metric(Mh)
+            self.build_from_basis(l, b, U.to(self.dev, non_blocking=True), W.to(self.dev, non_blocking=True), T)
+        return finish
 
     def build_from_basis(self, l, b, U, W, T):
         """Everything of the build after the eigen-decomposition (QGS codes, QGC projection, Lloyd
