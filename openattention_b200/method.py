@@ -83,7 +83,9 @@ def query_metric(Mpre_l, inv_freq, scaling, q, T, Qn, win=WIN, P=PQ):
     dev = q.device
     Mst = rot_avg(Mpre_l, inv_freq, scaling, T, win)
     Pn = min(P, max(Qn - 2, 1))
-    pi = torch.linspace(0, max(Qn - 3, 0), Pn, device=dev).long().unique()
+    # question rows: computed on the host (unique() on the device would stall the host until the device
+    # drains, and the prefill overlaps this with device work), moved by a non-blocking pinned copy
+    pi = torch.linspace(0, max(Qn - 3, 0), Pn).long().unique().pin_memory().to(dev, non_blocking=True)
     qsel = q[0, :, T - Qn:, :].index_select(1, pi).float()
     freqs = (Qn - pi).float().unsqueeze(-1) * inv_freq.to(dev).unsqueeze(0)
     emb = torch.cat([freqs, freqs], -1)
