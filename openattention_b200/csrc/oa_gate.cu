@@ -62,7 +62,6 @@ struct GateArgs {
 // (threads c, c + 64, ...): ranks by counting, the integer prefix of the caps in ratio order (one
 // warp) beside the double suffix sum of the weights (one thread of the other warp).
 constexpr int kEgThreads = 64;
-constexpr int kEgW = kEgThreads / 32;
 constexpr int kEgB = 4;            // clusters per batch per warp
 constexpr int kEgSelCache = 64;    // selected tokens whose K rows are staged in shared memory
 
@@ -78,14 +77,16 @@ size_t eg_smem_bytes(int C, int NS) {
   return c4 * 4 * 18 + ns4 * 4 * 2 + (size_t)std::min(NS, kEgSelCache) * kD * 2;  // 15 fp32 + 3 int per cluster
 }
 
-__global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(const GateArgs a) {
+template <int NT>
+__global__ void __launch_bounds__(NT, NT == 64 ? 8 : 2) errorgate_waterfill_kernel(const GateArgs a) {
+  constexpr int kW = NT / 32;  // warps
   extern __shared__ __align__(16) unsigned char eg_smem[];
   const int r = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int kv = r / kG;
   const int C = a.C, NS = a.NS;
-  __shared__ float s_red[kEgW];
-  __shared__ int s_redi[kEgW];
+  __shared__ float s_red[kW];
+  __shared__ int s_redi[kW];
   EgShared S;
   {
     unsigned char* p = eg_smem;
@@ -126,7 +127,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
   auto fetch = [&](int b, float (&x)[kEgB][4], float (&x2)[kEgB][4]) {
 #pragma unroll
     for (int k = 0; k < kEgB; ++k) {
-      const int c = warp + kEgW * (b * kEgB + k);
+      const int c = warp + kW * (b * kEgB + k);
       const int64_t base = (rC + min(c, C - 1)) * kD;
       const float4 u = c < C ? __ldg(reinterpret_cast<const float4*>(a.Sk + base) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
       const float4 u2 = c < C ? __ldg(reinterpret_cast<const float4*>(a.Sk2 + base) + lane) : make_float4(0.f, 0.f, 0.f, 0.f);
@@ -134,11 +135,11 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
       x2[k][0] = u2.x; x2[k][1] = u2.y; x2[k][2] = u2.z; x2[k][3] = u2.w;
     }
   };
-  const int nbatch = (C + kEgW * kEgB - 1) / (kEgW * kEgB);
+  const int nbatch = (C + kW * kEgB - 1) / (kW * kEgB);
   fetch(0, ck, ck2);
   if (nbatch > 1) fetch(1, nk, nk2);
   // ---- selected tokens: their clusters and their K rows are fetched side by side
-  for (int j = tid; j < NS; j += kEgThreads) {
+  for (int j = tid; j < NS; j += NT) {
     const int t = a.sel[(int64_t)r * NS + j];
     const bool v = t >= 0 && t < a.Lmax;
     S.selt[j] = v ? t : -1;
@@ -147,23 +148,23 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
   {  // K rows of the selected tokens: a thread's indices first, then all its row loads, then the stores
     constexpr int kSU = 4;
     const int ne = min(NS, kEgSelCache) * 16;
-    for (int e0 = tid; e0 < ne; e0 += kEgThreads * kSU) {
+    for (int e0 = tid; e0 < ne; e0 += NT * kSU) {
       int t[kSU];
 #pragma unroll
       for (int u = 0; u < kSU; ++u) {
-        const int e = e0 + kEgThreads * u;
+        const int e = e0 + NT * u;
         t[u] = e < ne ? a.sel[(int64_t)r * NS + (e >> 4)] : -1;
       }
       uint4 x[kSU];
 #pragma unroll
       for (int u = 0; u < kSU; ++u) {
-        const int e = e0 + kEgThreads * u;
+        const int e = e0 + NT * u;
         x[u] = (t[u] >= 0 && t[u] < a.Lmax) ? __ldg(reinterpret_cast<const uint4*>(Kr + (int64_t)t[u] * kD + (e & 15) * 8))
                                             : make_uint4(0u, 0u, 0u, 0u);
       }
 #pragma unroll
       for (int u = 0; u < kSU; ++u) {
-        const int e = e0 + kEgThreads * u;
+        const int e = e0 + NT * u;
         if (t[u] >= 0 && t[u] < a.Lmax) *reinterpret_cast<uint4*>(S.selk + (e >> 4) * kD + (e & 15) * 8) = x[u];
       }
     }
@@ -176,7 +177,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
     q2[i] = __fmul_rn(qv[i], qv[i]);
   }
   // tail counts and ln n_t, one thread per cluster, while the rows are in flight
-  for (int c = tid; c < C; c += kEgThreads) {
+  for (int c = tid; c < C; c += NT) {
     float ntc = a.nb[rC + c];
     int ns_c = 0;
     for (int j = 0; j < NS; ++j)
@@ -203,14 +204,14 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
         ck2[k][i] = nk2[k][i];
       }
     if (b + 2 < nbatch) fetch(b + 2, nk, nk2);
-    const int cb = warp + kEgW * b * kEgB;  // clusters cb + kEgW * k
+    const int cb = warp + kW * b * kEgB;  // clusters cb + kW * k
     int any = 0;
 #pragma unroll
-    for (int k = 0; k < kEgB; ++k) any |= (cb + kEgW * k < C) ? S.nsel[cb + kEgW * k] : 0;
+    for (int k = 0; k < kEgB; ++k) any |= (cb + kW * k < C) ? S.nsel[cb + kW * k] : 0;
     for (int j = 0; any && j < NS; ++j) {  // selected tokens leave their clusters, in list order
       const int cj = S.selc[j];
       const int d = cj - cb;
-      if (cj < 0 || d < 0 || d >= kEgW * kEgB || d % kEgW != 0) continue;  // warp-uniform
+      if (cj < 0 || d < 0 || d >= kW * kEgB || d % kW != 0) continue;  // warp-uniform
       float kf[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i)
@@ -218,7 +219,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
                                                  : Kr[(int64_t)S.selt[j] * kD + 4 * lane + i]);
 #pragma unroll
       for (int k = 0; k < kEgB; ++k) {
-        if (d == kEgW * k) {
+        if (d == kW * k) {
 #pragma unroll
           for (int i = 0; i < 4; ++i) {
             sk[k][i] = __fsub_rn(sk[k][i], kf[i]);
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
     float zd[kEgB], sd[kEgB];
 #pragma unroll
     for (int k = 0; k < kEgB; ++k) {
-      const int c = cb + kEgW * k;
+      const int c = cb + kW * k;
       const float inv = c < C ? S.inv[c] : 1.f;
       float kb[4], var[4];
 #pragma unroll
@@ -246,7 +247,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
     if (lane == 0) {
 #pragma unroll
       for (int k = 0; k < kEgB; ++k) {
-        const int c = cb + kEgW * k;
+        const int c = cb + kW * k;
         if (c < C) {
           S.zd[c] = zd[k];
           S.sd[c] = sd[k];
@@ -256,7 +257,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
   }
   __syncthreads();
   float smax = -INFINITY;
-  for (int c = tid; c < C; c += kEgThreads) {
+  for (int c = tid; c < C; c += NT) {
     const float zbar = __fmul_rn(0.08838834764831845f, S.zd[c]);
     const float s2 = __fmul_rn(0.0078125f, S.sd[c]);
     const float er = erf_f(__fmul_rn(__fsqrt_rn(s2), 0.70710677f));
@@ -274,9 +275,9 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
   __syncthreads();
   smax = s_red[0];
 #pragma unroll
-  for (int v = 1; v < kEgW; ++v) smax = fmaxf(smax, s_red[v]);
+  for (int v = 1; v < kW; ++v) smax = fmaxf(smax, s_red[v]);
   float tot_part = 0.f;
-  for (int c = tid; c < C; c += kEgThreads) {
+  for (int c = tid; c < C; c += NT) {
     const bool live = S.nt[c] > 1.f;
     const float w = live ? exp_f(__fsub_rn(S.score[c], smax)) : 0.f;
     const float cap = live ? S.nt[c] : 0.f;
@@ -294,11 +295,11 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
     __syncthreads();
     float t = 0.f;
 #pragma unroll
-    for (int w = 0; w < kEgW; ++w) t = __fadd_rn(t, s_red[w]);
+    for (int w = 0; w < kW; ++w) t = __fadd_rn(t, s_red[w]);
     return t;
   };
   const float tot = block_sum(tot_part);  // its barriers also publish w, cap, ratio, score
-  for (int c = tid; c < C; c += kEgThreads) {  // ranks by (ratio asc, cluster asc), (score desc, cluster asc)
+  for (int c = tid; c < C; c += NT) {  // ranks by (ratio asc, cluster asc), (score desc, cluster asc)
     const float ratio = S.ratio[c];
     const float sm = S.nt[c] > 1.f ? S.score[c] : -INFINITY;
     int r1 = 0, r2 = 0;
@@ -312,7 +313,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
     S.rank2[c] = r2;
   }
   __syncthreads();
-  for (int j = tid; j < C; j += kEgThreads) {  // caps, weights and ratios in ratio order
+  for (int j = tid; j < C; j += NT) {  // caps, weights and ratios in ratio order
     const int o = S.ord[j];
     S.capo[j] = S.cap[o];
     S.wo[j] = S.w[o];
@@ -335,7 +336,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
       S.cex[j] = ex;
       ex = __fadd_rn(ex, S.capo[j]);
     }
-  } else if (lane == 0) {  // suffix sums of the weights in ratio order, accumulated in double from the end
+  } else if (warp == 1 && lane == 0) {  // suffix sums of the weights in ratio order, accumulated in double from the end
     double acc = 0.0;
     for (int j = C - 1; j >= 0; --j) {
       acc = __dadd_rn(acc, (double)S.wo[j]);
@@ -344,7 +345,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
   }
   __syncthreads();
   int jj = 0x7fffffff;
-  for (int j = tid; j < C; j += kEgThreads) {
+  for (int j = tid; j < C; j += NT) {
     const float ws = S.wsuf[j];
     const float f = ws > 0.f ? __fadd_rn(S.cex[j], __fmul_rn(S.rato[j], ws)) : INFINITY;
     if (f >= a.E) jj = min(jj, j);
@@ -355,11 +356,11 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
   __syncthreads();
   jj = s_redi[0];
 #pragma unroll
-  for (int v = 1; v < kEgW; ++v) jj = min(jj, s_redi[v]);
+  for (int v = 1; v < kW; ++v) jj = min(jj, s_redi[v]);
   if (jj == 0x7fffffff) jj = 0;
   const float lam = __fdiv_rn(__fsub_rn(a.E, S.cex[jj]), fmaxf(S.wsuf[jj], 1e-30f));
   float q_part = 0.f;
-  for (int c = tid; c < C; c += kEgThreads) {
+  for (int c = tid; c < C; c += NT) {
     float qb = fminf(S.cap[c], floorf(__fmul_rn(lam, S.w[c])));
     if (tot <= a.E) qb = S.cap[c];
     S.qb[c] = qb;
@@ -367,7 +368,7 @@ __global__ void __launch_bounds__(kEgThreads, 8) errorgate_waterfill_kernel(cons
   }
   const float sumq = block_sum(q_part);
   const float rem = fmaxf(__fsub_rn(fminf(tot, a.E), sumq), 0.f);
-  for (int c = tid; c < C; c += kEgThreads) {  // leftovers: one each to the best-scoring clusters with room
+  for (int c = tid; c < C; c += NT) {  // leftovers: one each to the best-scoring clusters with room
     const int my = S.rank2[c];
     int before = 0;
     for (int j = 0; j < C; ++j) before += (S.qb[j] < S.cap[j] && S.rank2[j] < my) ? 1 : 0;
@@ -1910,8 +1911,19 @@ extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const voi
   GateArgs a{static_cast<const __nv_bfloat16*>(q), q_stride, static_cast<const __nv_bfloat16*>(K), (int)Lmax, (int)C,
              (int)n_sel, asg, sel, Sk, Sk2, nb, E, score, nt, quota, zdot, status};
   const size_t smem = eg_smem_bytes((int)C, (int)n_sel);
-  if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(errorgate_waterfill_kernel), smem, fn)) return rc;
-  errorgate_waterfill_kernel<<<(unsigned)(B * kHQ), kEgThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  // few rows (small batches): 8 warps per row shorten each row's chain; a full batch keeps 2 warps per
+  // row so that every row is resident at once.  Results do not depend on the choice.
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (B * kHQ <= 2 * sms) {
+    if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(errorgate_waterfill_kernel<256>), smem, fn)) return rc;
+    errorgate_waterfill_kernel<256><<<(unsigned)(B * kHQ), 256, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  } else {
+    if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(errorgate_waterfill_kernel<kEgThreads>), smem, fn))
+      return rc;
+    errorgate_waterfill_kernel<kEgThreads><<<(unsigned)(B * kHQ), kEgThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  }
   return oa_check_launch(fn);
 }
 
