@@ -92,16 +92,24 @@ def test_build_matches_reference(golden_dir, name):
     z = _load(golden_dir, name)
     st, K, V = _state_from_fixture(x, z)
     n0 = x["n0"]
-    assert np.array_equal(st["Sk"].astype(np.float64).sum(-1), z["Sk_sum"])
-    assert np.array_equal(st["Sk2"].astype(np.float64).sum(-1), z["Sk2_sum"])
-    assert np.array_equal(st["Sv"].astype(np.float64).sum(-1), z["Sv_sum"])
-    assert np.array_equal(st["Sk"][:, ::16, ::4], z["Sk_rows"])
+
+    def same(name, got, want):
+        got, want = np.asarray(got), np.asarray(want)
+        if not np.array_equal(got, want):
+            bad = np.argwhere(got != want)
+            d = np.abs(got.astype(np.float64) - want.astype(np.float64))
+            raise AssertionError(f"{name}: {len(bad)} of {got.size} differ, first at {bad[0].tolist()}, "
+                                 f"max |diff| {d.max():.3e}")
+    same("Sk_sum", st["Sk"].astype(np.float64).sum(-1), z["Sk_sum"])
+    same("Sk2_sum", st["Sk2"].astype(np.float64).sum(-1), z["Sk2_sum"])
+    same("Sv_sum", st["Sv"].astype(np.float64).sum(-1), z["Sv_sum"])
+    same("Sk_rows", st["Sk"][:, ::16, ::4], z["Sk_rows"])
     for b in range(x["B"]):
         scale, codes = O.build_codes(K[b], z["U"][b], n0)
-        assert np.array_equal(scale, z["scale"][b].reshape(HKV, 32))
-        assert np.array_equal(codes[:, :n0], z["codes"][b][:, :n0])
-        assert np.array_equal(st["nb"][b], np.stack([np.bincount(st["asg"][b, h, :n0], minlength=int(z["C"]))
-                                                     for h in range(HQ)]).astype(np.float32))
+        same(f"scale[{b}]", scale, z["scale"][b].reshape(HKV, 32))
+        same(f"codes[{b}]", codes[:, :n0], z["codes"][b][:, :n0])
+        same(f"nb[{b}]", st["nb"][b], np.stack([np.bincount(st["asg"][b, h, :n0], minlength=int(z["C"]))
+                                                for h in range(HQ)]).astype(np.float32))
 
 
 @pytest.mark.parametrize("name", list(cases.DECODE_CASES))
