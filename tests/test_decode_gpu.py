@@ -333,11 +333,13 @@ def test_decode_32k_steps_bit_exact(rho):
     assert int(m.status.item()) == 0
 
 
-@pytest.mark.parametrize("B,n0,rho", [(1, 131072, 0.05), (2, 65536, 0.01), (4, 8192, 0.05)])
+@pytest.mark.parametrize("B,n0,rho", [(1, 131072, 0.05), (2, 65536, 0.01), (4, 8192, 0.05), (16, 4096, 0.01)])
 def test_decode_sweep_shapes_bit_exact(B, n0, rho):
     """Extreme points of the latency sweep (contexts 8K..128K, 1% and 5% read): a GPU-built state,
     then decode steps checked against the oracle.  At 128K the score row no longer fits shared memory
-    (top-q reads its keys from global memory); at 5% the read lists are long (E = 1335, C = 192)."""
+    (top-q keys go through its workspace); at 5% the read lists are long (E = 1335, C = 192).  B = 16
+    (512 rows) takes the launch shapes of full batches: ErrorGate with two warps per row, top-q with
+    one CTA per row at a time (smaller batches: eight warps per row, a row's clusters split over CTAs)."""
     from openattention_b200 import synth
     dev = torch.device("cuda")
     steps = 3
