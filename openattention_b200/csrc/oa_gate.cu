@@ -1038,7 +1038,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
 // For rows whose score row does not fit shared memory (beyond about 49K positions) top-q runs in two
 // kernels over a caller workspace of R x ckw 16-bit keys:
 //   topq_permute_kernel: one CTA per row stages the score row in chunks of kPmChunk positions (bulk
-//     copies); for each chunk, warps take clusters and key the run of the cluster's members whose
+//     copies; 64 KB chunks let two CTAs share an SM, one staging while the other walks); for each chunk, warps take clusters and key the run of the cluster's members whose
 //     positions fall in the chunk (member lists are ascending within a cluster, so each run starts
 //     where the previous chunk's ended), writing the keys into the workspace in CSR order; the
 //     member list is read once;
@@ -1046,7 +1046,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
 //     cluster's contiguous keys in the workspace (register path as topq_stream_kernel, radix path
 //     for larger clusters), with generated tokens keyed from the score row.
 constexpr int kPmThreads = 1024;
-constexpr int kPmChunk = 65536;  // positions staged per pass
+constexpr int kPmChunk = 32768;  // positions staged per pass (64 KB: two CTAs per SM)
 constexpr int kPmU = 8;            // 32-member groups a warp loads at once
 constexpr int kCkThreads = 256;
 constexpr int kCkWarps = kCkThreads / 32;
