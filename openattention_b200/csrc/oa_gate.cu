@@ -1746,18 +1746,21 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
   __syncthreads();
   const __nv_bfloat16* Kr = a.K + (int64_t)kv * a.Lmax * kD + hl * 8;
   const __nv_bfloat16* Vr = a.V + (int64_t)kv * a.Lmax * kD + hl * 8;
-  // ---- pass A: token dots (K rows) and q.Sk for live clusters
-  for (int j0 = hw; j0 < NT; j0 += kPFHalf * kPFU) {
+  // ---- pass A: token dots (K rows) and q.Sk for live clusters.  The loops that reduce over a
+  //      half-warp with full-mask shuffles run a CTA-uniform trip count: with the half-warp index in
+  //      the loop bound, the two halves of a warp would differ by one trip whenever NT = 2w + 1 (mod
+  //      64), and one half would shuffle with lanes that have left the loop.
+  for (int jb = 0; jb < NT; jb += kPFHalf * kPFU) {
     uint4 kw[kPFU];
 #pragma unroll
     for (int u = 0; u < kPFU; ++u) {
-      const int j = j0 + u * kPFHalf;
+      const int j = jb + hw + u * kPFHalf;
       const int t = j < NT ? S.tok[j] : -1;
       kw[u] = t >= 0 ? ldg_stream(reinterpret_cast<const uint4*>(Kr + (int64_t)t * kD)) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kPFU; ++u) {
-      const int j = j0 + u * kPFHalf;
+      const int j = jb + hw + u * kPFHalf;
       const float d = hw_sum(dot8(qv, kw[u]));
       if (hl == 0 && j < NT) S.z[j] = d;
     }
@@ -1768,18 +1771,18 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
     for (int c = tid; c < C; c += kPF)
       if (S.inv[c] > 0.f) S.qsk[c] = __fmul_rn(a.zdot[rowC + c], a.nt[rowC + c]);
   }
-  for (int c0 = hw; a.zdot == nullptr && c0 < C; c0 += kPFHalf * 4) {
+  for (int cb = 0; a.zdot == nullptr && cb < C; cb += kPFHalf * 4) {
     float4 x[4], y[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int c = c0 + u * kPFHalf;
+      const int c = cb + hw + u * kPFHalf;
       const bool live = c < C && S.inv[c] > 0.f;
       x[u] = live ? __ldg(reinterpret_cast<const float4*>(Skr + (int64_t)c * kD)) : make_float4(0.f, 0.f, 0.f, 0.f);
       y[u] = live ? __ldg(reinterpret_cast<const float4*>(Skr + (int64_t)c * kD + 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
-      const int c = c0 + u * kPFHalf;
+      const int c = cb + hw + u * kPFHalf;
       const float d = hw_sum(dot8f(qv, x[u], y[u]));
       if (hl == 0 && c < C) S.qsk[c] = d;
     }

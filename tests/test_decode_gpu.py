@@ -376,3 +376,74 @@ def test_decode_sweep_shapes_bit_exact(B, n0, rho):
         assert np.abs(got - o["out"]).max() <= 2e-3
         assert np.linalg.norm(got - o["out"]) <= 1e-3 * np.linalg.norm(o["out"])
     assert int(m.status.item()) == 0
+
+
+def _proxy_flash_inputs(C, NS, E, Lmax=4096, seed=0):
+    """A consistent read set for one request (32 rows) without the selection stages: random keys and
+    values, random assignments with their cluster sums, NS selected positions per row, quotas within the
+    tail counts (sum <= E) and their members as the quota segments of exp_idx, and ErrorGate's zdot
+    (the tail mean's q dot)."""
+    rng = np.random.default_rng(seed)
+    R, kv = HQ, np.arange(HQ) // (HQ // 8)
+    K = O.bits(torch.from_numpy(rng.standard_normal((1, 8, Lmax, D), dtype=np.float32)).to(torch.bfloat16))
+    V = O.bits(torch.from_numpy(rng.standard_normal((1, 8, Lmax, D), dtype=np.float32)).to(torch.bfloat16))
+    q = O.bits(torch.from_numpy(rng.standard_normal((R, D), dtype=np.float32)).to(torch.bfloat16))
+    Kf, Vf = O.bf16_to_f32(K[0]).astype(np.float64), O.bf16_to_f32(V[0]).astype(np.float64)
+    qf = O.bf16_to_f32(q).astype(np.float64)
+    asg = rng.integers(0, C, size=(R, Lmax)).astype(np.int32)
+    Sk, Sv = np.zeros((R, C, D)), np.zeros((R, C, D))
+    sel = np.zeros((R, NS), np.int32)
+    nt, quota = np.zeros((R, C), np.float32), np.zeros((R, C), np.float32)
+    exp_idx = np.full((R, E), -1, np.int32)
+    zdot = np.zeros((R, C), np.float32)
+    for r in range(R):
+        np.add.at(Sk[r], asg[r], Kf[kv[r]])
+        np.add.at(Sv[r], asg[r], Vf[kv[r]])
+        sel[r] = rng.choice(Lmax, NS, replace=False)
+        tail = np.ones(Lmax, bool)
+        tail[sel[r]] = False
+        ts = Sk[r].copy()
+        np.subtract.at(ts, asg[r, sel[r]], Kf[kv[r], sel[r]])
+        nt[r] = np.bincount(asg[r][tail], minlength=C)
+        cap = max(1, 2 * E // C)
+        quota[r] = np.minimum(nt[r], rng.integers(0, cap + 1, size=C))
+        while quota[r].sum() > E:
+            quota[r, int(np.argmax(quota[r]))] -= 1
+        zdot[r] = (ts @ qf[r]) / np.maximum(nt[r], 1.0)
+        j = 0
+        for c in range(C):
+            members = np.flatnonzero(tail & (asg[r] == c))[:int(quota[r, c])]
+            exp_idx[r, j:j + len(members)] = members
+            j += len(members)
+    return dict(K=K, V=V, q=q, asg=asg, Sk=Sk.astype(np.float32), Sv=Sv.astype(np.float32), sel=sel, nt=nt,
+                quota=quota, exp_idx=exp_idx, zdot=zdot, Lmax=Lmax, C=C)
+
+
+@pytest.mark.parametrize("C,NS,E,use_zdot", [
+    (64, 41, 216, True), (64, 43, 216, True), (64, 45, 216, True), (64, 47, 216, True), (192, 14, 1335, True),
+    (33, 41, 216, False), (35, 43, 216, False), (37, 45, 216, False), (39, 47, 216, False)])
+def test_proxy_flash_read_list_lengths(C, NS, E, use_zdot):
+    """The deployed proxy flash kernel at read-list lengths NS + E = 1, 3, 5, 7 (mod 64) and, on the path
+    that reads Sk, cluster counts C = 1, 3, 5, 7 (mod 32): the lengths at which the two half-warps of one
+    warp see a different number of 64-entry (32-cluster) trips.  (192, 14, 1335) is the step at 32K
+    positions and 5% read.  Output within 2e-3 max-abs and 1e-3 relative-L2 of the fp32 estimator."""
+    x = _proxy_flash_inputs(C, NS, E)
+    R, Lmax = HQ, x["Lmax"]
+    dev = torch.device("cuda")
+    Kg, Vg = O.from_bits(x["K"]).to(dev), O.from_bits(x["V"]).to(dev)
+    st = {"nb": torch.zeros(1, HQ, C, device=dev), "asg": torch.from_numpy(x["asg"]).view(1, HQ, Lmax).to(dev),
+          "Sk": torch.from_numpy(x["Sk"]).view(1, HQ, C, D).to(dev), "Sv": torch.from_numpy(x["Sv"]).view(1, HQ, C, D).to(dev)}
+    g = lambda a: torch.from_numpy(a).to(dev)  # noqa: E731
+    out = torch.empty(R, D, dtype=torch.float32, device=dev)
+    status = torch.zeros(1, dtype=torch.int32, device=dev)
+    S.residual_flash(O.from_bits(x["q"]).to(dev), Kg, Vg, st, g(x["sel"]), g(x["exp_idx"]), g(x["nt"]), g(x["quota"]),
+                     out, status=status, zdot=g(x["zdot"]) if use_zdot else None)
+    torch.cuda.synchronize()
+    Skr, Svr, nr = O.residual_sums(x["K"], x["V"], x["asg"], x["sel"], x["exp_idx"], x["Sk"], x["Sv"], x["nt"],
+                                   x["quota"])
+    est = O.estimator_fp32(x["q"], x["K"].reshape(8, Lmax, D), x["V"].reshape(8, Lmax, D), x["sel"], x["exp_idx"],
+                           Skr, Svr, nr)
+    got = out.cpu().double().numpy()
+    assert np.abs(got - est).max() <= 2e-3
+    assert np.linalg.norm(got - est) <= 1e-3 * np.linalg.norm(est)
+    assert int(status.item()) == 0
