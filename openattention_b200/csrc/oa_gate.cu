@@ -23,6 +23,11 @@ namespace {
 constexpr int kMaxC = 256;
 constexpr int kGateThreads = 256;
 
+// A quota as the whole number of tokens it allots, clamped to [0, E].  The water-filling's quotas are
+// whole numbers in that range already; a value a caller passes outside it (negative, NaN, above E)
+// then cannot carry a prefix of quotas outside the expanded list.
+__device__ __forceinline__ int quota_int(float x, int E) { return x > 0.f ? (int)fminf(x, (float)E) : 0; }
+
 __device__ __forceinline__ float warp_tree_dot(const float (&a)[4], const float (&b)[4]) {
   float v = __fmul_rn(a[0], b[0]);
   v = __fmaf_rn(a[1], b[1], v);
@@ -507,7 +512,7 @@ __global__ void __launch_bounds__(kTqThreads, 3) topq_kernel(const TopqArgs a) {
     if (a.smem_keys && nbytes > 0) bulk_load(s_spill, sr, (uint32_t)nbytes, bar);
     s_next = 0;
   }
-  for (int c = tid; c < C; c += kTqThreads) s_q[c] = (int)a.quota[(int64_t)r * C + c];
+  for (int c = tid; c < C; c += kTqThreads) s_q[c] = quota_int(a.quota[(int64_t)r * C + c], a.E);
   __syncthreads();
   if (tid == 0) {
     int run = 0;
@@ -777,7 +782,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
   auto load_meta = [&](int row, int set) {
     const int64_t rc0 = (int64_t)row * C;
     for (int c = tid; c < C; c += kTsThreads) {
-      s_q_[set][c] = (int)a.quota[rc0 + c];
+      s_q_[set][c] = quota_int(a.quota[rc0 + c], a.E);
       s_cs_[set][c] = a.cstart[rc0 + c];
       s_cl_[set][c] = a.clen[rc0 + c];
       s_rcnt_[set][c] = a.reclist ? a.reccnt[rc0 + c] : 0x7fffffff;
@@ -1140,7 +1145,7 @@ __global__ void __launch_bounds__(kCkThreads) topq_ck_kernel(const TopqArgs a, c
   const int32_t* mrow = a.mem + (int64_t)r * a.Lmax;
   const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
   int32_t* out = a.exp + (int64_t)r * a.E;
-  for (int c = tid; c < C; c += kCkThreads) s_q[c] = (int)a.quota[rC + c];
+  for (int c = tid; c < C; c += kCkThreads) s_q[c] = quota_int(a.quota[rC + c], a.E);
   if (tid == 0) s_next = 0;
   __syncthreads();
   if (tid == 0) {
@@ -1425,7 +1430,7 @@ __global__ void __launch_bounds__(kRW * 32, 2) residual_kernel(const ResidArgs a
   __shared__ int s_base[kMaxC + 1];
   __shared__ int s_q[kMaxC];
   __shared__ float s_m[kRW], s_l[kRW];
-  for (int c = tid; c < C; c += blockDim.x) s_q[c] = (int)a.quota[(int64_t)r * C + c];
+  for (int c = tid; c < C; c += blockDim.x) s_q[c] = quota_int(a.quota[(int64_t)r * C + c], a.E);
   const int NT = a.NS + a.E;
   for (int j = tid; j < NT; j += blockDim.x) {
     const int t = j < a.NS ? a.sel[(int64_t)r * a.NS + j] : a.exp[(int64_t)r * a.E + (j - a.NS)];
@@ -1696,7 +1701,10 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
     const int t = j < NS ? a.sel[(int64_t)r * NS + j] : a.exp[(int64_t)r * a.E + (j - NS)];
     const bool v = t >= 0 && t < a.Lmax;
     S.tok[j] = v ? t : -1;
-    if (j < NS) S.cl[j] = v ? (int16_t)a.asg[(int64_t)r * a.Lmax + t] : (int16_t)-1;
+    if (j < NS) {  // an assignment outside [0, C) counts as none
+      const int ca = v ? a.asg[(int64_t)r * a.Lmax + t] : -1;
+      S.cl[j] = (int16_t)(ca >= 0 && ca < C ? ca : -1);
+    }
   }
   float qv[8];
   {
@@ -1709,7 +1717,7 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
     const int per = (C + 31) / 32;
     const int c0 = lane * per, c1 = min(C, c0 + per);
     int run = 0;
-    for (int c = c0; c < c1; ++c) run += (int)S.w[c];
+    for (int c = c0; c < c1; ++c) run += quota_int(S.w[c], a.E);
     int incl = run;
 #pragma unroll
     for (int off = 1; off < 32; off <<= 1) {
@@ -1719,7 +1727,7 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
     int ex = incl - run;
     for (int c = c0; c < c1; ++c) {
       S.base[c] = ex;
-      ex += (int)S.w[c];
+      ex += quota_int(S.w[c], a.E);
     }
     if (lane == 31) S.base[C] = incl;
   }
@@ -1953,7 +1961,8 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
                        const int32_t* n_dev, const int32_t* n0_dev, int32_t* exp_idx, int32_t* status,
                        void* workspace, size_t workspace_bytes, void* stream) {
   const char* fn = "oa_topq";
-  OA_REQUIRE(R > 0 && Lmax > 0 && Lmax < (1 << 30) && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
+  OA_REQUIRE(R > 0 && Lmax > 0 && Lmax < (1 << 30) && C > 0 && C <= kMaxC && E > 0 && E < (1 << 23),
+             "%s: bad sizes", fn);
   OA_REQUIRE(score_stride >= ((Lmax + 7) & ~7ll) && score_stride % 8 == 0 && oa_aligned16(scores),
              "%s: score rows must be 16-byte aligned and hold Lmax rounded up to 8", fn);
   OA_REQUIRE(scores && mem && cstart && clen && asg && quota && n_dev && n0_dev && exp_idx, "%s: null pointer", fn);
