@@ -180,7 +180,8 @@ int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64
  * cluster's offset sum_{c'<c} q_c' in ascending position; -1 pads.  Candidates are the cluster's CSR
  * members (positions < n0) and its generated tokens: reclist (may be NULL) while it holds them all
  * (reccnt <= rmax), else positions in [n0, n) with asg == c.  C <= 256.  status (may be NULL): set to
- * 4 if a bulk copy of the score row did not complete in the bounded wait.
+ * 4 if a bulk copy of the score row did not complete in the bounded wait.  Quotas are whole numbers
+ * (as oa_errorgate_waterfill writes them); a value outside [0, E] is clamped to it.  E < 2^23.
  * workspace (may be NULL): oa_topq_workspace_bytes(R, Lmax, E) bytes, 16-byte aligned, used for rows
  * too long for the shared-memory kernel (their member keys are permuted into it); without it such
  * rows read their keys from global memory, which is much slower.
@@ -197,8 +198,8 @@ size_t oa_topq_workspace_bytes(int64_t R, int64_t Lmax, int64_t E);
 /* Residual proxies: per (row, cluster) the pooled sums minus every token read (sel in order, then
  * the cluster's exp segment), n' = nt - quota, kbar' / vbar' = bf16(sums / max(n', 1)) (R, C, 128),
  * log_n = ln max(n', 1) if n' > 0.5 else -inf (R, C) fp32.  Replaces _k_resid_scatter +
- * _k_resid_norm (inference/ours_fused.py:367-407), without atomics.  status: as oa_errorgate_waterfill
- * (value 3). */
+ * _k_resid_norm (inference/ours_fused.py:367-407), without atomics.  Quotas outside [0, E] are clamped
+ * to it when the segments are placed.  status: as oa_errorgate_waterfill (value 3). */
 int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, const int32_t* asg,
                 const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E, const float* Sk,
                 const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar, float* log_n,
@@ -214,6 +215,8 @@ int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C
  *    oa_errorgate_waterfill's zdot for this step; then q . Sk_b is taken from it and Sk is not read.
  *  - kbar / vbar (and optionally log_n) given: the bf16 proxies are formed exactly as oa_residual
  *    forms them (bit-identical), written, and attended; zdot is ignored.
+ * Quotas outside [0, E] are clamped to it when the segments are placed; a selected token whose
+ * assignment is outside [0, C) counts as in no cluster.
  * status (may be NULL): device int32, unused by this entry. */
 int oa_residual_flash(const void* q, int64_t q_stride, const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C,
                       const int32_t* asg, const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E,
