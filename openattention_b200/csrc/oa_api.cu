@@ -30,6 +30,7 @@ struct SmemOptIn {
   int device;
   size_t static_bytes;  // the kernel's static shared memory
   size_t dyn_set;       // the dynamic limit set so far (0: the 48 KB default)
+  bool carveout_set;    // the largest shared-memory carveout was requested
 };
 std::mutex g_smem_mu;
 std::vector<SmemOptIn> g_smem;
@@ -38,7 +39,7 @@ std::vector<SmemOptIn> g_smem;
 // The kernel's static size is queried once per device and the limit is raised only when a launch
 // needs more than was set before: both are host calls that are not free, and launches in a decode
 // loop repeat the same sizes.
-int oa_smem_opt_in(const void* kernel, size_t dyn, const char* what) {
+int oa_smem_opt_in(const void* kernel, size_t dyn, const char* what, bool max_carveout) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
@@ -50,13 +51,18 @@ int oa_smem_opt_in(const void* kernel, size_t dyn, const char* what) {
     cudaFuncAttributes fa;
     e = cudaFuncGetAttributes(&fa, kernel);
     if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
-    g_smem.push_back(SmemOptIn{kernel, dev, fa.sharedSizeBytes, 0});
+    g_smem.push_back(SmemOptIn{kernel, dev, fa.sharedSizeBytes, 0, false});
     ent = &g_smem.back();
   }
   if (dyn + ent->static_bytes > 48 * 1024 && dyn > ent->dyn_set) {
     e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn);
     if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
     ent->dyn_set = dyn;
+  }
+  if (max_carveout && !ent->carveout_set) {
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+    ent->carveout_set = true;
   }
   return OA_OK;
 }

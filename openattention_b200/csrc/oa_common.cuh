@@ -48,6 +48,16 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
 
+// ---- 16-byte asynchronous copies global -> shared (both addresses 16-byte aligned; through L2 only).
+// The data never passes through registers; cp_async_wait_all returns once this thread's copies have
+// landed (a hardware wait on the thread's own copies, no polling), and a barrier then publishes them.
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n\tcp.async.wait_group 0;" ::: "memory");
+}
+
 // ---- TMA bulk copies (cp.async.bulk, no multicast) completing on an mbarrier, with bounded waits
 __device__ __forceinline__ void mbar_init(uint32_t bar) {
   asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(1) : "memory");
@@ -99,8 +109,10 @@ enum {
 int oa_fail(int code, const char* fmt, ...);
 int oa_check_launch(const char* what);
 // Raise a kernel's dynamic shared-memory limit when its static arrays plus `dyn` bytes pass the
-// 48 KB default (the opt-in counts the static part too).  Returns an OA status.
-int oa_smem_opt_in(const void* kernel, size_t dyn, const char* what);
+// 48 KB default (the opt-in counts the static part too).  With max_carveout, the kernel also asks
+// for the largest shared-memory share of the SM's L1 (for kernels whose occupancy is set by shared
+// memory and that do not rely on L1).  Returns an OA status.
+int oa_smem_opt_in(const void* kernel, size_t dyn, const char* what, bool max_carveout = false);
 
 #define OA_REQUIRE(cond, ...)                      \
   do {                                             \

@@ -53,7 +53,7 @@ struct IndexArgs {
 // updates the cluster's pooled sums.  Every dot keeps its sequential fma order over d (or c).
 constexpr int kIuCentCache = 256;  // clusters whose centroids are staged in shared memory
 
-__global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
+__global__ void __launch_bounds__(128, 8) index_update_kernel(const IndexArgs a) {
   extern __shared__ __align__(16) float iu_cent[];  // min(C, kIuCentCache) x 16
   const int r = blockIdx.x;
   const int kv = r / kG, g = r % kG;
@@ -69,22 +69,21 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
   const int cstage = min(C, kIuCentCache);
   const float* ce = a.cent + (int64_t)r * C * kRC;
   const float* Uk = a.U + (int64_t)kv * kD * kRQ;
-  // Every thread issues all of its loads (U, W, centroids, the new K / V element, q) before it stores
-  // any of them, so the staging costs one memory round trip.
+  // U, W and the centroids go to shared memory as 16-byte asynchronous copies, issued together with
+  // the loads of the new K / V element and q, so the staging costs one memory round trip and holds no
+  // registers (8 CTAs of 128 threads per SM: every row of a 32-request batch is resident at once).
   constexpr int kUV = kD * kRQ / 4 / 128;  // float4 of U per thread (8)
   constexpr int kWV = kD * kRC / 8 / 128;  // uint4 of W per thread (2)
-  constexpr int kCV = kIuCentCache * kRC / 4 / 128;  // float4 of centroids per thread, at most (8)
   const int ncv = cstage * kRC / 4;
-  float4 ub[kUV], cb[kCV];
-  uint4 wb[kWV];
 #pragma unroll
-  for (int u = 0; u < kUV; ++u) ub[u] = __ldg(reinterpret_cast<const float4*>(Uk) + tid + 128 * u);
+  for (int u = 0; u < kUV; ++u)
+    cp_async16(reinterpret_cast<float4*>(sU) + tid + 128 * u, reinterpret_cast<const float4*>(Uk) + tid + 128 * u);
 #pragma unroll
   for (int u = 0; u < kWV; ++u)
-    wb[u] = __ldg(reinterpret_cast<const uint4*>(a.W + (int64_t)r * kD * kRC) + tid + 128 * u);
-#pragma unroll
-  for (int u = 0; u < kCV; ++u)
-    cb[u] = tid + 128 * u < ncv ? __ldg(reinterpret_cast<const float4*>(ce) + tid + 128 * u) : make_float4(0.f, 0.f, 0.f, 0.f);
+    cp_async16(reinterpret_cast<uint4*>(sW) + tid + 128 * u,
+               reinterpret_cast<const uint4*>(a.W + (int64_t)r * kD * kRC) + tid + 128 * u);
+  for (int i = tid; i < ncv; i += 128)
+    cp_async16(reinterpret_cast<float4*>(iu_cent) + i, reinterpret_cast<const float4*>(ce) + i);
   __nv_bfloat16 kb = __float2bfloat16_rn(0.f), vb = kb, qb = kb;
   if (have_tok) {
     if (a.k_new != nullptr) {
@@ -100,13 +99,7 @@ __global__ void __launch_bounds__(128) index_update_kernel(const IndexArgs a) {
     }
   }
   if (a.q != nullptr) qb = a.q[(int64_t)r * a.q_stride + tid];
-#pragma unroll
-  for (int u = 0; u < kUV; ++u) reinterpret_cast<float4*>(sU)[tid + 128 * u] = ub[u];
-#pragma unroll
-  for (int u = 0; u < kWV; ++u) reinterpret_cast<uint4*>(sW)[tid + 128 * u] = wb[u];
-#pragma unroll
-  for (int u = 0; u < kCV; ++u)
-    if (tid + 128 * u < ncv) reinterpret_cast<float4*>(iu_cent)[tid + 128 * u] = cb[u];
+  cp_async_wait_all();
   kf[tid] = __bfloat162float(kb);
   vf[tid] = __bfloat162float(vb);
   qf[tid] = __bfloat162float(qb);
@@ -640,7 +633,7 @@ int index_update_entry(const char* fn, void* K, void* V, int64_t B, int64_t Lmax
               (int)Lmax, (int)C, static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new)};
   const size_t smem = (size_t)std::min<int64_t>(C, kIuCentCache) * kRC * sizeof(float);
   OA_REQUIRE(oa_aligned16(cent) && oa_aligned16(U) && oa_aligned16(W), "%s: U / W / cent must be 16-byte aligned", fn);
-  if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(index_update_kernel), smem, fn)) return rc;
+  if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(index_update_kernel), smem, fn, true)) return rc;
   index_update_kernel<<<(unsigned)(B * kHQ), 128, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }
