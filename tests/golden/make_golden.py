@@ -141,9 +141,12 @@ def golden_decode(bl, name, metric_path):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("OA_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("OA_REFERENCE"),
+                    help="checkout of the reference (or set OA_REFERENCE)")
     ap.add_argument("--only", default="")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("--reference (or OA_REFERENCE) is required")
     torch.set_num_threads(os.cpu_count() or 1)
     tmp = tempfile.mkdtemp()
     metric_path = os.path.join(tmp, "static_metric.pt")
