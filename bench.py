@@ -2,7 +2,7 @@
 """Decode-attention-stage benchmark of the OpenAttention deployed path on B200 (BASELINE config c2).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--batch B] [--ctx N]
-    python bench.py --sweep [--sweep-b 1,32] [--sweep-n 8192,131072]   (latency sweep, one line per point)
+    python bench.py --sweep [--sweep-b 1,32] [--sweep-n 8192,131072] [--sweep-rho 0.05]   (latency sweep)
 
 Workload per GPU: B=32 requests, 32K-token bf16 KV caches (seeded synthetic, see
 openattention_b200/synth.py), 1% read (C=64, E=216), ONE layer's decode step: index update + QGS
@@ -617,7 +617,8 @@ def run_sweep(a):
     torch.cuda.set_device(dev)
     Bs = [int(x) for x in a.sweep_b.split(",")] if a.sweep_b else SWEEP_B
     Ns = [int(x) for x in a.sweep_n.split(",")] if a.sweep_n else SWEEP_N
-    for rho in SWEEP_RHO:
+    rhos = [float(x) for x in a.sweep_rho.split(",")] if a.sweep_rho else SWEEP_RHO
+    for rho in rhos:
         for n0 in Ns:
             for B in Bs:
                 print(json.dumps(sweep_point(dev, B, n0, rho, a.steps, a.warmup)), flush=True)
@@ -747,6 +748,7 @@ def main():
                     help="latency sweep of the decode step over batch x context x read (one JSON line per point)")
     ap.add_argument("--sweep-b", default="", help="comma list of batches for --sweep")
     ap.add_argument("--sweep-n", default="", help="comma list of contexts for --sweep")
+    ap.add_argument("--sweep-rho", default="", help="comma list of read fractions for --sweep (0.01, 0.03, 0.05)")
     ap.add_argument("--ctx", type=int, default=N_CTX,
                     help="context length (default 32768, the benchmark config; others only for profiling)")
     ap.add_argument("--batch", type=int, default=None,
