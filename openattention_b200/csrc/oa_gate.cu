@@ -1126,7 +1126,9 @@ __global__ void __launch_bounds__(kPmThreads) topq_permute_kernel(const TopqArgs
   }
 }
 
-__global__ void __launch_bounds__(kCkThreads) topq_ck_kernel(const TopqArgs a, const uint16_t* ck, int64_t ckw) {
+// parts > 1 (fewer rows than SMs): CTA (row, p) takes the clusters [p C / parts, (p+1) C / parts) of its row.
+__global__ void __launch_bounds__(kCkThreads) topq_ck_kernel(const TopqArgs a, const uint16_t* ck, int64_t ckw,
+                                                             int parts) {
   __shared__ int s_base[kMaxC + 1];
   __shared__ int s_q[kMaxC];
   __shared__ int s_next;
@@ -1134,10 +1136,11 @@ __global__ void __launch_bounds__(kCkThreads) topq_ck_kernel(const TopqArgs a, c
   __shared__ int s_hist[kCkWarps][256];
   __shared__ uint64_t s_w64[kCkWarps][64];
   extern __shared__ __align__(16) uint16_t ck_win[];  // per warp kCkWinSlots keys
-  const int r = blockIdx.x;
+  const int r = blockIdx.x / parts, part = blockIdx.x - r * parts;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const unsigned lt = (1u << lane) - 1u;
   const int C = a.C;
+  const int c_lo = part * C / parts, c_hi = (part + 1) * C / parts;
   const int n = __ldg(a.n_dev), n0 = __ldg(a.n0_dev);
   const int nsp = min(n, a.Lmax);
   const int64_t rC = (int64_t)r * C;
@@ -1146,7 +1149,7 @@ __global__ void __launch_bounds__(kCkThreads) topq_ck_kernel(const TopqArgs a, c
   const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
   int32_t* out = a.exp + (int64_t)r * a.E;
   for (int c = tid; c < C; c += kCkThreads) s_q[c] = quota_int(a.quota[rC + c], a.E);
-  if (tid == 0) s_next = 0;
+  if (tid == 0) s_next = c_lo;
   __syncthreads();
   if (tid == 0) {
     int run = 0;
@@ -1157,7 +1160,8 @@ __global__ void __launch_bounds__(kCkThreads) topq_ck_kernel(const TopqArgs a, c
     s_base[C] = run;
   }
   __syncthreads();
-  for (int i = s_base[C] + tid; i < a.E; i += kCkThreads) out[i] = -1;
+  if (part == 0)
+    for (int i = s_base[C] + tid; i < a.E; i += kCkThreads) out[i] = -1;
   // member keys from the workspace (kb = 0); generated tokens keyed from the score row
   const TsRow w{ckr, nullptr, a.scores + (int64_t)r * a.sw, mrow, n0, nsp, 0, 0};
   int* hist = s_hist[warp];
@@ -1167,10 +1171,10 @@ __global__ void __launch_bounds__(kCkThreads) topq_ck_kernel(const TopqArgs a, c
     if (lane == 0) {
       do {
         c = atomicAdd(&s_next, 1);
-      } while (c < C && s_q[c] <= 0);
+      } while (c < c_hi && s_q[c] <= 0);
     }
     c = __shfl_sync(0xffffffffu, c, 0);
-    if (c >= C) break;
+    if (c >= c_hi) break;
     const int q = s_q[c], base = s_base[c];
     const int cs = a.cstart[rC + c], nmem = a.clen[rC + c];
     const int cnt = a.reclist ? a.reccnt[rC + c] : 0x7fffffff;
@@ -1998,7 +2002,12 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
     if (rc != OA_OK) return rc;
     const size_t smem_ck = (size_t)kCkWarps * kCkWinSlots * sizeof(uint16_t);
     if (int rc2 = oa_smem_opt_in(reinterpret_cast<const void*>(topq_ck_kernel), smem_ck, fn)) return rc2;
-    topq_ck_kernel<<<(unsigned)R, kCkThreads, smem_ck, st>>>(a, ck, ckw);
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // fewer rows than SMs: each row's clusters are split over up to 4 CTAs
+    const int parts = (int)std::max<int64_t>(1, std::min<int64_t>({4, sms / R, C}));
+    topq_ck_kernel<<<(unsigned)(R * parts), kCkThreads, smem_ck, st>>>(a, ck, ckw, parts);
     return oa_check_launch(fn);
   }
   const bool in_smem = spill_bytes <= 160 * 1024;  // larger rows read their keys from global memory
