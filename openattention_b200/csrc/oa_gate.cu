@@ -1047,7 +1047,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
 //     positions fall in the chunk (member lists are ascending within a cluster, so each run starts
 //     where the previous chunk's ended), writing the keys into the workspace in CSR order; the
 //     member list is read once;
-//   topq_ck_kernel: one CTA per row; warps take the clusters with q > 0 and select from the
+//   topq_ck_kernel: one CTA per row (both kernels split a row's clusters over up to four CTAs when
+//     there are fewer rows than SMs); warps take the clusters with q > 0 and select from the
 //     cluster's contiguous keys in the workspace (register path as topq_stream_kernel, radix path
 //     for larger clusters), with generated tokens keyed from the score row.
 constexpr int kPmThreads = 1024;
@@ -1058,13 +1059,16 @@ constexpr int kCkWarps = kCkThreads / 32;
 constexpr int kCkWin = 4096;  // member keys a warp stages in shared memory per window
 constexpr int kCkWinSlots = kCkWin + 16 + 64;  // + alignment slack of the 16-byte loads + 64 generated keys
 
-__global__ void __launch_bounds__(kPmThreads) topq_permute_kernel(const TopqArgs a, uint16_t* ck, int64_t ckw) {
+// parts > 1: CTA (row, p) stages every chunk of its row but keys only the clusters [p C / parts, (p+1) C / parts).
+__global__ void __launch_bounds__(kPmThreads) topq_permute_kernel(const TopqArgs a, uint16_t* ck, int64_t ckw,
+                                                                  int parts) {
   extern __shared__ __align__(128) uint16_t pm_spill[];  // kPmChunk positions
   __shared__ int s_lo[kMaxC];  // per cluster: its first member not keyed yet
   __shared__ int s_next;
   __shared__ __align__(8) uint64_t mbar;
-  const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31;
+  const int r = blockIdx.x / parts, part = blockIdx.x - r * parts, tid = threadIdx.x, lane = tid & 31;
   const int C = a.C;
+  const int c_lo = part * C / parts, c_hi = (part + 1) * C / parts;
   const int n = __ldg(a.n_dev), n0 = __ldg(a.n0_dev);
   const int npos = min(min(n, n0), a.Lmax);  // member lists hold positions < n0
   const int64_t rC = (int64_t)r * C;
@@ -1074,7 +1078,7 @@ __global__ void __launch_bounds__(kPmThreads) topq_permute_kernel(const TopqArgs
   const uint32_t bar = smem_u32(&mbar);
   for (int c = tid; c < C; c += kPmThreads) s_lo[c] = 0;
   if (tid == 0) {
-    s_next = 0;
+    s_next = c_lo;
     mbar_init(bar);
   }
   __syncthreads();
@@ -1098,7 +1102,7 @@ __global__ void __launch_bounds__(kPmThreads) topq_permute_kernel(const TopqArgs
       int c = 0;
       if (lane == 0) c = atomicAdd(&s_next, 1);
       c = __shfl_sync(0xffffffffu, c, 0);
-      if (c >= C) break;
+      if (c >= c_hi) break;
       const int cs = a.cstart[rC + c], nmem = a.clen[rC + c];
       int lo = s_lo[c];
       while (lo < nmem) {
@@ -1122,7 +1126,7 @@ __global__ void __launch_bounds__(kPmThreads) topq_permute_kernel(const TopqArgs
       if (lane == 0) s_lo[c] = lo;
     }
     __syncthreads();  // the staging buffer is refilled by the next pass
-    if (tid == 0) s_next = 0;
+    if (tid == 0) s_next = c_lo;
   }
 }
 
@@ -1996,17 +2000,17 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
     uint16_t* ck = static_cast<uint16_t*>(workspace);
     const int64_t ckw = ck_stride(Lmax);
     const size_t smem = (size_t)kPmChunk * 2;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    // fewer rows than SMs: each row's clusters are split over up to 4 CTAs in both kernels
+    const int parts = (int)std::max<int64_t>(1, std::min<int64_t>({4, sms / R, C}));
     if (int rc0 = oa_smem_opt_in(reinterpret_cast<const void*>(topq_permute_kernel), smem, fn)) return rc0;
-    topq_permute_kernel<<<(unsigned)R, kPmThreads, smem, st>>>(a, ck, ckw);
+    topq_permute_kernel<<<(unsigned)(R * parts), kPmThreads, smem, st>>>(a, ck, ckw, parts);
     int rc = oa_check_launch(fn);
     if (rc != OA_OK) return rc;
     const size_t smem_ck = (size_t)kCkWarps * kCkWinSlots * sizeof(uint16_t);
     if (int rc2 = oa_smem_opt_in(reinterpret_cast<const void*>(topq_ck_kernel), smem_ck, fn)) return rc2;
-    int dev = 0, sms = 148;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    // fewer rows than SMs: each row's clusters are split over up to 4 CTAs
-    const int parts = (int)std::max<int64_t>(1, std::min<int64_t>({4, sms / R, C}));
     topq_ck_kernel<<<(unsigned)(R * parts), kCkThreads, smem_ck, st>>>(a, ck, ckw, parts);
     return oa_check_launch(fn);
   }
