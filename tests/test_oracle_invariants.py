@@ -1,0 +1,83 @@
+"""The oracle's water-filling and within-cluster top-q against the properties the reference states
+for them, on seeded random rows (CPU only).
+
+Water-filling (inference/methods_eager.py:558-581, invariants checked by the reference's own self-test
+at :725-727): quotas are whole numbers, 0 <= quota <= cap with cap = n_t for live clusters (n_t > 1)
+and 0 otherwise, and sum(quota) = min(E, sum(cap)).
+
+Top-q (inference/ours_graph.py:93-166): each cluster's segment of exp_idx, at offset sum of the
+earlier quotas, holds the q best candidates of the cluster by score (ties -> lower position) in
+ascending position order, and -1 pads the rest.  Checked against a brute-force sort."""
+import numpy as np
+import pytest
+
+import oracle as O
+
+
+def _caps(nt):
+    return np.where(nt > 1.0, nt, 0.0)
+
+
+@pytest.mark.parametrize("C,E", [(64, 216), (192, 679), (192, 1335)])
+def test_waterfill_invariants(C, E):
+    rng = np.random.default_rng(C * 7 + E)
+    rows = []
+    for kind in range(6):
+        for _ in range(8):
+            score = rng.normal(0.0, 3.0, C).astype(np.float32)
+            nt = rng.integers(0, 600, C).astype(np.float32)
+            if kind == 1:    # total capacity below E: every live cluster gets its cap
+                nt = rng.integers(0, max(2, 2 * E // C), C).astype(np.float32)
+            elif kind == 2:  # no live cluster
+                nt = rng.integers(0, 2, C).astype(np.float32)
+            elif kind == 3:  # ties in the scores
+                score = np.round(score).astype(np.float32)
+            elif kind == 4:  # one cluster dominates the weights
+                score[rng.integers(C)] += 40.0
+            elif kind == 5:  # weights spanning many orders of magnitude
+                score = rng.normal(0.0, 30.0, C).astype(np.float32)
+            rows.append((score, nt))
+    score = np.stack([r[0] for r in rows])
+    nt = np.stack([r[1] for r in rows])
+    quota = O.waterfill(score, nt, E)
+    cap = _caps(nt)
+    assert np.all(quota == np.floor(quota)), "quotas are whole numbers"
+    assert np.all(quota >= 0) and np.all(quota <= cap)
+    np.testing.assert_array_equal(quota.sum(1), np.minimum(float(E), cap.sum(1)))
+
+
+def _bf16_bits(x):
+    return (np.asarray(x, np.float32).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def test_topq_is_the_exact_top_q():
+    rng = np.random.default_rng(11)
+    R, C, Lmax, n, E = 8, 16, 2048, 1900, 400
+    asg = rng.integers(0, C, (R, Lmax)).astype(np.int32)
+    # coarse scores: many exact ties between positions
+    s = _bf16_bits(np.round(rng.normal(0.0, 2.0, (R, Lmax)) * 4) / 4)
+    s[:, n:] = 0xFF80
+    sel = rng.choice(n, (R, 12), replace=True)
+    for r in range(R):
+        s[r, sel[r]] = 0xFF80  # selected tokens are out of the race
+    quota = np.zeros((R, C), np.float32)
+    for r in range(R):
+        live = s[r, :n] != 0xFF80
+        avail = np.bincount(asg[r, :n][live], minlength=C)
+        q = np.minimum(avail, rng.integers(0, 2 * E // C, C))
+        while q.sum() > E:
+            q[int(np.argmax(q))] -= 1
+        quota[r] = q
+    exp_idx = O.topq(s, asg, quota, n, E)
+    sf = O.bf16_to_f32(s)
+    for r in range(R):
+        base = 0
+        for c in range(C):
+            q = int(quota[r, c])
+            cand = np.flatnonzero(asg[r, :n] == c)
+            order = sorted(cand.tolist(), key=lambda t: (-sf[r, t], t))
+            want = sorted(order[:q])
+            got = exp_idx[r, base:base + q].tolist()
+            assert got == want, (r, c)
+            base += q
+        assert np.all(exp_idx[r, base:] == -1)
