@@ -81,3 +81,29 @@ def test_topq_is_the_exact_top_q():
             assert got == want, (r, c)
             base += q
         assert np.all(exp_idx[r, base:] == -1)
+
+
+def _round_bf16(x32):
+    """fp32 -> bf16 bits, round to nearest even (finite inputs)."""
+    u = np.asarray(x32, np.float32).view(np.uint32).astype(np.uint64)
+    return ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+
+
+def test_scan_is_bf16_of_the_once_rounded_exact_sum():
+    """QGS scores (graph_runner.py:100-120) are bf16(fp32(sum_j code_j zq_j)) with the sum taken
+    exactly and rounded once, so they do not depend on a summation order; sink, local and beyond-n
+    positions are -inf.  zq rows here span fewer than 2^21 in magnitude, where every product is
+    exact in the kernel's fixed-point limbs too."""
+    rng = np.random.default_rng(5)
+    B, Lmax, n, ns, nl = 1, 640, 600, 2, 3
+    codes = rng.integers(-127, 128, (B, 8, Lmax, 32)).astype(np.int8)
+    mag = 2.0 ** rng.uniform(-6, 2, (B * 32, 32))
+    zq = _bf16_bits(mag * rng.choice([-1.0, 1.0], (B * 32, 32)))
+    s = O.scan(codes, zq, n, ns, nl, sw=Lmax)
+    zf = O.bf16_to_f32(zq).astype(np.float64)
+    for r in range(B * 32):
+        exact = codes[r // 128, (r % 32) // 4].astype(np.float64) @ zf[r]  # (Lmax,), exact in float64
+        want = _round_bf16(exact.astype(np.float32))
+        want[:ns] = 0xFF80
+        want[n - nl:] = 0xFF80
+        np.testing.assert_array_equal(s[r], want)
