@@ -107,3 +107,48 @@ def test_scan_is_bf16_of_the_once_rounded_exact_sum():
         want[:ns] = 0xFF80
         want[n - nl:] = 0xFF80
         np.testing.assert_array_equal(s[r], want)
+
+
+def test_errorgate_matches_the_formula_in_float64():
+    """ErrorGate (ours_fused.py:122-154): per cluster b, the tail after removing the selected tokens
+    Sk_t = Sk - sum k, Sk2_t = Sk2 - sum k^2, n_t = n_b - #selected; kbar = Sk_t / max(n_t, 1),
+    var = max(Sk2_t / max(n_t, 1) - kbar^2, 0), zbar = s q.kbar, s2 = s^2 sum_d q_d^2 var_d and
+    score = zbar + ln max(n_t, 1) + s2 / 2 + ln max(erf(sqrt(s2 / 2)), 1e-30), s = 128^-1/2.
+    The oracle's fp32 evaluation is held to 2e-4 relative of the float64 formula; n_t exactly."""
+    rng = np.random.default_rng(3)
+    Lmax, C, NS, D = 256, 8, 6, 128
+    K = _bf16_bits(rng.normal(0.0, 1.0, (1, 8, Lmax, D)))
+    q = _bf16_bits(rng.normal(0.0, 1.0, (32, D)))
+    asg = rng.integers(0, C - 1, (32, Lmax)).astype(np.int32)
+    asg[:, :40] = 0  # one large cluster
+    asg[:, 40] = C - 1  # and one whose single member is selected below: an empty tail
+    Kf = O.bf16_to_f32(K[0]).astype(np.float64)
+    qf = O.bf16_to_f32(q).astype(np.float64)
+    Sk, Sk2 = np.zeros((32, C, D)), np.zeros((32, C, D))
+    sel = np.zeros((32, NS), np.int32)
+    for r in range(32):
+        np.add.at(Sk[r], asg[r], Kf[r // 4])
+        np.add.at(Sk2[r], asg[r], Kf[r // 4] ** 2)
+        sel[r] = rng.choice(Lmax, NS, replace=False)
+        sel[r, 0] = 40
+    nb = np.stack([np.bincount(asg[r], minlength=C) for r in range(32)]).astype(np.float32)
+    Sk32, Sk232 = Sk.astype(np.float32), Sk2.astype(np.float32)
+    score, nt = O.errorgate(q, K, asg, sel, Sk32, Sk232, nb)
+    from math import erf, log, sqrt
+    sc = 128 ** -0.5
+    for r in range(32):
+        skt, sk2t = Sk32[r].astype(np.float64), Sk232[r].astype(np.float64)
+        ntr = nb[r].astype(np.float64)
+        for t in sel[r]:
+            c = asg[r, t]
+            skt[c] -= Kf[r // 4, t]
+            sk2t[c] -= Kf[r // 4, t] ** 2
+            ntr[c] -= 1
+        np.testing.assert_array_equal(nt[r], ntr.astype(np.float32))
+        for c in range(C):
+            m = max(ntr[c], 1.0)
+            kb = skt[c] / m
+            var = np.maximum(sk2t[c] / m - kb * kb, 0.0)
+            s2 = sc * sc * float((qf[r] ** 2) @ var)
+            want = sc * float(qf[r] @ kb) + log(m) + s2 / 2 + log(max(erf(sqrt(s2 / 2)), 1e-30))
+            assert abs(float(score[r, c]) - want) <= 2e-4 * max(1.0, abs(want)), (r, c, float(score[r, c]), want)
