@@ -152,3 +152,52 @@ def test_errorgate_matches_the_formula_in_float64():
             s2 = sc * sc * float((qf[r] ** 2) @ var)
             want = sc * float(qf[r] @ kb) + log(m) + s2 / 2 + log(max(erf(sqrt(s2 / 2)), 1e-30))
             assert abs(float(score[r, c]) - want) <= 2e-4 * max(1.0, abs(want)), (r, c, float(score[r, c]), want)
+
+
+def test_residual_proxies_match_the_read_sets():
+    """Residual proxies (ours_fused.py:367-407): per cluster, the pooled sums minus every token read
+    (selected tokens by their assignment, expanded tokens by the quota segment their slot is in),
+    n' = n_t - q, kbar' = bf16(Sk' / max(n', 1)), vbar' likewise, log n' = ln max(n', 1) when n' > 0.5
+    else -inf.  Compared with the same sums in float64: log n' to 1e-6, the bf16 proxies to one bf16
+    rounding plus the fp32 cancellation error of the pooled sums."""
+    rng = np.random.default_rng(8)
+    Lmax, C, NS, E, D = 512, 12, 5, 96, 128
+    K = _bf16_bits(rng.normal(0.0, 1.0, (1, 8, Lmax, D)))
+    V = _bf16_bits(rng.normal(0.0, 1.0, (1, 8, Lmax, D)))
+    Kf, Vf = O.bf16_to_f32(K[0]).astype(np.float64), O.bf16_to_f32(V[0]).astype(np.float64)
+    asg = rng.integers(0, C, (32, Lmax)).astype(np.int32)
+    Sk, Sv = np.zeros((32, C, D)), np.zeros((32, C, D))
+    sel = np.zeros((32, NS), np.int32)
+    nt = np.zeros((32, C), np.float32)
+    quota = np.zeros((32, C), np.float32)
+    exp_idx = np.full((32, E), -1, np.int32)
+    for r in range(32):
+        kv = r // 4
+        np.add.at(Sk[r], asg[r], Kf[kv])
+        np.add.at(Sv[r], asg[r], Vf[kv])
+        sel[r] = rng.choice(Lmax, NS, replace=False)
+        tail = np.ones(Lmax, bool)
+        tail[sel[r]] = False
+        nt[r] = np.bincount(asg[r][tail], minlength=C)
+        quota[r] = np.minimum(nt[r], rng.integers(0, 2 * E // C, C))
+        quota[r, 0] = nt[r, 0]  # a cluster read completely: n' = 0, log n' = -inf
+        while quota[r].sum() > E:
+            quota[r, 1 + int(np.argmax(quota[r, 1:]))] -= 1
+        j = 0
+        for c in range(C):
+            m = np.flatnonzero(tail & (asg[r] == c))[:int(quota[r, c])]
+            exp_idx[r, j:j + len(m)] = m
+            j += len(m)
+    Sk32, Sv32 = Sk.astype(np.float32), Sv.astype(np.float32)
+    kbar, vbar, logn = O.residual(K, V, asg, sel, exp_idx, Sk32, Sv32, nt, quota)
+    Skr, Svr, nr = O.residual_sums(K, V, asg, sel, exp_idx, Sk32, Sv32, nt, quota)
+    live = nr > 0.5
+    want_ln = np.where(live, np.log(np.maximum(nr, 1.0)), -np.inf)
+    assert np.array_equal(np.isinf(logn), ~live)
+    np.testing.assert_allclose(logn[live], want_ln[live], rtol=0, atol=1e-6)
+    inv = 1.0 / np.maximum(nr, 1.0)[..., None]
+    for got, S, Sr in ((kbar, Sk, Skr), (vbar, Sv, Svr)):
+        g = O.bf16_to_f32(got).astype(np.float64)
+        want = Sr * inv
+        tol = 2.0 ** -8 * np.abs(want) + 1e-5 * np.abs(S).max(-1, keepdims=True) * inv
+        assert np.all(np.abs(g - want) <= tol)
