@@ -201,3 +201,25 @@ def test_residual_proxies_match_the_read_sets():
         want = Sr * inv
         tol = 2.0 ** -8 * np.abs(want) + 1e-5 * np.abs(S).max(-1, keepdims=True) * inv
         assert np.all(np.abs(g - want) <= tol)
+
+
+def test_select_is_the_exact_top_k():
+    """QGS select (graph_runner.py:123-159): sel = [0 .. ns-1, n-nl .. n-1, the k best scores ranked by
+    (score desc, position asc)] and the chosen scores become -inf.  The best-tiles-first search of the
+    reference is exact (every top-k score lies in one of the k best tiles by maximum), so the check
+    is a brute-force sort over all positions below n, with many tied scores."""
+    rng = np.random.default_rng(21)
+    R, n, ns, nl, k = 16, 3000, 2, 3, 9
+    s = _bf16_bits(np.round(rng.normal(0.0, 1.5, (R, n)) * 2) / 2)
+    s[:, :ns] = 0xFF80
+    s[:, n - nl:] = 0xFF80
+    s[3, ns:n - nl] = s[3, ns]  # one row where every candidate ties
+    s0 = s.copy()
+    sel = O.select(s, n, ns, nl, k)
+    sf = O.bf16_to_f32(s0)
+    for r in range(R):
+        order = sorted(range(n), key=lambda t: (-sf[r, t], t))[:k]
+        assert sel[r].tolist() == list(range(ns)) + list(range(n - nl, n)) + order
+        want = s0[r].copy()
+        want[order] = 0xFF80
+        np.testing.assert_array_equal(s[r], want)
