@@ -223,3 +223,56 @@ def test_select_is_the_exact_top_k():
         want = s0[r].copy()
         want[order] = 0xFF80
         np.testing.assert_array_equal(s[r], want)
+
+
+def test_index_update_against_float64():
+    """Index update of the new token (ours_graph.py:43-90): per KV head, code = clamp(rint(k.U / scale),
+    +-127); per query head, zp = bf16(k.W) - colmean, cluster = argmax_c(zp.cent_c - |cent_c|^2 / 2)
+    (ties -> lower id), then n_b += 1, Sk += k, Sk2 += k^2, Sv += v (one fp32 add each) and the position
+    appended to the cluster's generated list while it has room (the count always advances).  Codes
+    within one step of the float64 value; the cluster equal to the float64 choice unless the two best
+    are within 1e-3; the sums exactly."""
+    rng = np.random.default_rng(13)
+    Lmax, C, D, pos, rmax = 64, 12, 128, 40, 256
+    st = O.new_state(1, Lmax, C, rmax)
+    st["U"][0] = (rng.normal(size=(8, D, 32)) / np.sqrt(D)).astype(np.float32)
+    st["scale"][0] = (np.abs(rng.normal(size=(8, 32))) * 0.05 + 0.02).astype(np.float32)
+    st["W"][0] = _bf16_bits(rng.normal(size=(32, D, 16)) / np.sqrt(D))
+    st["colmean"][0] = (rng.normal(size=(32, 16)) * 0.1).astype(np.float32)
+    st["cent"][0] = rng.normal(size=(32, C, 16)).astype(np.float32)
+    st["nb"][0] = rng.integers(1, 20, (32, C)).astype(np.float32)
+    for k_ in ("Sk", "Sk2", "Sv"):
+        st[k_][0] = rng.normal(size=(32, C, D)).astype(np.float32)
+    st["reccnt"][0] = rng.integers(0, 5, (32, C)).astype(np.int32)
+    st["reccnt"][0, :8] = rmax  # the first KV head's query heads: lists already full
+    K = _bf16_bits(rng.normal(size=(1, 8, Lmax, D)))
+    V = _bf16_bits(rng.normal(size=(1, 8, Lmax, D)))
+    snap = {k_: v.copy() for k_, v in st.items()}
+    O.index_update(st, K, V, pos)
+    kf = O.bf16_to_f32(K[0, :, pos]).astype(np.float64)  # (8, D)
+    vf32, kf32 = O.bf16_to_f32(V[0, :, pos]), O.bf16_to_f32(K[0, :, pos])
+    z = np.einsum("kd,kdj->kj", kf, st["U"][0].astype(np.float64)) / st["scale"][0]
+    code_ref = np.clip(np.rint(z), -127, 127)
+    assert np.abs(st["codes"][0, :, pos].astype(np.int64) - code_ref).max() <= 1
+    assert (st["codes"][0, :, pos] != code_ref).sum() <= 2
+    cent = st["cent"][0].astype(np.float64)
+    for h in range(32):
+        kv = h // 4
+        proj = kf[kv] @ O.bf16_to_f32(st["W"][0, h]).astype(np.float64)
+        zp = O.bf16_to_f32(_round_bf16(proj.astype(np.float32))).astype(np.float64) - st["colmean"][0, h]
+        dist = cent[h] @ zp - 0.5 * (cent[h] ** 2).sum(1)
+        cid = int(st["asg"][0, h, pos])
+        best = int(np.argmax(dist))
+        assert cid == best or dist[best] - dist[cid] < 1e-3, (h, cid, best)
+        others = np.arange(C) != cid
+        np.testing.assert_array_equal(st["nb"][0, h, others], snap["nb"][0, h, others])
+        assert st["nb"][0, h, cid] == snap["nb"][0, h, cid] + 1
+        np.testing.assert_array_equal(st["Sk"][0, h, cid], snap["Sk"][0, h, cid] + kf32[kv])
+        np.testing.assert_array_equal(st["Sk2"][0, h, cid], snap["Sk2"][0, h, cid] + kf32[kv] * kf32[kv])
+        np.testing.assert_array_equal(st["Sv"][0, h, cid], snap["Sv"][0, h, cid] + vf32[kv])
+        np.testing.assert_array_equal(st["Sk"][0, h, others], snap["Sk"][0, h, others])
+        cnt = int(snap["reccnt"][0, h, cid])
+        assert st["reccnt"][0, h, cid] == cnt + 1
+        if cnt < rmax:
+            assert st["reclist"][0, h, cid, cnt] == pos
+        np.testing.assert_array_equal(st["reclist"][0, h, others], snap["reclist"][0, h, others])
