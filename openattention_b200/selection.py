@@ -25,6 +25,26 @@ def _need(name, t, dtype, shape=None):
         raise RuntimeError(f"{name}: shape {tuple(t.shape)} != {tuple(shape)}")
 
 
+def _on(dev, *named):
+    """Every given (name, tensor) pair, None skipped, is a CUDA tensor on `dev`.  A kernel given a host
+    tensor's address would fault or, on a GPU that can reach host memory, silently read the wrong
+    memory; a tensor on another GPU would be read across the link, or not at all."""
+    for name, t in named:
+        if t is not None and (not t.is_cuda or t.device != dev):
+            raise RuntimeError(f"{name}: need a tensor on {dev}, got one on {t.device}")
+
+
+def _state_on(dev, st):
+    _on(dev, *((f"state[{k!r}]", t) for k, t in st.items()))
+
+
+def _rows(name, t, dtype, R, cols=None):
+    """(R, cols) rows of `dtype` whose last dimension is contiguous (the row stride is passed on)."""
+    if t.dtype != dtype or t.dim() != 2 or t.shape[0] != R or t.stride(1) != 1 or (cols is not None and t.shape[1] != cols):
+        raise RuntimeError(f"{name}: need ({R}, {cols if cols is not None else 'n'}) {dtype} rows with a contiguous "
+                           f"last dim, got {tuple(t.shape)} {t.dtype}")
+
+
 def append_kv(K, V, k_new, v_new, n_dev, offset=0, advance=True, kv_idx=None):
     """Writes the new token's K/V rows (B, 8, 128) at position n_dev + offset of the caches (B, 8, Lmax,
     128) in one launch; with advance, n_dev += 1 and kv_idx (int64, optional) = the old n_dev."""
@@ -36,6 +56,7 @@ def append_kv(K, V, k_new, v_new, n_dev, offset=0, advance=True, kv_idx=None):
     _need("n_dev", n_dev, torch.int32, (1,))
     if kv_idx is not None:
         _need("kv_idx", kv_idx, torch.int64, (1,))
+    _on(K.device, ("V", V), ("k_new", k_new), ("v_new", v_new), ("n_dev", n_dev), ("kv_idx", kv_idx))
     _lib.call("oa_append_kv", _ptr(K), _ptr(V), B, Lmax, _ptr(k_new), _ptr(v_new), _ptr(n_dev), int(offset),
               1 if advance else 0, _ptr(kv_idx), _stream(K))
 
@@ -52,6 +73,8 @@ def index_update(K, V, st, n_dev, q=None, zq=None, k_new=None, v_new=None):
         if q.dtype != torch.bfloat16 or q.stride(-1) != 1 or q.shape != (B * HQ, D):
             raise RuntimeError("q must be (B*32, 128) bf16 with a contiguous last dim")
         _need("zq", zq, torch.bfloat16, (B * HQ, RQ))
+    _on(K.device, ("V", V), ("n_dev", n_dev), ("q", q), ("zq", zq), ("k_new", k_new), ("v_new", v_new))
+    _state_on(K.device, st)
     rec = st.get("reclist")
     rmax = 0 if rec is None else rec.shape[-1]
     tail = (_ptr(st["codes"]), _ptr(st["U"]), _ptr(st["scale"]), _ptr(st["W"]), _ptr(st["colmean"]), _ptr(st["cent"]),
@@ -71,6 +94,7 @@ def qgs_scan(codes, zq, n_dev, ns, nl, scores, tile_max, status=None):
     _need("zq", zq, torch.bfloat16, (B * HQ, RQ))
     if scores.dtype != torch.bfloat16 or tile_max.dtype != torch.float32 or scores.stride(1) != 1:
         raise RuntimeError("scores must be bf16 (R, >= Lmax) and tile_max fp32 (R, >= NT)")
+    _on(codes.device, ("zq", zq), ("n_dev", n_dev), ("scores", scores), ("tile_max", tile_max), ("status", status))
     _lib.call("oa_qgs_scan", _ptr(codes), _ptr(zq), B, Lmax, _ptr(n_dev), int(ns), int(nl), _ptr(scores),
               scores.stride(0), _ptr(tile_max), tile_max.stride(0), _ptr(status), _stream(codes))
 
@@ -78,6 +102,9 @@ def qgs_scan(codes, zq, n_dev, ns, nl, scores, tile_max, status=None):
 def qgs_select(scores, tile_max, Lmax, n_dev, ns, nl, k_top, sel):
     R = scores.shape[0]
     _need("sel", sel, torch.int32, (R, ns + nl + k_top))
+    _rows("scores", scores, torch.bfloat16, R)
+    _rows("tile_max", tile_max, torch.float32, R)
+    _on(scores.device, ("tile_max", tile_max), ("n_dev", n_dev), ("sel", sel))
     _lib.call("oa_qgs_select", _ptr(scores), scores.stride(0), _ptr(tile_max), tile_max.stride(0), R, Lmax,
               _ptr(n_dev), int(ns), int(nl), int(k_top), _ptr(sel), _stream(scores))
 
@@ -90,6 +117,11 @@ def errorgate_waterfill(q, K, st, sel, E, score, nt, quota, status=None, zdot=No
     for nm, t in (("score", score), ("nt", nt), ("quota", quota), ("zdot", zdot)):
         _need(nm, t, torch.float32, (R, C))
     _need("sel", sel, torch.int32)
+    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
+    _rows("q", q, torch.bfloat16, R, D)
+    _on(K.device, ("q", q), ("sel", sel), ("score", score), ("nt", nt), ("quota", quota), ("zdot", zdot),
+        ("status", status))
+    _state_on(K.device, st)
     _lib.call("oa_errorgate_waterfill", _ptr(q), q.stride(0), _ptr(K), B, Lmax, C, _ptr(st["asg"]), _ptr(sel),
               sel.shape[1], _ptr(st["Sk"]), _ptr(st["Sk2"]), _ptr(st["nb"]), float(E), _ptr(score), _ptr(nt),
               _ptr(quota), _ptr(zdot), _ptr(status), _stream(K))
@@ -106,6 +138,11 @@ def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx, status=None, workspace=No
     B, _, Lmax = st["asg"].shape
     C = st["nb"].shape[-1]
     _need("exp_idx", exp_idx, torch.int32, (R, E))
+    _need("quota", quota, torch.float32, (R, C))
+    _rows("scores", scores, torch.bfloat16, R)
+    _on(scores.device, ("quota", quota), ("n_dev", n_dev), ("n0_dev", n0_dev), ("exp_idx", exp_idx),
+        ("status", status), ("workspace", workspace))
+    _state_on(scores.device, st)
     rec = st.get("reclist")
     _lib.call("oa_topq", _ptr(scores), scores.stride(0), R, Lmax, C, _ptr(st["mem"]), _ptr(st["cstart"]),
               _ptr(st["clen"]), _ptr(st["asg"]), _ptr(rec), _ptr(st.get("reccnt")),
@@ -120,6 +157,15 @@ def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn, status=None):
     _need("kbar", kbar, torch.bfloat16, (R, C, D))
     _need("vbar", vbar, torch.bfloat16, (R, C, D))
     _need("logn", logn, torch.float32, (R, C))
+    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("V", V, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("sel", sel, torch.int32)
+    _need("exp_idx", exp_idx, torch.int32)
+    _need("nt", nt, torch.float32, (R, C))
+    _need("quota", quota, torch.float32, (R, C))
+    _on(K.device, ("V", V), ("sel", sel), ("exp_idx", exp_idx), ("nt", nt), ("quota", quota), ("kbar", kbar),
+        ("vbar", vbar), ("logn", logn), ("status", status))
+    _state_on(K.device, st)
     _lib.call("oa_residual", _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["asg"]), _ptr(sel), sel.shape[1], _ptr(exp_idx),
               exp_idx.shape[1], _ptr(st["Sk"]), _ptr(st["Sv"]), _ptr(nt), _ptr(quota), _ptr(kbar), _ptr(vbar),
               _ptr(logn), _ptr(status), _stream(K))
@@ -136,6 +182,16 @@ def residual_flash(q, K, V, st, sel, exp_idx, nt, quota, out, kbar=None, vbar=No
         raise RuntimeError("out must be (B*32, 128) bf16 or fp32 with a contiguous last dim")
     code = _lib.OA_F32 if out.dtype == torch.float32 else _lib.OA_BF16
     _need("zdot", zdot, torch.float32, (R, C))
+    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("V", V, torch.bfloat16, (B, HKV, Lmax, D))
+    _rows("q", q, torch.bfloat16, R, D)
+    _need("sel", sel, torch.int32)
+    _need("exp_idx", exp_idx, torch.int32)
+    _need("nt", nt, torch.float32, (R, C))
+    _need("quota", quota, torch.float32, (R, C))
+    _on(K.device, ("q", q), ("V", V), ("sel", sel), ("exp_idx", exp_idx), ("nt", nt), ("quota", quota), ("out", out),
+        ("kbar", kbar), ("vbar", vbar), ("logn", logn), ("status", status), ("zdot", zdot))
+    _state_on(K.device, st)
     _lib.call("oa_residual_flash", _ptr(q), q.stride(0), _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["asg"]), _ptr(sel),
               sel.shape[1], _ptr(exp_idx), exp_idx.shape[1], _ptr(st["Sk"]), _ptr(st["Sv"]), _ptr(nt), _ptr(quota),
               _ptr(zdot), _ptr(kbar), _ptr(vbar), _ptr(logn), _ptr(out), out.stride(0), code, float(sm_scale),

@@ -1,0 +1,60 @@
+"""The Python stage wrappers reject tensors a kernel cannot use before anything reaches the library:
+host tensors (whose addresses a kernel would fault on, or on a GPU that can reach host memory read
+silently), tensors on another device, and rows of the wrong dtype or layout.  CPU only: every call
+here must raise before its first launch."""
+import pytest
+import torch
+
+from openattention_b200 import selection as S
+from openattention_b200.geometry import D, HKV, HQ, RQ
+
+B, Lmax, C, E, NS = 1, 64, 8, 16, 5
+R = B * HQ
+
+
+def _host_inputs():
+    bf, f32, i32 = torch.bfloat16, torch.float32, torch.int32
+    st = S.new_state(B, Lmax, C, "cpu")
+    return dict(
+        K=torch.zeros(B, HKV, Lmax, D, dtype=bf), V=torch.zeros(B, HKV, Lmax, D, dtype=bf), st=st,
+        q=torch.zeros(R, D, dtype=bf), zq=torch.zeros(R, RQ, dtype=bf), n_dev=torch.ones(1, dtype=i32),
+        scores=torch.zeros(R, S.padded_len(Lmax), dtype=bf), tmax=torch.zeros(R, Lmax // 32, dtype=f32),
+        sel=torch.zeros(R, NS, dtype=i32), exp_idx=torch.zeros(R, E, dtype=i32), nt=torch.zeros(R, C, dtype=f32),
+        quota=torch.zeros(R, C, dtype=f32), score=torch.zeros(R, C, dtype=f32), out=torch.zeros(R, D, dtype=f32),
+        kbar=torch.zeros(R, C, D, dtype=bf), vbar=torch.zeros(R, C, D, dtype=bf), logn=torch.zeros(R, C, dtype=f32),
+        k_new=torch.zeros(B, HKV, D, dtype=bf), v_new=torch.zeros(B, HKV, D, dtype=bf))
+
+
+CALLS = {
+    "append_kv": lambda x: S.append_kv(x["K"], x["V"], x["k_new"], x["v_new"], x["n_dev"]),
+    "index_update": lambda x: S.index_update(x["K"], x["V"], x["st"], x["n_dev"], q=x["q"], zq=x["zq"]),
+    "qgs_scan": lambda x: S.qgs_scan(x["st"]["codes"], x["zq"], x["n_dev"], 1, 1, x["scores"], x["tmax"]),
+    "qgs_select": lambda x: S.qgs_select(x["scores"], x["tmax"], Lmax, x["n_dev"], 1, 1, NS - 2, x["sel"]),
+    "errorgate_waterfill": lambda x: S.errorgate_waterfill(x["q"], x["K"], x["st"], x["sel"], E, x["score"],
+                                                           x["nt"], x["quota"]),
+    "topq": lambda x: S.topq(x["scores"], x["st"], x["quota"], E, x["n_dev"], x["n_dev"], x["exp_idx"]),
+    "residual": lambda x: S.residual(x["K"], x["V"], x["st"], x["sel"], x["exp_idx"], x["nt"], x["quota"],
+                                     x["kbar"], x["vbar"], x["logn"]),
+    "residual_flash": lambda x: S.residual_flash(x["q"], x["K"], x["V"], x["st"], x["sel"], x["exp_idx"], x["nt"],
+                                                 x["quota"], x["out"]),
+}
+
+
+@pytest.mark.parametrize("name", list(CALLS))
+def test_host_tensors_are_rejected(name):
+    with pytest.raises(RuntimeError, match="CUDA|need a tensor on"):
+        CALLS[name](_host_inputs())
+
+
+def test_device_and_layout_helpers():
+    cuda0 = torch.device("cuda", 0)
+    with pytest.raises(RuntimeError, match="need a tensor on cuda:0"):
+        S._on(cuda0, ("x", torch.zeros(2)))
+    S._on(cuda0, ("none", None))  # absent optional tensors pass
+    with pytest.raises(RuntimeError, match="state\\['nb'\\]"):
+        S._state_on(cuda0, {"nb": torch.zeros(1)})
+    S._rows("q", torch.zeros(4, 8, dtype=torch.bfloat16), torch.bfloat16, 4, 8)
+    for bad in (torch.zeros(4, 8, dtype=torch.float32), torch.zeros(3, 8, dtype=torch.bfloat16),
+                torch.zeros(8, 4, dtype=torch.bfloat16).t(), torch.zeros(4, 8, 1, dtype=torch.bfloat16)):
+        with pytest.raises(RuntimeError, match="contiguous last dim"):
+            S._rows("q", bad, torch.bfloat16, 4, 8)
