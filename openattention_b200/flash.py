@@ -42,6 +42,13 @@ def _check(name, t, dtype, ndim):
         raise RuntimeError(f"{name} must have {ndim} dims, got shape {tuple(t.shape)}")
 
 
+def _same_device(dev, **tensors):
+    for name, t in tensors.items():
+        if t is not None and (not isinstance(t, torch.Tensor) or t.device != dev):
+            where = t.device if isinstance(t, torch.Tensor) else type(t).__name__
+            raise RuntimeError(f"{name} must be a tensor on {dev} (q's device), got {where}")
+
+
 def _flash(entry, q, k, v, sel_idx, exp_idx, kbar, vbar, log_n, sm_scale, nb, out_dtype, nsplit, out,
            workspace):
     _check("q", q, torch.bfloat16, 2)
@@ -54,6 +61,10 @@ def _flash(entry, q, k, v, sel_idx, exp_idx, kbar, vbar, log_n, sm_scale, nb, ou
                            f"k {tuple(k.shape)}, v {tuple(v.shape)}")
     if q.stride(1) != 1 or k.stride(2) != 1:
         raise RuntimeError("the last dim of q, k and v must be contiguous")
+    # every tensor on q's GPU: a host tensor's address would fault in the kernel (or, where the GPU
+    # can reach host memory, be read silently), and another GPU's would be read across the link
+    dev = q.device
+    _same_device(dev, k=k, v=v, sel_idx=sel_idx, exp_idx=exp_idx, out=out, workspace=workspace)
     sel_idx = sel_idx.to(torch.int32).contiguous()
     exp_idx = exp_idx.to(torch.int32).contiguous()
     if sel_idx.dim() != 2 or exp_idx.dim() != 2 or sel_idx.shape[0] != BQ or exp_idx.shape[0] != BQ:
@@ -63,6 +74,9 @@ def _flash(entry, q, k, v, sel_idx, exp_idx, kbar, vbar, log_n, sm_scale, nb, ou
         _check("kbar", kbar, torch.bfloat16, 3)
         _check("vbar", vbar, torch.bfloat16, 3)
         _check("log_n", log_n, torch.float32, 2)
+        _same_device(dev, kbar=kbar, vbar=vbar, log_n=log_n)
+        if log_n.stride(1) != 1:
+            raise RuntimeError("log_n must have a contiguous last dim")
         if kbar.stride() != vbar.stride() or kbar.shape != vbar.shape or kbar.stride(2) != 1:
             raise RuntimeError("kbar/vbar must share shape and strides with a contiguous last dim")
         if NB > kbar.shape[1] or log_n.shape[1] < NB:
@@ -74,6 +88,11 @@ def _flash(entry, q, k, v, sel_idx, exp_idx, kbar, vbar, log_n, sm_scale, nb, ou
         out_dtype = q.dtype
     if out is None:
         out = torch.empty(BQ, D, dtype=out_dtype, device=q.device)
+    elif out.dtype not in (torch.bfloat16, torch.float32) or out.shape != (BQ, D) or out.stride(1) != 1:
+        raise RuntimeError(f"out must be ({BQ}, {D}) bf16 or fp32 with a contiguous last dim, got "
+                           f"{tuple(out.shape)} {out.dtype}")
+    if workspace is not None and workspace.dtype != torch.uint8:
+        raise RuntimeError("workspace must be a uint8 tensor (its size is its byte count)")
     code = {torch.bfloat16: _lib.OA_BF16, torch.float32: _lib.OA_F32}[out.dtype]
     lib = _lib.load()
     need = lib.oa_flash_workspace_bytes(BQ, sel_idx.shape[1], exp_idx.shape[1], NB, int(nsplit))

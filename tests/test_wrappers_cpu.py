@@ -58,3 +58,20 @@ def test_device_and_layout_helpers():
                 torch.zeros(8, 4, dtype=torch.bfloat16).t(), torch.zeros(4, 8, 1, dtype=torch.bfloat16)):
         with pytest.raises(RuntimeError, match="contiguous last dim"):
             S._rows("q", bad, torch.bfloat16, 4, 8)
+
+
+def test_flash_entries_reject_host_and_foreign_tensors():
+    from openattention_b200 import flash as F
+    bf = torch.bfloat16
+    q, k = torch.zeros(4, D, dtype=bf), torch.zeros(1, 16, D, dtype=bf)
+    sel, ex = torch.zeros(4, 2, dtype=torch.int32), torch.zeros(4, 3, dtype=torch.int32)
+    kb, ln = torch.zeros(1, 2, D, dtype=bf), torch.zeros(4, 2)
+    for fn in (F.decode_expand_attention, F.ours_flash):
+        with pytest.raises(RuntimeError, match="CUDA"):
+            fn(q, k, k, sel, ex, kb, kb, ln)
+    cuda0 = torch.device("cuda", 0)
+    F._same_device(cuda0, out=None, workspace=None)
+    with pytest.raises(RuntimeError, match="sel_idx must be a tensor on cuda:0"):
+        F._same_device(cuda0, sel_idx=sel)
+    with pytest.raises(RuntimeError, match="exp_idx must be a tensor on cuda:0 .*list"):
+        F._same_device(cuda0, exp_idx=[1, 2])
