@@ -34,6 +34,28 @@ def test_library_exports_every_declared_symbol():
         assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
 
 
+def header_arities():
+    """Parameter count of every oa_* function the public header declares."""
+    out = {}
+    inc = os.path.join(ROOT, "include")
+    for f in sorted(os.listdir(inc)):
+        if f.endswith(".h"):
+            src = re.sub(r"/\*.*?\*/", "", open(os.path.join(inc, f)).read(), flags=re.S)
+            for name, params in re.findall(r"\b(oa_\w+)\s*\(([^;{]*?)\)\s*;", src, flags=re.S):
+                params = params.strip()
+                out[name] = 0 if params in ("", "void") else params.count(",") + 1
+    return out
+
+
+def test_ctypes_signatures_match_the_header():
+    """A ctypes argument list longer or shorter than the C declaration would pass garbage silently."""
+    arities = header_arities()
+    assert set(arities) == set(header_functions())
+    for name, n in arities.items():
+        assert len(_lib.SIGNATURES[name][1]) == n, f"{name}: header has {n} parameters, ctypes table " \
+                                                   f"{len(_lib.SIGNATURES[name][1])}"
+
+
 def test_version_and_error_path():
     lib = _lib.load()
     assert b"sm_100a" in lib.oa_version()
