@@ -46,6 +46,8 @@ B_PER_GPU, N_CTX, RHO = 32, 32768, 0.01
 VALUE_SLOTS = 4  # step graphs the `value` loop takes in turn (their inputs are staged before timing)
 SCAN_BYTES_PER_TOKEN = 32  # int8 codes per token per KV head (the scan's algorithmic bytes)
 LAUNCHES_PER_STEP = 7      # append_kv, index_update, qgs_scan, qgs_select, errorgate_waterfill, topq, residual_flash
+CLOCK_SOAK_S = 0.5         # step replays before warm-up while the clock sampler runs (state reset after)
+CLOCK_SOAK_MAX_STEPS = 4096
 
 
 def dist_env():
@@ -90,7 +92,7 @@ class Clocks:
     def __enter__(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                                          "-lms", "20"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
             t_end = time.time() + 5.0
@@ -102,7 +104,7 @@ class Clocks:
 
     def _read(self):
         for line in self.proc.stdout:
-            self.lines.append(line.strip())
+            self.lines.append((time.time(), line.strip()))
 
     def __exit__(self, *exc):
         if self.proc is not None:
@@ -112,10 +114,13 @@ class Clocks:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
 
-    def summary(self):
+    def summary(self, t0=None, t1=None, window=""):
+        """Median SM clock, max clock and throttle reasons over the samples taken in [t0, t1] (host time)."""
         sm, mx, reasons = [], None, set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines[1:]:  # the first sample predates the load
+        for ts, ln in self.lines[1:]:  # the first sample predates the load
+            if (t0 is not None and ts < t0) or (t1 is not None and ts > t1):
+                continue
             f = [x.strip() for x in ln.split(",")]
             if len(f) < 9 or f[0] != self.index:
                 continue
@@ -127,20 +132,24 @@ class Clocks:
             for nm, v in zip(names, f[5:9]):
                 if v.lower().startswith("active"):
                     reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+               "samples": len(sm)}
+        if window:
+            out["window"] = window
+        return out
 
 
 # ------------------------------------------------------------------ our arm
-def build_workload(dev, seed, steps_total):
+def build_workload(dev, seed, steps_total, extra_positions=0):
     from openattention_b200 import method as Mth
     from openattention_b200 import synth
     from openattention_b200.geometry import HQ
     B, n0 = B_PER_GPU, N_CTX
-    Lmax = n0 + steps_total + 16
+    Lmax = n0 + steps_total + extra_positions + 16
     K, V, mus = synth.kv_torch(seed, B, n0, Lmax, dev)
     Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40] * B
-    m = Mth.OursB200(types.SimpleNamespace(rho=RHO), B, Lmax, dev, layers=1)
+    m = Mth.OursB200(types.SimpleNamespace(rho=RHO, static_metric=synth.static_metric_standin(7, 1)), B, Lmax, dev,
+                     layers=1)
     g = torch.Generator(device=dev)
     qpre = torch.empty(1, HQ, n0, 128, dtype=torch.bfloat16, device=dev)
     for b in range(B):
@@ -399,7 +408,8 @@ def run_ours(a):
     steps_total = a.warmup + 2 * a.steps + 8
     from openattention_b200 import shard
     # every rank runs its own B=32 requests (request sharding, shard.plan with batch = 32 * world)
-    m, Mth, qs, nks, nvs, n0, Lmax = build_workload(dev, seed=shard.request_seed(17, rank), steps_total=steps_total)
+    m, Mth, qs, nks, nvs, n0, Lmax = build_workload(dev, seed=shard.request_seed(17, rank), steps_total=steps_total,
+                                                    extra_positions=CLOCK_SOAK_MAX_STEPS)
     gs = GraphStep(m, Mth, n0, dev)
     # `value`: VALUE_SLOTS step graphs with input buffers of their own, filled once before timing and
     # taken in turn, so the timed steps read inputs already resident in HBM (no staging copies)
@@ -429,18 +439,28 @@ def run_ours(a):
     def max_over_ranks(x):
         return shard.max_over_ranks(x, device=dev)
 
-    # ---- value: device-resident inputs (clocks sampled over warm-up and the timed region)
+    # ---- value: device-resident inputs.  The nvidia-smi sampler (20 ms) runs from a clock soak through
+    #      the timed region: the soak replays the same step for CLOCK_SOAK_S (state restored after it),
+    #      so the clock record covers the step under load even when K steps take only a few ms.
     clk = Clocks(dev).__enter__()
+    t_soak = time.time()
+    soak = 0
+    while soak < CLOCK_SOAK_MAX_STEPS and time.time() - t_soak < CLOCK_SOAK_S:
+        for _ in range(32):
+            gsv[soak % VALUE_SLOTS].replay()
+            soak += 1
+        torch.cuda.synchronize()
+    reset()
     for s in range(a.warmup):
         gsv[s % VALUE_SLOTS].replay()
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    if True:
-        e0.record()
-        for s in range(a.steps):
-            gsv[(a.warmup + s) % VALUE_SLOTS].replay()
-        e1.record()
-        torch.cuda.synchronize()
+    e0.record()
+    for s in range(a.steps):
+        gsv[(a.warmup + s) % VALUE_SLOTS].replay()
+    e1.record()
+    torch.cuda.synchronize()
+    t_timed_end = time.time()
     clk.__exit__(None, None, None)
     barrier()
     ms = max_over_ranks(e0.elapsed_time(e1) / a.steps)
@@ -535,7 +555,9 @@ def run_ours(a):
             "stages": stages,
             "step_roofline": {"alg_bytes": step_alg, "achieved": round(step_gbs, 1), "unit": "GB/s",
                               "frac": round(step_gbs / peak, 4), "n": n_now},
-            "clocks": clk.summary(),
+            "clocks": clk.summary(t_soak, t_timed_end + 0.05,
+                                  window=f"clock soak ({soak} replays of the step, {CLOCK_SOAK_S:g} s) through the timed "
+                                         "region"),
             "cpu_baseline": cpu,
             "stage_us_per_step_per_gpu": round(ms * 1e3, 3),
         }
@@ -567,7 +589,8 @@ def sweep_point(dev, B, n0, rho, steps, warmup):
     V = V1.expand(B, -1, -1, -1).contiguous()
     del K1, V1
     Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40] * B
-    m = Mth.OursB200(types.SimpleNamespace(rho=rho), B, Lmax, dev, layers=1)
+    m = Mth.OursB200(types.SimpleNamespace(rho=rho, static_metric=synth.static_metric_standin(7, 1)), B, Lmax, dev,
+                     layers=1)
     g = torch.Generator(device=dev)
     g.manual_seed(43)
     qpre = torch.zeros(1, HQ, n0, 128, dtype=torch.bfloat16, device=dev)

@@ -91,8 +91,11 @@ size_t oa_flash_workspace_bytes(int64_t BQ, int64_t n_sel, int64_t n_exp, int64_
  * point calls no cudaMalloc, cudaFree or other allocating routine.
  *
  * Set-up: the first call on a device (with that device current) looks up the array's device
- * address and keeps it; make that first call before any stream capture.  Every call clears the
- * ticket counters on `stream` before its kernel.  All calls on one device share the one array, which
+ * address and keeps it; make that first call before any stream capture.  The kept address belongs to
+ * the device's primary context: after cudaDeviceReset (or anything else that destroys that context)
+ * it is stale, so do not call this entry point again in that process.  Every call that passes its
+ * argument checks clears the ticket counters on `stream` before its kernel (a rejected call touches
+ * nothing).  All calls on one device share the one array, which
  * keeps the last call's contents: calls that overlap on the GPU (other streams, other host threads)
  * race on it and give wrong results, so order them (one stream, or events). */
 int oa_flash_qhead_proxies_noalloc(const void* q, int64_t q_stride, const void* k, const void* v,

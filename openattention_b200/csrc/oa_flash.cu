@@ -248,8 +248,10 @@ int flash_entry(bool qhead, const void* q, int64_t q_stride, const void* k, cons
                 const void* kbar, const void* vbar, int64_t kb_sh, int64_t kb_sb, const float* log_n,
                 int64_t ln_stride, void* out, int64_t out_stride, int out_dtype, int64_t BQ, int64_t BH,
                 int64_t K, int64_t NB, float sm_scale, int nsplit, void* workspace, size_t ws_bytes,
-                void* stream) {
-  const char* fn = qhead ? "oa_flash_qhead_proxies" : "oa_flash_kvhead_proxies";
+                void* stream, const char* fn_name = nullptr, bool clear_tickets = false) {
+  // fn_name: the entry point named in error messages; clear_tickets: zero the split's ticket counters on
+  // `stream` before the kernel, once every argument has been checked (a rejected call changes nothing)
+  const char* fn = fn_name ? fn_name : (qhead ? "oa_flash_qhead_proxies" : "oa_flash_kvhead_proxies");
   OA_REQUIRE(BQ > 0 && BH > 0 && BQ % BH == 0, "%s: need BQ > 0, BH > 0 and BQ %% BH == 0 (BQ=%lld BH=%lld)",
              fn, (long long)BQ, (long long)BH);
   OA_REQUIRE(BQ <= 0x7fffffff, "%s: BQ too large", fn);
@@ -314,6 +316,10 @@ int flash_entry(bool qhead, const void* q, int64_t q_stride, const void* k, cons
   }
   dim3 grid((unsigned)BQ, (unsigned)ns);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (clear_tickets && a.cnt != nullptr) {
+    const cudaError_t e = cudaMemsetAsync(a.cnt, 0, (size_t)BQ * sizeof(unsigned), st);
+    if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: clearing the ticket counters failed: %s", fn, cudaGetErrorString(e));
+  }
   if (qhead) {
     if (out_dtype == OA_F32)
       flash_kernel<true, true><<<grid, kThreads, 0, st>>>(a);
@@ -381,7 +387,10 @@ std::mutex g_scratch_mu;
 void* g_scratch_ptr[kNoAllocMaxDevices] = {};
 
 // Device address of g_flash_scratch on the current device, looked up once per device (with that
-// device current) and kept for later calls.  Returns a status; *out is set on success.
+// device current) and kept for later calls.  Returns a status; *out is set on success.  The kept
+// address belongs to the device's primary context: after cudaDeviceReset (or anything else that
+// destroys and recreates that context) it is stale, and this entry point must not be used again in
+// the process.
 int scratch_on_current_device(const char* fn, void** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
@@ -429,14 +438,10 @@ extern "C" int oa_flash_qhead_proxies_noalloc(const void* q, int64_t q_stride, c
   if (need > 0) {
     const int rc = oa::scratch_on_current_device(fn, &scratch);
     if (rc != OA_OK) return rc;
-    // The ticket counters must start at zero; clear them rather than trust what an earlier call left.
-    const cudaError_t e =
-        cudaMemsetAsync(scratch, 0, (size_t)BQ * sizeof(unsigned), static_cast<cudaStream_t>(stream));
-    if (e != cudaSuccess) {
-      return oa_fail(OA_ERR_CUDA, "%s: clearing the ticket counters failed: %s", fn, cudaGetErrorString(e));
-    }
   }
+  // The ticket counters must start at zero: flash_entry clears them on the stream (rather than trust what
+  // an earlier call left), after it has checked every argument, so a rejected call leaves the array as it was.
   return oa::flash_entry(true, q, q_stride, k, v, kv_stride_h, kv_stride_t, sel, n_sel, exp_idx, n_exp, kbar,
                          vbar, kbar_stride_h, kbar_stride_b, log_n, log_n_stride, out, out_stride, out_dtype, BQ,
-                         BH, K, NB, sm_scale, nsplit, scratch, need, stream);
+                         BH, K, NB, sm_scale, nsplit, scratch, need, stream, fn, /*clear_tickets=*/true);
 }

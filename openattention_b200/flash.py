@@ -20,12 +20,15 @@ SC = 128 ** -0.5
 _ws_cache: dict = {}
 
 
-def _workspace(device: torch.device, rows: int, nbytes: int) -> torch.Tensor | None:
-    """Zero-filled scratch for the split-K mode, cached per (device, row count) and grown on demand
-    (its leading per-row ticket counters are only guaranteed zero for the row count it served)."""
+def _workspace(device: torch.device, rows: int, nbytes: int, stream: int) -> torch.Tensor | None:
+    """Zero-filled scratch for the split-K mode, cached per (device, stream, row count) and grown on
+    demand (its leading per-row ticket counters are only guaranteed zero for the row count it served).
+    Keyed by stream: calls on one stream run in order and may share a workspace, while calls on two
+    streams can overlap on the GPU and would race on one workspace's counters and partial sums.
+    Callers that pass `workspace=` themselves must give overlapping calls different workspaces."""
     if nbytes == 0:
         return None
-    key = (device.type, device.index, rows)
+    key = (device.type, device.index, stream, rows)
     ws = _ws_cache.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.zeros(nbytes, dtype=torch.uint8, device=device)
@@ -96,9 +99,9 @@ def _flash(entry, q, k, v, sel_idx, exp_idx, kbar, vbar, log_n, sm_scale, nb, ou
     code = {torch.bfloat16: _lib.OA_BF16, torch.float32: _lib.OA_F32}[out.dtype]
     lib = _lib.load()
     need = lib.oa_flash_workspace_bytes(BQ, sel_idx.shape[1], exp_idx.shape[1], NB, int(nsplit))
-    if need and workspace is None:
-        workspace = _workspace(q.device, BQ, need)
     stream = torch.cuda.current_stream(q.device).cuda_stream
+    if need and workspace is None:
+        workspace = _workspace(q.device, BQ, need, stream)
     _lib.call(entry, _lib.ptr(q), q.stride(0), _lib.ptr(k), _lib.ptr(v), k.stride(0), k.stride(1),
               _lib.ptr(sel_idx), sel_idx.shape[1], _lib.ptr(exp_idx), exp_idx.shape[1],
               _lib.ptr(kbar) if NB else 0, _lib.ptr(vbar) if NB else 0,

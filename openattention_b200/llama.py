@@ -46,7 +46,8 @@ class RandomLlama:
     """Random bf16 weights (std 1/sqrt(fan-in)), caches and the OpenAttention method for B requests
     of up to Lmax positions."""
 
-    def __init__(self, cfg: LlamaConfig, B: int, Lmax: int, dev, rho: float = 0.01, seed: int = 0):
+    def __init__(self, cfg: LlamaConfig, B: int, Lmax: int, dev, rho: float = 0.01, seed: int = 0,
+                 static_metric=None):
         self.cfg, self.B, self.Lmax = cfg, B, Lmax
         self.dev = torch.device(dev)
         g = torch.Generator(device=self.dev)
@@ -74,7 +75,13 @@ class RandomLlama:
         self.K = [torch.zeros(B, HKV, Lmax, D, dtype=torch.bfloat16, device=self.dev) for _ in range(cfg.layers)]
         self.V = [torch.zeros(B, HKV, Lmax, D, dtype=torch.bfloat16, device=self.dev) for _ in range(cfg.layers)]
         Mth.C.K, Mth.C.V, Mth.C.qlen = self.K, self.V, [cfg.qlen] * B
-        self.method = Mth.OursB200(types.SimpleNamespace(rho=rho), B, Lmax, self.dev, layers=cfg.layers)
+        # the weights are random, so the query metric of the real model means nothing here: the seeded
+        # stand-in is the default (a real checkpoint would pass the reference's asset)
+        if static_metric is None:
+            from .synth import static_metric_standin
+            static_metric = static_metric_standin(7, cfg.layers)
+        self.method = Mth.OursB200(types.SimpleNamespace(rho=rho, static_metric=static_metric), B, Lmax, self.dev,
+                                   layers=cfg.layers)
         self.graph = None
 
     # ------------------------------------------------------------------ pieces

@@ -3,7 +3,8 @@
 inference/ours_fastbuild.py:143-307 OursG3 "ours3").
 
     C.K = [...]; C.V = [...]          # per layer (B, 8, Lmax, 128) bf16 caches, owned by the caller
-    m = OursB200(SimpleNamespace(rho=0.01), B, Lmax, "cuda")
+    a = SimpleNamespace(rho=0.01, static_metric_path="llama-3.1-8b-instruct.query_metric.triu.pt")
+    m = OursB200(a, B, Lmax, "cuda")  # the metric: the reference's asset (packed or unpacked form)
     m.build(l, b, q_prefill, T)       # prefill: per layer and batch row, after K/V[:, :, :T] are written
     out = m.decode(l, q, n)           # decode: q (B, 32, 1, 128) bf16, new token already at n - 1
 
@@ -75,25 +76,36 @@ def rot_avg(Mpre: torch.Tensor, inv_freq: torch.Tensor, scaling: float, p: int, 
     return cc * M + cs * (M @ J.T) + sc * (J @ M) + ss * (J @ M @ J.T)
 
 
-def query_metric(Mpre_l, inv_freq, scaling, q, T, Qn, win=WIN, P=PQ):
-    """M = 1/2 trnorm(static metric rotated to [T, T+win)) + 1/2 trnorm(question rows)
-    (inference/methods_eager.py:510-518).  q: (1, 32, T, D) prefill queries."""
+def question_rows(Qn: int, P: int = PQ) -> torch.Tensor:
+    """Indices (into the last Qn prefill rows) of the question rows the metric uses: up to P rows spread
+    over [0, Qn - 3] (inference/methods_eager.py:512-513).  A host tensor."""
+    Pn = min(P, max(Qn - 2, 1))
+    return torch.linspace(0, max(Qn - 3, 0), Pn).long().unique()
+
+
+def metric_from_rows(Mst, qsel, pi, Qn, inv_freq, scaling):
+    """M = 1/2 trnorm(Mst) + 1/2 trnorm(Mq), Mq the mean outer product of the question rows qsel
+    (32, P, D) fp32 rotated back by RoPE at offsets Qn - pi (inference/methods_eager.py:514-518)."""
     def nt(x):
         return x / torch.diagonal(x, dim1=-2, dim2=-1).sum(-1).clamp(min=1e-12)[..., None, None]
-    dev = q.device
-    Mst = rot_avg(Mpre_l, inv_freq, scaling, T, win)
-    Pn = min(P, max(Qn - 2, 1))
-    # question rows: computed on the host (unique() on the device would stall the host until the device
-    # drains, and the prefill overlaps this with device work), moved by a non-blocking pinned copy
-    pi = torch.linspace(0, max(Qn - 3, 0), Pn).long().unique().pin_memory().to(dev, non_blocking=True)
-    qsel = q[0, :, T - Qn:, :].index_select(1, pi).float()
-    freqs = (Qn - pi).float().unsqueeze(-1) * inv_freq.to(dev).unsqueeze(0)
+    freqs = (Qn - pi).float().unsqueeze(-1) * inv_freq.unsqueeze(0)
     emb = torch.cat([freqs, freqs], -1)
     cos, sin = emb.cos() * scaling, emb.sin() * scaling
     h = D // 2
     qrot = qsel * cos + torch.cat([-qsel[..., h:], qsel[..., :h]], -1) * sin
     Mq = torch.matmul(qrot.transpose(-1, -2), qrot) / qrot.shape[1]
     return 0.5 * nt(Mst) + 0.5 * nt(Mq)
+
+
+def query_metric(Mpre_l, inv_freq, scaling, q, T, Qn, win=WIN, P=PQ):
+    """M = 1/2 trnorm(static metric rotated to [T, T+win)) + 1/2 trnorm(question rows)
+    (inference/methods_eager.py:510-518), all on q's device.  q: (1, 32, T, D) prefill queries.
+    OursB200 evaluates the same function on the host (rot_avg + metric_from_rows on CPU tensors), the
+    reference's CPU arithmetic, so that its bases equal the reference's bit for bit."""
+    Mst = rot_avg(Mpre_l, inv_freq, scaling, T, win)
+    pi = question_rows(Qn, P)
+    qsel = q[0, :, T - Qn:, :].index_select(1, pi.to(q.device)).float()
+    return metric_from_rows(Mst, qsel, pi.to(q.device), Qn, inv_freq.to(q.device), scaling)
 
 
 def basis_from_metric(M: torch.Tensor):
@@ -123,19 +135,52 @@ def kmeans_seeds(T: int, Cn: int, layer: int) -> torch.Tensor:
     return torch.randperm(T, generator=g)[:Cn]
 
 
+def unpack_metric(packed: dict) -> torch.Tensor:
+    """The full symmetric metric (..., d, d) from the shipped upper-triangle form {"M_triu": (..., d(d+1)/2),
+    "dim": d} (assets/restore_query_metric.py:18-27): entry k of a row of M_triu is M[i, j] = M[j, i]
+    for the k-th pair (i <= j) in row-major order of the upper triangle."""
+    d = int(packed["dim"])
+    tri = packed["M_triu"]
+    if tri.shape[-1] != d * (d + 1) // 2:
+        raise RuntimeError(f"M_triu has {tri.shape[-1]} entries per matrix, a {d}x{d} triangle has {d * (d + 1) // 2}")
+    i, j = torch.triu_indices(d, d)
+    M = tri.new_zeros(*tri.shape[:-1], d, d)
+    M[..., i, j] = tri
+    M[..., j, i] = tri
+    return M
+
+
 def load_static_metric(a, layers: int):
-    """The pre-RoPE query metric (L, 32, D, D): `a.static_metric` (tensor or dict), else the file named
-    by OA_STATIC_M (the reference's unpacked asset format: {"M", "inv_freq", "attention_scaling"}),
-    else the seeded stand-in of synth.static_metric_numpy."""
+    """(M (L, 32, D, D) fp32 pre-RoPE query metric, inv_freq (64,), attention scaling).
+
+    Source, first found: `a.static_metric` (a tensor, or a dict in either asset form), the file
+    `a.static_metric_path`, the file named by OA_STATIC_M.  Both forms of the reference's asset are
+    read: the shipped packed one (assets/llama-3.1-8b-instruct.query_metric.triu.pt: "M_triu", "dim",
+    "inv_freq", "attention_scaling") and the unpacked one the reference writes on first use ("M", ...,
+    inference/methods_eager.py:474-480).  Without a metric this raises: the QGS and QGC bases are
+    derived from it, and a made-up metric would silently select different tokens."""
     src = getattr(a, "static_metric", None)
-    if src is None and os.environ.get("OA_STATIC_M") and os.path.exists(os.environ["OA_STATIC_M"]):
-        src = torch.load(os.environ["OA_STATIC_M"], map_location="cpu", weights_only=False)
+    path = getattr(a, "static_metric_path", None) or os.environ.get("OA_STATIC_M")
+    if src is None and path:
+        if not os.path.exists(path):
+            raise RuntimeError(f"static query metric file {path!r} does not exist")
+        src = torch.load(path, map_location="cpu", weights_only=False)
     if src is None:
-        from .synth import static_metric_numpy
-        return static_metric_numpy(getattr(a, "metric_seed", 7), layers), llama31_inv_freq(), 1.0
+        raise RuntimeError("no static query metric: pass a.static_metric (tensor or asset dict), "
+                           "a.static_metric_path, or set OA_STATIC_M to the reference's asset "
+                           "(llama-3.1-8b-instruct.query_metric.triu.pt or its unpacked form)")
     if isinstance(src, dict):
-        return src["M"].float(), src.get("inv_freq", llama31_inv_freq()).float(), float(src.get("attention_scaling", 1.0))
-    return src.float(), llama31_inv_freq(), 1.0
+        M = unpack_metric(src) if "M_triu" in src else src["M"]
+        inv = src.get("inv_freq")
+        inv = llama31_inv_freq() if inv is None else inv
+        M, scaling = M.float(), float(src.get("attention_scaling", 1.0))
+    else:
+        M, inv, scaling = src.float(), llama31_inv_freq(), 1.0
+    if M.dim() != 4 or tuple(M.shape[1:]) != (HQ, D, D):
+        raise RuntimeError(f"static metric must be (layers, {HQ}, {D}, {D}), got {tuple(M.shape)}")
+    if M.shape[0] < layers:
+        raise RuntimeError(f"static metric holds {M.shape[0]} layers, the method needs {layers}")
+    return M[:layers].contiguous(), inv.float(), scaling
 
 
 # ------------------------------------------------------------------ the method
@@ -146,7 +191,8 @@ class OursB200:
     FUSED (default): the residual proxies and the attention run as one kernel (the K/V rows of the
     read tokens are gathered once); keep_proxies additionally writes kbar', vbar', ln n' out.
     FUSED = False runs oa_residual and then calls `flash.ours_flash` through the module attribute,
-    the hook the reference's tests spy on."""
+    the hook the reference's tests spy on; decode takes that path too whenever `flash.ours_flash` has
+    been replaced, so a harness that installs a spy sees the step's sel / exp_idx / proxies."""
     name = "ours3"
     FUSED = True
     keep_proxies = False
@@ -161,9 +207,11 @@ class OursB200:
         self.C, self.E = budget(a.rho)
         self.NL = layers or getattr(a, "layers", None) or NL
         Mpre, inv_freq, scaling = load_static_metric(a, self.NL)
-        self.Mpre = Mpre.to(self.dev)
-        self.inv_freq = inv_freq.to(self.dev)
+        # the metric is evaluated on the host, in the reference's CPU arithmetic (see build_async)
+        self.Mpre = Mpre.cpu()
+        self.inv_freq = inv_freq.cpu()
         self.scaling = scaling
+        self._mst = {}  # layer -> (T, static metric rotated to T): shared by the requests of one prefill length
         self.st = [S.new_state(B, Lmax, self.C, self.dev, RMAX) for _ in range(self.NL)]
         R, Cn, E, dev = self.R, self.C, self.E, self.dev
         self.NT = (Lmax + 31) // 32          # 32-token tiles of the QGS tile maxima
@@ -199,20 +247,30 @@ class OursB200:
         self.build_async(l, b, q, T)()
 
     def build_async(self, l, b, q, T):
-        """build() in two halves.  Now: the query metric on the device and its copy to pinned host memory
-        (q is not used after this returns).  The returned callable: the host eigen-decomposition, then
-        the device build.  A prefill loop calls it after enqueueing its next layer, so the host half
-        overlaps device work."""
+        """build() in two halves.  Now: the question rows of q (at most 64 per head) are copied to pinned
+        host memory (q is not used after this returns).  The returned callable: the query metric and its
+        eigen-decomposition on the host, then the device build.  A prefill loop calls it after enqueueing
+        its next layer, so the host half overlaps device work.
+
+        The metric is host arithmetic on purpose: it is the reference's own CPU computation, so the
+        bases (and through them codes and clusters) are bit-identical to the reference's; a device
+        evaluation would round its fp32 matmuls differently and perturb the eigenvectors."""
         Qn = C.qlen[b] if C.qlen else 40
-        M = query_metric(self.Mpre[l], self.inv_freq, self.scaling, q, T, Qn)
-        Mh = torch.empty(M.shape, dtype=torch.float32, pin_memory=True)
-        Mh.copy_(M, non_blocking=True)
+        pi = question_rows(Qn)
+        rows = q[0, :, T - Qn:, :].index_select(1, pi.pin_memory().to(q.device, non_blocking=True))
+        rows_h = torch.empty(rows.shape, dtype=rows.dtype, pin_memory=True)
+        rows_h.copy_(rows, non_blocking=True)
         done = torch.cuda.Event()
         done.record()
 
         def finish():
+            hit = self._mst.get(l)
+            if hit is None or hit[0] != T:
+                hit = (T, rot_avg(self.Mpre[l], self.inv_freq, self.scaling, T, WIN))
+                self._mst[l] = hit
             done.synchronize()
-            U, W = basis_from_host_metric(Mh)
+            M = metric_from_rows(hit[1], rows_h.float(), pi, Qn, self.inv_freq, self.scaling)
+            U, W = basis_from_host_metric(M)
             self.build_from_basis(l, b, U.to(self.dev, non_blocking=True), W.to(self.dev, non_blocking=True), T)
         return finish
 
@@ -284,7 +342,10 @@ class OursB200:
         """The reference's decode(l, q, n) (the new token's K/V already in C.K[l] / C.V[l] at n - 1).  With
         k_new, v_new (B, 8, 128) bf16 the caller leaves that write to the index update, which does it in
         the same launch (oa_index_update_append)."""
-        if not self.FUSED:
+        if not self.FUSED or flash_mod.ours_flash is not _OURS_FLASH:
+            # unfused, or a caller has replaced flash.ours_flash (the reference's equivalence harnesses
+            # swap bl.ours_flash for a spy that records sel / exp_idx / the proxies): the residual proxies
+            # are formed and the attention goes through that attribute, so the spy sees every call
             qr, sel = self.select(l, q, n, k_new=k_new, v_new=v_new)
             return self.attend(l, qr, sel, self.exp_idx, self.kbar, self.vbar, self.logn)
         qr, sel = self.select(l, q, n, residual=False, k_new=k_new, v_new=v_new)
@@ -304,3 +365,4 @@ class OursB200:
 
 
 METHODS = {"ours3": OursB200, "ours": OursB200}
+_OURS_FLASH = flash_mod.ours_flash  # the library's own operator (a replaced attribute is a caller's hook)

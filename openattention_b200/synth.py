@@ -72,6 +72,12 @@ def static_metric_numpy(seed: int, layers: int = 1):
     return torch.from_numpy(M.astype(np.float32))
 
 
+def static_metric_standin(seed: int = 7, layers: int = 1) -> dict:
+    """The stand-in in the reference asset's unpacked form, for OursB200(a, ...) with
+    a.static_metric = static_metric_standin(...) (synthetic workloads only)."""
+    return {"M": static_metric_numpy(seed, layers), "inv_freq": llama31_inv_freq(), "attention_scaling": 1.0}
+
+
 # ------------------------------------------------------------------ torch (device, large caches)
 def kv_torch(seed: int, B: int, n: int, Lmax: int, device, dtype=torch.bfloat16):
     """B requests of the same law, generated on `device`: K, V (B, 8, Lmax, D) and centroids (B, 8, 64, D)."""

@@ -27,7 +27,11 @@ DECODE_CASES = {
     "decode_c0": dict(B=1, n0=4096, steps=3, rho=0.01, seed=100, mseed=7),
     # two requests at 3% (C=192, E=679), 1024-token context
     "decode_b2_r3": dict(B=2, n0=1024, steps=2, rho=0.03, seed=200, mseed=8),
+    # one request at 1% with the REFERENCE's static query metric (layer 0 of its shipped asset, kept in
+    # metric_l0.npz in the asset's packed form) instead of the seeded stand-in
+    "decode_real_l0": dict(B=1, n0=2048, steps=2, rho=0.01, seed=300, mseed="asset"),
 }
+METRIC_FIXTURE = "metric_l0.npz"
 QLEN = 40
 
 
@@ -78,6 +82,25 @@ def decode_inputs(name):
         new_k.append(torch.stack(ks))
         new_v.append(torch.stack(vs))
         qdec.append(synth.queries_numpy(seed + 20000 + s, B * HQ).view(B, HQ, 1, D))
-    M = synth.static_metric_numpy(c["mseed"], layers=1)
+    if c["mseed"] == "asset":
+        M, inv_freq = asset_metric()
+    else:
+        M, inv_freq = synth.static_metric_numpy(c["mseed"], layers=1), synth.llama31_inv_freq()
     return dict(B=B, n0=n0, steps=steps, Lmax=Lmax, rho=c["rho"], K=K, V=V, qpre=qpre, new_k=new_k, new_v=new_v,
-                qdec=qdec, M=M)
+                qdec=qdec, M=M, inv_freq=inv_freq)
+
+
+def asset_packed():
+    """Layer 0 of the reference's static-metric asset in its shipped packed form (a dict as the asset's)."""
+    import os
+    z = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), METRIC_FIXTURE))
+    return {"M_triu": torch.from_numpy(z["M_triu"]), "dim": int(z["dim"]), "inv_freq": torch.from_numpy(z["inv_freq"]),
+            "attention_scaling": float(z["attention_scaling"])}
+
+
+def asset_metric():
+    """(M (1, 32, 128, 128), inv_freq) of asset_packed(), unpacked by this package's loader."""
+    from openattention_b200.method import load_static_metric
+    import types
+    M, inv, _ = load_static_metric(types.SimpleNamespace(static_metric=asset_packed()), 1)
+    return M, inv

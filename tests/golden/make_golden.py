@@ -5,7 +5,8 @@
 Needs a checkout of the reference (it is not available on GPU machines; the fixtures are committed).
 The reference's package __init__ pulls in ray / matplotlib / seaborn, which are stubbed here; its
 eager method class writes the unpacked static metric to OA_STATIC_M, which points at a temporary
-file holding this repository's seeded metric stand-in.  Nothing of the reference is copied: its
+file holding the case's metric: this repository's seeded stand-in, or (decode_real_l0) layer 0 of the
+reference's own asset.  Nothing of the reference is copied: its
 functions are executed and their outputs saved.
 
 Fixtures:
@@ -13,6 +14,8 @@ Fixtures:
                     evaluated on cases.flash_inputs("flash_qhead")
   flash_kvhead.npz  bench_flash_latency.make_paths(...)["ours_torch"] (bench_flash_latency.py:126-133),
                     the reference's unfused PyTorch path with per-KV-head proxies
+  metric_l0.npz     layer 0 of the reference's shipped static query metric
+                    (assets/llama-3.1-8b-instruct.query_metric.triu.pt, Apache-2.0), in its packed form
   decode_*.npz      methods_eager.Ours build + decode steps (inference/methods_eager.py:505-654) with the
                     attention stage of OursUnfused (:671-685): post-build state, and per step the
                     selected / expanded indices, ErrorGate scores, quotas, proxies and outputs
@@ -84,9 +87,18 @@ def golden_flash_kvhead(bfl):
     return dict(out=npc(out.view(BQ, D).float()))
 
 
+def golden_metric_l0(ref_root):
+    """Layer 0 of the reference's shipped static-metric asset, kept in its packed (upper-triangle) form."""
+    d = torch.load(os.path.join(ref_root, "assets", "llama-3.1-8b-instruct.query_metric.triu.pt"), map_location="cpu",
+                   weights_only=False)
+    return dict(M_triu=npc(d["M_triu"][:1]), dim=np.array(d["dim"]), inv_freq=npc(d["inv_freq"]),
+                attention_scaling=np.array(float(d.get("attention_scaling", 1.0))),
+                source=np.array(f"{d.get('source')} ({d.get('n_requests')} requests), layer 0 of 32"))
+
+
 def golden_decode(bl, name, metric_path):
     x = cases.decode_inputs(name)
-    torch.save({"M": x["M"], "inv_freq": llama31_inv_freq(), "attention_scaling": 1.0}, metric_path)
+    torch.save({"M": x["M"], "inv_freq": x["inv_freq"], "attention_scaling": 1.0}, metric_path)
     bl.NL = 1
     bl.DEPLOYED[0.05] = (192, 1335)
     B, n0, Lmax = x["B"], x["n0"], x["Lmax"]
@@ -153,7 +165,9 @@ def main():
     torch.save({"M": torch.zeros(1, HQ, D, D), "inv_freq": llama31_inv_freq(), "attention_scaling": 1.0},
                metric_path)
     bl, bfl = import_reference(a.reference, metric_path)
-    jobs = {"flash_qhead": lambda: golden_flash_qhead(bl), "flash_kvhead": lambda: golden_flash_kvhead(bfl)}
+    # the metric fixture first: the decode case that uses the real asset reads it through cases.py
+    jobs = {"metric_l0": lambda: golden_metric_l0(a.reference), "flash_qhead": lambda: golden_flash_qhead(bl),
+            "flash_kvhead": lambda: golden_flash_kvhead(bfl)}
     for name in cases.DECODE_CASES:
         jobs[name] = (lambda nm: (lambda: golden_decode(bl, nm, metric_path)))(name)
     for name, fn in jobs.items():

@@ -18,6 +18,7 @@ from helpers import state_from_fixture, to_gpu_state, to_np
 from openattention_b200 import flash as F
 from openattention_b200 import method as Mth
 from openattention_b200 import selection as S
+from openattention_b200 import synth
 from openattention_b200.geometry import HQ
 
 pytestmark = pytest.mark.gpu
@@ -35,7 +36,8 @@ def _eq(name, gpu, ref):
 
 
 def _method(B, Lmax, rho, dev="cuda"):
-    return Mth.OursB200(types.SimpleNamespace(rho=rho), B, Lmax, dev, layers=1)
+    return Mth.OursB200(types.SimpleNamespace(rho=rho, static_metric=synth.static_metric_standin(7, 1)), B, Lmax, dev,
+                        layers=1)
 
 
 @pytest.mark.parametrize("name", list(cases.DECODE_CASES))
@@ -181,9 +183,93 @@ def test_build_bit_exact(name, golden_dir):
     _eq("clen", g["clen"], st_np["clen"])
     for k in ("Sk", "Sk2", "Sv"):
         _eq(k, g[k], st_np[k])
-    # the reference's own codes and scale (same basis) are reproduced exactly
+    # the reference's own codes, scale, cluster assignments and counts (same basis) are reproduced exactly
     _eq("codes_vs_reference", g["codes"][:, :, :n0], z["codes"][:, :, :n0])
     _eq("scale_vs_reference", g["scale"], z["scale"].reshape(B, 8, 32))
+    _eq("asg_vs_reference", g["asg"][:, :, :n0], z["asg"].astype(np.int32))
+    _eq("nb_vs_reference", g["nb"], z["nb"])
+
+
+@pytest.mark.parametrize("name", list(cases.DECODE_CASES))
+def test_build_from_metric_matches_reference(name, golden_dir):
+    """The whole build through the method API (OursB200.build: query metric on the GPU, host eigh, the
+    build kernels) from the case's static metric -- for decode_real_l0 layer 0 of the reference's own
+    asset, handed over in its packed form -- reproduces the reference's bases, codes, scale, cluster
+    assignments and counts bit for bit, and the oracle's centroids and column means."""
+    x = cases.decode_inputs(name)
+    z = np.load(os.path.join(golden_dir, f"{name}.npz"))
+    B, n0, Lmax, rho = x["B"], x["n0"], x["Lmax"], x["rho"]
+    metric = cases.asset_packed() if name == "decode_real_l0" else {"M": x["M"], "inv_freq": x["inv_freq"]}
+    m = Mth.OursB200(types.SimpleNamespace(rho=rho, static_metric=metric), B, Lmax, "cuda", layers=1)
+    Mth.C.K, Mth.C.V, Mth.C.qlen = [x["K"].cuda()], [x["V"].cuda()], [cases.QLEN] * B
+    for b in range(B):
+        m.build(0, b, x["qpre"][b].cuda(), n0)
+    torch.cuda.synchronize()
+    g = m.st[0]
+    _eq("U", g["U"], z["U"])
+    _eq("W", g["W"], z["W"])
+    _eq("codes", g["codes"][:, :, :n0], z["codes"][:, :, :n0])
+    _eq("scale", g["scale"], z["scale"].reshape(B, 8, 32))
+    _eq("asg", g["asg"][:, :, :n0], z["asg"].astype(np.int32))
+    _eq("nb", g["nb"], z["nb"])
+    st_np = O.new_state(B, Lmax, m.C)
+    K, V = O.bits(x["K"]), O.bits(x["V"])
+    for b in range(B):
+        O.build_from_basis(st_np, b, K[b], V[b], z["U"][b], z["W"][b], n0, layer=0)
+    for k in ("colmean", "cent", "mem", "cstart", "clen", "Sk", "Sk2", "Sv"):
+        _eq(k, g[k] if k not in ("mem",) else g[k][:, :, :n0], st_np[k] if k != "mem" else st_np[k][:, :, :n0])
+
+
+def test_decode_c2_bit_exact():
+    """The benchmark configuration itself (c2: B = 32 requests, 32K-token caches, 1% read) for three decode
+    steps against the oracle: every request built on the GPU (the build is checked against the oracle
+    above), the state copied into the oracle, then selected and expanded indices, quotas and tail counts
+    bit-exact, and the deployed fused output within 2e-3 max-abs / 1e-3 relative-L2 of the fp32
+    estimator."""
+    dev = torch.device("cuda")
+    B, n0, steps, rho = 32, 32768, 3, 0.01
+    Lmax = n0 + steps + 8
+    K, V, mus = synth.kv_torch(17, B, n0, Lmax, dev)
+    Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40] * B
+    m = _method(B, Lmax, rho)
+    C, E, R = m.C, m.E, B * HQ
+    g = torch.Generator(device=dev)
+    qpre = torch.zeros(1, HQ, n0, D, dtype=torch.bfloat16, device=dev)
+    for b in range(B):
+        g.manual_seed(5017 + b)
+        qpre[:, :, n0 - 64:] = torch.randn(1, HQ, 64, D, generator=g, device=dev).to(torch.bfloat16)
+        m.build(0, b, qpre, n0)
+    del qpre
+    Mth.C.n_dev = None
+    Mth.C.n0_dev = torch.tensor([n0], dtype=torch.int32, device=dev)
+    st_np = {k: (O.bits(v) if v.dtype == torch.bfloat16 else v.cpu().numpy()).copy() for k, v in m.st[0].items()}
+    Kn, Vn = O.bits(K).copy(), O.bits(V).copy()
+    out = torch.empty(R, D, dtype=torch.float32, device=dev)
+    g.manual_seed(9017)
+    for s in range(steps):
+        n = n0 + s + 1
+        nk, nv = synth.new_tokens_torch(20017 + s, mus, n - 1)
+        K[:, :, n - 1], V[:, :, n - 1] = nk, nv
+        Kn[:, :, n - 1], Vn[:, :, n - 1] = O.bits(nk), O.bits(nv)
+        q = torch.randn(B, HQ, 1, D, generator=g, device=dev).to(torch.bfloat16)
+        qr, sel = m.select(0, q, n, residual=False)
+        S.residual_flash(qr, K, V, m.st[0], sel, m.exp_idx, m.nt, m.quota, out, status=m.status, zdot=m.zdot)
+        torch.cuda.synchronize()
+        o = O.decode_step(st_np, O.bits(q.reshape(R, D)), Kn, Vn, n, rho, C, E)
+        _eq(f"step{s}.sel", sel, o["sel"])
+        _eq(f"step{s}.nt", m.nt, o["nt"])
+        _eq(f"step{s}.quota", m.quota, o["quota"])
+        _eq(f"step{s}.exp_idx", m.exp_idx, o["exp_idx"])
+        Skr, Svr, nr = O.residual_sums(Kn, Vn, st_np["asg"].reshape(R, -1), o["sel"], o["exp_idx"],
+                                       st_np["Sk"].reshape(R, C, D), st_np["Sv"].reshape(R, C, D), o["nt"], o["quota"])
+        est = O.estimator_fp32(O.bits(q.reshape(R, D)), Kn.reshape(B * 8, Lmax, D), Vn.reshape(B * 8, Lmax, D),
+                               o["sel"], o["exp_idx"], Skr, Svr, nr)
+        got = out.cpu().double().numpy()
+        assert np.abs(got - est).max() <= 2e-3
+        assert np.linalg.norm(got - est) <= 1e-3 * np.linalg.norm(est)
+    for k in ("codes", "asg", "nb", "Sk", "Sk2", "Sv", "reclist", "reccnt"):
+        _eq(f"state.{k}", m.st[0][k], st_np[k])
+    assert int(m.status.item()) == 0
 
 
 def test_decode_graph_replay_matches_eager():
@@ -238,7 +324,9 @@ def test_decode_graph_replay_matches_eager():
 def test_decode_with_fused_kv_append_matches_written_cache():
     """decode(l, q, n, k_new, v_new): the index update's launch writes the new token's K/V rows; the
     caches, the index state and the outputs equal those of the reference contract (rows written
-    first, then decode), over several steps."""
+    first, then decode), over several steps; and every fused step matches the oracle (selected and
+    expanded indices bit-exact, the bf16 output within 2e-3 plus one bf16 rounding of the fp32
+    estimator)."""
     from openattention_b200 import synth
     B, n0, steps, rho = 2, 2048, 3, 0.01
     Lmax = n0 + steps + 8
@@ -258,6 +346,9 @@ def test_decode_with_fused_kv_append_matches_written_cache():
         m = _method(B, Lmax, rho)
         for b in range(B):
             m.build(0, b, qpre, n0)
+        if mode == "fused":  # the oracle follows the fused path from the same built state
+            st_np = {k: to_np(v).copy() for k, v in m.st[0].items()}
+            Kn, Vn = O.bits(Kc).copy(), O.bits(Vc).copy()
         outs = []
         for s in range(steps):
             n = n0 + s + 1
@@ -272,6 +363,19 @@ def test_decode_with_fused_kv_append_matches_written_cache():
                 o = m.decode(0, q, n)
             else:
                 o = m.decode(0, q, n, k_new=kn, v_new=vn)
+                torch.cuda.synchronize()
+                Kn[:, :, n - 1], Vn[:, :, n - 1] = O.bits(kn), O.bits(vn)
+                R, C = B * HQ, m.C
+                ref = O.decode_step(st_np, O.bits(q.reshape(R, D)), Kn, Vn, n, rho, C, m.E)
+                _eq(f"fused step{s}.sel", m.last_sel, ref["sel"])
+                _eq(f"fused step{s}.exp_idx", m.exp_idx, ref["exp_idx"])
+                Skr, Svr, nr = O.residual_sums(Kn, Vn, st_np["asg"].reshape(R, -1), ref["sel"], ref["exp_idx"],
+                                               st_np["Sk"].reshape(R, C, D), st_np["Sv"].reshape(R, C, D),
+                                               ref["nt"], ref["quota"])
+                est = O.estimator_fp32(O.bits(q.reshape(R, D)), Kn.reshape(B * 8, Lmax, D),
+                                       Vn.reshape(B * 8, Lmax, D), ref["sel"], ref["exp_idx"], Skr, Svr, nr)
+                got = o.float().cpu().numpy().reshape(R, D)   # bf16 output: the estimator rounded once
+                assert np.all(np.abs(got - est) <= 2e-3 + np.abs(est) * 2.0 ** -8)
             outs.append(o.clone())
         torch.cuda.synchronize()
         res[mode] = (torch.stack(outs), Kc, Vc, {k: v.clone() for k, v in m.st[0].items()})

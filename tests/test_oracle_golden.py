@@ -159,3 +159,109 @@ def test_decode_steps_match_reference(golden_dir, name):
         ref = z[f"s{s}_out"]   # OursUnfused.attend: bf16 probabilities, bf16 matmuls
         rel = np.linalg.norm(out - ref, axis=1) / np.linalg.norm(ref, axis=1)
         assert np.median(rel) < 1.5e-2 and rel.max() < 5e-2
+
+
+# ------------------------------------------------------------------ the build against the reference
+REF_ROOT = os.environ.get("OA_REFERENCE", "/root/reference")
+
+
+def _reference_asset():
+    p = os.path.join(REF_ROOT, "assets", "llama-3.1-8b-instruct.query_metric.triu.pt")
+    if not os.path.exists(p):
+        pytest.skip("the reference checkout (its static-metric asset) is not on this machine")
+    import torch
+    return torch.load(p, map_location="cpu", weights_only=False)
+
+
+def test_metric_unpack_matches_reference_restore():
+    """method.unpack_metric on the reference's shipped asset == the reference's own restore
+    (assets/restore_query_metric.py:18-27, imported from the checkout), all 32 layers; the fixture
+    metric_l0.npz is layer 0 of that asset."""
+    import importlib.util
+    import torch
+    from openattention_b200 import method as Mth
+    packed = _reference_asset()
+    spec = importlib.util.spec_from_file_location("restore_query_metric",
+                                                  os.path.join(REF_ROOT, "assets", "restore_query_metric.py"))
+    rq = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(rq)
+    want = rq.unpack(packed)["M"]
+    got = Mth.unpack_metric(packed)
+    assert got.shape == (32, 32, 128, 128) and torch.equal(got, want)
+    fx = cases.asset_packed()
+    assert torch.equal(fx["M_triu"], packed["M_triu"][:1]) and torch.equal(fx["inv_freq"], packed["inv_freq"])
+
+
+def test_load_static_metric_forms_and_missing():
+    """The loader reads the packed and the unpacked asset form to the same M, and raises without a metric."""
+    import types
+    import torch
+    from openattention_b200 import method as Mth
+    packed = cases.asset_packed()
+    M1, inv1, s1 = Mth.load_static_metric(types.SimpleNamespace(static_metric=packed), 1)
+    M2, inv2, s2 = Mth.load_static_metric(types.SimpleNamespace(static_metric={"M": M1, "inv_freq": inv1}), 1)
+    assert torch.equal(M1, M2) and torch.equal(inv1, inv2) and s1 == s2 == 1.0
+    assert torch.equal(M1, M1.transpose(-1, -2))
+    old = os.environ.pop("OA_STATIC_M", None)
+    try:
+        with pytest.raises(RuntimeError, match="no static query metric"):
+            Mth.load_static_metric(types.SimpleNamespace(), 1)
+        with pytest.raises(RuntimeError, match="holds 1 layers"):
+            Mth.load_static_metric(types.SimpleNamespace(static_metric=packed), 2)
+    finally:
+        if old is not None:
+            os.environ["OA_STATIC_M"] = old
+
+
+@pytest.mark.parametrize("name", list(cases.DECODE_CASES))
+def test_basis_matches_reference(golden_dir, name):
+    """The product's query metric (static metric rotated to the decode window + question rows) and its
+    eigen-bases equal the reference's U (QGS) and W (QGC) bit for bit (inference/methods_eager.py:510-528);
+    decode_real_l0 uses layer 0 of the reference's own asset."""
+    from openattention_b200 import method as Mth
+    x = cases.decode_inputs(name)
+    z = _load(golden_dir, name)
+    for b in range(x["B"]):
+        M = Mth.query_metric(x["M"][0], x["inv_freq"], 1.0, x["qpre"][b], x["n0"], cases.QLEN)
+        U, W = Mth.basis_from_host_metric(M.float())
+        assert np.array_equal(U.numpy(), z["U"][b]), f"U[{b}]"
+        assert np.array_equal(O.bits(W), z["W"][b]), f"W[{b}]"
+
+
+@pytest.mark.parametrize("name", list(cases.DECODE_CASES))
+def test_kmeans_matches_reference(golden_dir, name):
+    """The oracle's QGC projection and 4 Lloyd iterations (the GPU build equals the oracle bit for bit,
+    tests/test_decode_gpu.py) from the reference's W reproduce the reference's cluster assignments and
+    member counts exactly.  Centroids and column means differ only by the projection's rounding: the
+    reference's projection is a bf16 matmul whose fp32 accumulation order is the library's, so a
+    projected coordinate can differ by one bf16 ulp (2^-7 relative) where the exact sum sits near a
+    rounding boundary; a mean of such values moves by at most one ulp of its largest member."""
+    import torch
+    x = cases.decode_inputs(name)
+    z = _load(golden_dir, name)
+    C, n0 = int(z["C"]), x["n0"]
+    K = O.bits(x["K"])
+    ulp = 2.0 ** -7
+    for b in range(x["B"]):
+        zP, colmean = O.project(K[b], z["W"][b], n0)
+        asg, cent, nb = O.kmeans(zP, O.seeds(n0, C, 0), C)
+        assert np.array_equal(asg, z["asg"][b].astype(np.int32)), f"asg[{b}]"
+        assert np.array_equal(nb, z["nb"][b]), f"nb[{b}]"
+        # the reference's own projection (methods_eager.py:530-531) evaluated here, for the bounds
+        krep = x["K"][b, :, :n0].repeat_interleave(4, 0)
+        zr = torch.matmul(krep, O.from_bits(z["W"][b])).float().numpy()          # (32, T, 16), bf16 values
+        raw = zP.astype(np.float64) + colmean[:, None, :]   # the oracle's bf16 coordinates, up to fp32 rounding
+        d = np.abs(raw - zr)
+        # fp32 accumulation error of a 128-term dot is relative to the sum of |products|, which near a
+        # zero coordinate exceeds the coordinate itself
+        mag = np.abs(krep.float().numpy()) @ np.abs(O.from_bits(z["W"][b]).float().numpy())
+        slack = 2.0 ** -23 * (np.abs(zr) + np.abs(colmean)[:, None, :]) + 2.0 ** -20 * mag
+        assert np.all(d <= ulp * np.abs(zr) + slack), "projected coordinates differ by more than one bf16 ulp"
+        print(f"{name}[{b}]: {(d > slack).mean():.2e} of the projected coordinates differ by one bf16 ulp")
+        zc = z["colmean"][b].reshape(32, 16)
+        assert np.all(np.abs(colmean - zc) <= ulp * np.abs(zr).max(1) + 1e-6), f"colmean[{b}]"
+        for h in range(32):
+            big = np.zeros(C)
+            np.maximum.at(big, asg[h], np.abs(zr[h]).max(1))
+            bound = ulp * big + ulp * np.abs(zr[h]).max() + 1e-5
+            assert np.all(np.abs(cent[h] - z["cent"][b][h]) <= bound[:, None]), f"cent[{b}, {h}]"

@@ -115,7 +115,8 @@ def test_topq_long_rows_matches_oracle(use_ws):
     Lmax = n0 + 8
     K, V, _ = synth.kv_torch(51, B, n0, Lmax, dev)
     Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40]
-    m = Mth.OursB200(types.SimpleNamespace(rho=rho), B, Lmax, dev, layers=1)
+    m = Mth.OursB200(types.SimpleNamespace(rho=rho, static_metric=synth.static_metric_standin(7, 1)), B, Lmax, dev,
+                     layers=1)
     g = torch.Generator(device=dev)
     g.manual_seed(52)
     qpre = torch.zeros(1, HQ, n0, 128, dtype=torch.bfloat16, device=dev)

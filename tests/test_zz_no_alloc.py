@@ -74,18 +74,51 @@ def test_noalloc_matches_existing_entry_two_calls(out_dtype, splits):
 
 
 def test_noalloc_rejects_split_beyond_scratch():
+    """A split whose scratch exceeds the fixed array is refused with status 1 and a message.  Every
+    buffer holds the BQ rows the call names (a few MB), so even a broken size check would only give a
+    wrong answer, never an access outside them."""
     x = _inputs(0)
-    BQ = 4096  # rows never read: the size check fails before anything is launched
+    BQ, BH = 4096, 16
+    rep = BQ // x["q"].shape[0]
+    q = x["q"].repeat(rep, 1).contiguous()
+    sel = x["sel"].repeat(rep, 1).contiguous()
+    ex = x["exp"].repeat(rep, 1).contiguous()
+    ln = x["log_n"].repeat(rep, 1).contiguous()
+    kb = x["kbar"].repeat(rep, 1, 1).contiguous()
+    vb = x["vbar"].repeat(rep, 1, 1).contiguous()
+    k = x["k"][:BH].contiguous()
+    v = x["v"][:BH].contiguous()
     lib = _lib.load()
-    need = lib.oa_flash_workspace_bytes(BQ, x["sel"].shape[1], x["exp"].shape[1], x["kbar"].shape[1], 64)
+    need = lib.oa_flash_workspace_bytes(BQ, sel.shape[1], ex.shape[1], kb.shape[1], 64)
     assert need > SCRATCH_LIMIT
+    out = torch.full((BQ, 128), 7.0, dtype=torch.float32, device=q.device)
+    status = lib.oa_flash_qhead_proxies_noalloc(
+        q.data_ptr(), q.stride(0), k.data_ptr(), v.data_ptr(), k.stride(0), k.stride(1), sel.data_ptr(),
+        sel.shape[1], ex.data_ptr(), ex.shape[1], kb.data_ptr(), vb.data_ptr(), kb.stride(0), kb.stride(1),
+        ln.data_ptr(), ln.stride(0), out.data_ptr(), out.stride(0), _lib.OA_F32, BQ, BH, k.shape[1], kb.shape[1],
+        float(F.SC), 64, torch.cuda.current_stream().cuda_stream)
+    assert status == 1
+    msg = lib.oa_last_error_string()
+    assert b"scratch" in msg and b"oa_flash_qhead_proxies_noalloc" in msg
+    torch.cuda.synchronize()
+    assert bool((out == 7.0).all()), "a rejected call must not write its output"
+
+
+def test_noalloc_argument_error_names_the_entry_point():
+    """An argument error found after the size check (BQ not a multiple of BH) is refused with status 1,
+    its message names this entry point, and nothing is launched."""
+    x = _inputs(0)
     q, k = x["q"], x["k"]
-    out = torch.empty(64, 128, dtype=torch.float32, device=q.device)
+    BQ = q.shape[0]
+    out = torch.full((BQ, 128), 7.0, dtype=torch.float32, device=q.device)
+    lib = _lib.load()
     status = lib.oa_flash_qhead_proxies_noalloc(
         q.data_ptr(), q.stride(0), k.data_ptr(), x["v"].data_ptr(), k.stride(0), k.stride(1), x["sel"].data_ptr(),
         x["sel"].shape[1], x["exp"].data_ptr(), x["exp"].shape[1], x["kbar"].data_ptr(), x["vbar"].data_ptr(),
         x["kbar"].stride(0), x["kbar"].stride(1), x["log_n"].data_ptr(), x["log_n"].stride(0), out.data_ptr(),
-        out.stride(0), _lib.OA_F32, BQ, 16, k.shape[1], x["kbar"].shape[1], float(F.SC), 64,
+        out.stride(0), _lib.OA_F32, BQ, 3, k.shape[1], x["kbar"].shape[1], float(F.SC), 4,
         torch.cuda.current_stream().cuda_stream)
     assert status == 1
-    assert b"scratch" in lib.oa_last_error_string()
+    assert b"oa_flash_qhead_proxies_noalloc" in lib.oa_last_error_string()
+    torch.cuda.synchronize()
+    assert bool((out == 7.0).all())
