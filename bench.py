@@ -46,8 +46,8 @@ B_PER_GPU, N_CTX, RHO = 32, 32768, 0.01
 VALUE_SLOTS = 4  # step graphs the `value` loop takes in turn (their inputs are staged before timing)
 SCAN_BYTES_PER_TOKEN = 32  # int8 codes per token per KV head (the scan's algorithmic bytes)
 LAUNCHES_PER_STEP = 7      # append_kv, index_update, qgs_scan, qgs_select, errorgate_waterfill, topq, residual_flash
-CLOCK_SOAK_S = 0.5         # step replays before warm-up while the clock sampler runs (state reset after)
-CLOCK_SOAK_MAX_STEPS = 4096
+CLOCK_SOAK_S = 0.3         # step replays before warm-up while the clock sampler runs (state reset after)
+CLOCK_SOAK_MAX_STEPS = 1024
 
 
 def dist_env():
