@@ -140,16 +140,22 @@ class Clocks:
 
 
 # ------------------------------------------------------------------ our arm
-def build_workload(dev, seed, steps_total, extra_positions=0):
+def build_workload(dev, seed, steps_total, extra_positions=0, B=None, kv_heads=(0, 8)):
+    """B requests (default B_PER_GPU) of the synthetic law; with kv_heads = (k0, kc) this rank keeps only
+    those KV heads of every request (and their query heads), the KV-head shard of a small batch."""
     from openattention_b200 import method as Mth
     from openattention_b200 import synth
-    from openattention_b200.geometry import HQ
-    B, n0 = B_PER_GPU, N_CTX
+    from openattention_b200.geometry import G, HQ
+    B = B_PER_GPU if B is None else B
+    n0 = N_CTX
+    k0, kc = kv_heads
     Lmax = n0 + steps_total + extra_positions + 16
     K, V, mus = synth.kv_torch(seed, B, n0, Lmax, dev)
+    if kc != 8:
+        K, V, mus = K[:, k0:k0 + kc].contiguous(), V[:, k0:k0 + kc].contiguous(), mus[:, k0:k0 + kc].contiguous()
     Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40] * B
     m = Mth.OursB200(types.SimpleNamespace(rho=RHO, static_metric=synth.static_metric_standin(7, 1)), B, Lmax, dev,
-                     layers=1)
+                     layers=1, kv_heads=(k0, kc))
     g = torch.Generator(device=dev)
     qpre = torch.empty(1, HQ, n0, 128, dtype=torch.bfloat16, device=dev)
     for b in range(B):
@@ -160,6 +166,7 @@ def build_workload(dev, seed, steps_total, extra_positions=0):
     # per-step inputs: decode queries and the new K/V rows
     g.manual_seed(seed + 9000)
     qs = torch.randn(steps_total, B, HQ, 1, 128, generator=g, device=dev).to(torch.bfloat16)
+    qs = qs[:, :, G * k0:G * (k0 + kc)].contiguous()
     nks, nvs = [], []
     for s in range(steps_total):
         nk, nv = synth.new_tokens_torch(seed + 20000 + s, mus, n0 + s)
@@ -178,9 +185,9 @@ class GraphStep:
         from openattention_b200.geometry import HQ
         B = m.B
         self.m, self.Mth = m, Mth
-        self.q_in = torch.zeros(B, HQ, 1, 128, dtype=torch.bfloat16, device=dev)
-        self.k_in = torch.zeros(B, 8, 128, dtype=torch.bfloat16, device=dev)
-        self.v_in = torch.zeros(B, 8, 128, dtype=torch.bfloat16, device=dev)
+        self.q_in = torch.zeros(B, m.hq, 1, 128, dtype=torch.bfloat16, device=dev)
+        self.k_in = torch.zeros(B, m.hkv, 128, dtype=torch.bfloat16, device=dev)
+        self.v_in = torch.zeros(B, m.hkv, 128, dtype=torch.bfloat16, device=dev)
         # position counters: new ones for a new workload (fresh), else the ones of the graphs already
         # captured for this workload, which all advance the same counters
         if fresh or getattr(Mth.C, "kv_idx", None) is None or Mth.C.n_dev is None:
@@ -189,7 +196,7 @@ class GraphStep:
             Mth.C.n0_dev = torch.full((1,), n0, dtype=torch.int32, device=dev)
         self.n_host = n0 + 1  # ns/nl/k_top are constant over the benchmark window
         self.copy_out = copy_out
-        self.out_buf = torch.empty(B, HQ, 1, 128, dtype=torch.bfloat16, device=dev) if copy_out else None
+        self.out_buf = torch.empty(B, m.hq, 1, 128, dtype=torch.bfloat16, device=dev) if copy_out else None
         snap = {k: v.clone() for k, v in m.st[0].items()}
         n_snap, kv_snap = Mth.C.n_dev.clone(), Mth.C.kv_idx.clone()
         s = torch.cuda.Stream(dev)
@@ -243,7 +250,7 @@ class StageGraphStep(GraphStep):
         st, K, V = m.st[0], C.K[0], C.V[0]
         S.append_kv(K, V, self.k_in, self.v_in, C.n_dev, offset=0, advance=True, kv_idx=C.kv_idx)
         ns, nl, k_top = step_split(self.n_host, m.a.rho, m.C, m.E)
-        qr = self.q_in.reshape(m.B * HQ, D)
+        qr = self.q_in.reshape(m.R, D)
         sel = m._sel_buf(ns + nl + k_top)
         ev = self.ev
         ev[0].record()
@@ -287,7 +294,7 @@ def stage_profile(m, Mth, gs, iters):
     from openattention_b200 import selection as S
     from openattention_b200.geometry import D, HKV, HQ, step_split
     st, B, C, E = m.st[0], m.B, m.C, m.E
-    R, Rkv = B * HQ, B * HKV
+    R, Rkv = m.R, B * m.hkv
     n = int(Mth.C.n_dev.item())
     ns, nl, k_top = step_split(gs.n_host, RHO, C, E)
     NS = ns + nl + k_top
@@ -340,7 +347,7 @@ def stage_profile(m, Mth, gs, iters):
                                                                 status=m.status, zdot=m.zdot)),
     }
     # data-dependent byte counts of this step
-    quota = m.quota.view(B, HQ, C)
+    quota = m.quota.view(B, m.hq, C)
     members = int((st["clen"].float() * (quota > 0)).sum().item())
     reads = int((m.exp_idx >= 0).sum().item()) + R * NS
     nt_tiles = (n + 31) // 32
@@ -390,8 +397,8 @@ def cpu_baseline_sample(m, Mth, qs, nks, nvs, budget_s=12.0):
         times.append(time.perf_counter() - t0)
         steps += 1
     per_req = statistics.median(times)
-    return {"value": per_req * 1e6 * B_PER_GPU, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"{steps} decode steps of 1 request (n~{N_CTX}, rho={RHO:g}), median x {B_PER_GPU} requests; "
+    return {"value": per_req * 1e6 * m.B, "unit": UNIT, "cores": threads, "kind": "port",
+            "sample": f"{steps} decode steps of 1 request (n~{N_CTX}, rho={RHO:g}), median x {m.B} requests; "
                       f"oracle/oa_oracle.c with OpenMP on {threads} threads"}
 
 
@@ -407,9 +414,19 @@ def run_ours(a):
         pg = dist
     steps_total = a.warmup + 2 * a.steps + 8
     from openattention_b200 import shard
-    # every rank runs its own B=32 requests (request sharding, shard.plan with batch = 32 * world)
-    m, Mth, qs, nks, nvs, n0, Lmax = build_workload(dev, seed=shard.request_seed(17, rank), steps_total=steps_total,
-                                                    extra_positions=CLOCK_SOAK_MAX_STEPS)
+    if a.global_batch:
+        # a fixed batch split over the ranks (strong scaling): whole requests while there are at least as
+        # many as ranks, else every rank keeps all requests and a share of the 8 KV heads (shard.plan)
+        plan = shard.plan(a.global_batch, world, rank)
+        seed = 17 if plan.kind == "kvhead" else shard.request_seed(17, plan.req_start)
+        m, Mth, qs, nks, nvs, n0, Lmax = build_workload(dev, seed=seed, steps_total=steps_total,
+                                                        extra_positions=CLOCK_SOAK_MAX_STEPS, B=plan.req_count,
+                                                        kv_heads=(plan.kv_start, plan.kv_count))
+    else:
+        # every rank runs its own B=32 requests (request sharding, weak scaling)
+        plan = None
+        m, Mth, qs, nks, nvs, n0, Lmax = build_workload(dev, seed=shard.request_seed(17, rank),
+                                                        steps_total=steps_total, extra_positions=CLOCK_SOAK_MAX_STEPS)
     gs = GraphStep(m, Mth, n0, dev)
     # `value`: VALUE_SLOTS step graphs with input buffers of their own, filled once before timing and
     # taken in turn, so the timed steps read inputs already resident in HBM (no staging copies)
@@ -472,7 +489,7 @@ def run_ours(a):
     hq = qs.cpu().pin_memory()
     hk = nks.cpu().pin_memory()
     hv = nvs.cpu().pin_memory()
-    hout = torch.empty(max(a.steps, a.warmup), B_PER_GPU, HQ, 1, 128, dtype=torch.bfloat16).pin_memory()
+    hout = torch.empty(max(a.steps, a.warmup), m.B, m.hq, 1, 128, dtype=torch.bfloat16).pin_memory()
     n_now0, kv_now0 = Mth.C.n_dev.clone(), Mth.C.kv_idx.clone()
     gsp = [GraphStep(m, Mth, n0, dev, copy_out=True, fresh=False) for _ in range(2)]
     Mth.C.n_dev.copy_(n_now0)
@@ -536,16 +553,24 @@ def run_ours(a):
     res = None
     if rank == 0:
         cpu = cpu_baseline_sample(m, Mth, qs, nks, nvs) if world == 1 else None
+        if plan is None:  # weak scaling: µs per bs32 layer-step for the whole job
+            div, scaling, gb = world, "weak", B_PER_GPU * world
+            workload = f"c2 decode-attn-stage: B={B_PER_GPU} requests/GPU"
+            par = f"request-sharded x{world} (no data-path collective)"
+        else:  # strong scaling: µs per step of the fixed batch (max over ranks)
+            div, scaling, gb = 1, "strong", a.global_batch
+            workload = f"decode-attn-stage: global batch {a.global_batch}"
+            par = (f"{plan.kind}-sharded x{world}: rank 0 holds {plan.req_count} request(s) x {plan.kv_count} KV "
+                   "head(s) (no data-path collective)")
         res = {
-            "metric": METRIC, "value": round(ms * 1e3 / world, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
-            "warmup": a.warmup, "ms_per_step": round(ms, 5), "higher_is_better": False, "scaling": "weak",
+            "metric": METRIC, "value": round(ms * 1e3 / div, 3), "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": round(ms, 5), "higher_is_better": False, "scaling": scaling,
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded clustered RoPE keys, N(0,1) values/queries)",
-            "config": {"workload": f"c2 decode-attn-stage: B={B_PER_GPU} requests/GPU, n={N_CTX}+steps, rho={RHO:g} "
-                                   f"(C={m.C}, E={m.E}), one layer step as one CUDA graph",
-                       "global_batch": B_PER_GPU * world, "seq_len": N_CTX,
-                       "parallelism": f"request-sharded x{world} (no data-path collective)",
-                       "l2": "inputs larger than L2 (int8 codes 268 MB + bf16 K/V 4.3 GB per GPU), no flush"},
-            "e2e": {"value": round(ms_e2e * 1e3 / world, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+            "config": {"workload": f"{workload}, n={N_CTX}+steps, rho={RHO:g} (C={m.C}, E={m.E}), one layer step as "
+                                   "one CUDA graph",
+                       "global_batch": gb, "seq_len": N_CTX, "parallelism": par,
+                       "l2": "inputs larger than L2 (int8 codes 268 MB + bf16 K/V 4.3 GB per GPU at B=32), no flush"},
+            "e2e": {"value": round(ms_e2e * 1e3 / div, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": LAUNCHES_PER_STEP * a.steps,
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
@@ -653,15 +678,26 @@ def run_model_e2e(a):
     """Config c4: a random-initialised Llama-3.1-8B architecture with the OpenAttention path as its
     attention; dense prefill of a uniformly random prompt (plus the index build of every layer), then
     `--decode-steps` greedy decode steps replayed as one CUDA graph per step.  Reports ms per decode
-    step (per token of each request) and the aggregate tokens/s."""
+    step (per token of each request) and the aggregate tokens/s.
+
+    Under torchrun every rank is a batch replica (its own model copy, batch and prompt); after each step
+    the ranks' new token ids are gathered with NCCL (all_gather_into_tensor over NVLink, the only
+    collective), and the step time is the max over ranks."""
     from openattention_b200 import llama as L
-    dev = torch.device("cuda", 0)
+    from openattention_b200 import shard
+    rank, world, local = dist_env()
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=300))
     cfg = L.LlamaConfig()
     B, T, steps = B_PER_GPU, a.prompt, a.decode_steps
     model = L.RandomLlama(cfg, B, T + steps + a.warmup + 16, dev, rho=RHO, seed=1)
     g = torch.Generator(device=dev)
-    g.manual_seed(2)
+    g.manual_seed(2 + 1000 * rank)
     prompt = torch.randint(0, cfg.vocab, (B, T), generator=g, device=dev)
     model.prefill(prompt[:, :min(T, 1024)])  # warm-up: library handles, kernel selection, host buffers
     torch.cuda.synchronize()
@@ -671,25 +707,46 @@ def run_model_e2e(a):
     t_prefill = time.perf_counter() - t0
     model.start_decode(T, first)
     model.capture()
+    gathered = torch.empty(world * B, dtype=torch.long, device=dev)
+
+    def step():
+        tok = model.step_graph()
+        if dist is not None:  # every replica's new tokens, in rank order
+            dist.all_gather_into_tensor(gathered, tok)
+        return tok
+
     for _ in range(a.warmup):
-        model.step_graph()
+        step()
     torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
     for _ in range(steps):
-        model.step_graph()
+        step()
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / steps
+    ms = shard.max_over_ranks(e0.elapsed_time(e1) / steps, device=dev)
+    t_prefill = shard.max_over_ranks(t_prefill, device=dev)
+    status = int(model.method.status.item())
+    if dist is not None:
+        model.graph = None
+        torch.cuda.synchronize()
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return None
     return {"metric": "ms/token e2e (c4: random-init Llama-3.1-8B, OpenAttention 1% decode)", "value": round(ms, 4),
-            "unit": "ms/token", "n_gpus": 1, "steps": steps, "warmup": a.warmup, "higher_is_better": False,
-            "tokens_per_s": round(B * 1000.0 / ms, 1), "dtype": "bf16", "data": "synthetic (uniform random prompt)",
+            "unit": "ms/token", "n_gpus": world, "steps": steps, "warmup": a.warmup, "higher_is_better": False,
+            "tokens_per_s": round(world * B * 1000.0 / ms, 1), "dtype": "bf16",
+            "data": "synthetic (uniform random prompt)",
             "prefill_incl_build_s": round(t_prefill, 2),
             "prefill_plus_128_steps_s": round(t_prefill + 128 * ms / 1e3, 2),  # the reference's e2e-seconds measure
             "config": {"workload": "c4 end-to-end decode", "model": "Llama-3.1-8B architecture, random init",
-                       "global_batch": B, "prompt": T, "decode_steps": steps, "rho": RHO,
-                       "parallelism": "single GPU (batch replicas per GPU)"},
-            "status": int(model.method.status.item())}
+                       "global_batch": world * B, "prompt": T, "decode_steps": steps, "rho": RHO,
+                       "parallelism": (f"batch replicas x{world}, new token ids gathered by NCCL each step"
+                                       if world > 1 else "single GPU")},
+            "status": status}
 
 
 # ------------------------------------------------------------------ reference arm (CPU)
@@ -774,6 +831,9 @@ def main():
     ap.add_argument("--sweep-rho", default="", help="comma list of read fractions for --sweep (0.01, 0.03, 0.05)")
     ap.add_argument("--ctx", type=int, default=N_CTX,
                     help="context length (default 32768, the benchmark config; others only for profiling)")
+    ap.add_argument("--global-batch", type=int, default=None,
+                    help="a fixed batch split over the GPUs (strong scaling): by request, or by KV head when it is "
+                         "smaller than the GPU count (e.g. --gpus 8 --global-batch 1)")
     ap.add_argument("--batch", type=int, default=None,
                     help="requests per GPU (default 32, the benchmark config; smaller only for profiling; "
                          "--model-e2e defaults to 1, config c4)")
@@ -789,7 +849,9 @@ def main():
         run_sweep(a)
         return
     if a.model_e2e:
-        print(json.dumps(run_model_e2e(a)), flush=True)
+        res = run_model_e2e(a)
+        if res is not None:
+            print(json.dumps(res), flush=True)
         return
     res = run_reference(a) if a.impl == "reference" else run_ours(a)
     if res is not None:

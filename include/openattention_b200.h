@@ -9,7 +9,10 @@
  *
  * Fixed model geometry (Llama-3.1-8B attention): head_dim D = 128, 32 query heads, 8 KV heads
  * (G = 4 query heads per KV head), QGS rank 32, QGC rank 16.  A "row" is one (request, query head)
- * pair r = b*32 + h; its KV row is b*8 + h/4.
+ * pair; its KV row is row / 4.  Entry points that take `hkv` (1..8) work on arrays that hold hkv of
+ * each request's 8 KV heads and the 4*hkv query heads that read them (a KV-head shard of the
+ * requests; hkv = 8 is whole requests): row r = b*4*hkv + h, KV row b*hkv + h/4, and every shape
+ * below written with 8 / 32 heads has hkv / 4*hkv there.
  *
  * Dtype codes: OA_BF16 = 0, OA_F32 = 1.
  */
@@ -124,7 +127,7 @@ int oa_flash_qhead_proxies_noalloc(const void* q, int64_t q_stride, const void* 
  * +-127); per query head: nearest centroid of bf16(k.W) - colmean (ties -> lower id), asg, nb += 1,
  * Sk += k, Sk2 += k*k, Sv += v, generated-token list append (reclist may be NULL).  If q is not
  * NULL, zq (B*32, 32) bf16 = bf16((q.U) * scale) for q (B*32, 128) bf16 with row stride q_stride. */
-int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, int8_t* codes,
+int oa_index_update(const void* K, const void* V, int64_t B, int64_t hkv, int64_t Lmax, int64_t C, int8_t* codes,
                     const float* U, const float* scale, const void* W, const float* colmean, const float* cent,
                     int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv, int32_t* reclist, int32_t* reccnt,
                     int rmax, const void* q, int64_t q_stride, void* zq, const int32_t* n_dev, void* stream);
@@ -134,7 +137,8 @@ int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64
  * graph_runner.py:479-480, then runs _k_index_update_d2, ours_graph.py:43-90): k_new, v_new (B, 8, 128)
  * bf16 contiguous are the new token's rows; they are written into K, V at position n_dev[0] - 1 and
  * the index is updated from them, in one launch.  Other arguments as oa_index_update. */
-int oa_index_update_append(void* K, void* V, int64_t B, int64_t Lmax, int64_t C, const void* k_new, const void* v_new,
+int oa_index_update_append(void* K, void* V, int64_t B, int64_t hkv, int64_t Lmax, int64_t C, const void* k_new,
+                           const void* v_new,
                            int8_t* codes, const float* U, const float* scale, const void* W, const float* colmean,
                            const float* cent, int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv,
                            int32_t* reclist, int32_t* reccnt, int rmax, const void* q, int64_t q_stride, void* zq,
@@ -147,17 +151,17 @@ int oa_index_update_append(void* K, void* V, int64_t B, int64_t Lmax, int64_t C,
  * n_dev[0] becomes n_dev[0] + 1 and, if kv_idx is not NULL, kv_idx[0] (int64) the old n_dev[0].
  * A decode step that appends before the index update uses offset 0 and advance 1; a layer loop
  * that advanced the counters already uses offset -1 and advance 0. */
-int oa_append_kv(void* K, void* V, int64_t B, int64_t Lmax, const void* k_new, const void* v_new, int32_t* n_dev,
-                 int offset, int advance, int64_t* kv_idx, void* stream);
+int oa_append_kv(void* K, void* V, int64_t B, int64_t hkv, int64_t Lmax, const void* k_new, const void* v_new,
+                 int32_t* n_dev, int offset, int advance, int64_t* kv_idx, void* stream);
 
 /* QGS scan: scores (B*32, score_stride) bf16 = exact int8 dot products of codes and zq, rounded to
  * fp32 then bf16, -inf for t < ns and t >= n - nl; tile_max (B*32, tile_max_stride) fp32 = maximum
  * of each 32-token tile (tile_max_stride >= ceil(Lmax / 32)).  Replaces _k_qgs_scan_tm (inference/graph_runner.py:100-120).
  * status (may be NULL): device int32 set to 1 if a bulk copy of the codes did not complete within
  * the kernel's bounded wait (the affected tiles are then not computed). */
-int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64_t Lmax, const int32_t* n_dev, int ns, int nl,
-                void* scores, int64_t score_stride, float* tile_max, int64_t tile_max_stride, int32_t* status,
-                void* stream);
+int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64_t hkv, int64_t Lmax, const int32_t* n_dev,
+                int ns, int nl, void* scores, int64_t score_stride, float* tile_max, int64_t tile_max_stride,
+                int32_t* status, void* stream);
 
 /* Row top-k among the 2k 32-token tiles with the largest maxima (exact), ties -> lower position;
  * sel (R, ns+nl+k_top) int32 = [0..ns-1, n-nl..n-1, top-k by rank]; the selected scores are set to
@@ -173,7 +177,8 @@ int oa_qgs_select(void* scores, int64_t score_stride, const float* tile_max, int
  * oa_residual_flash can use instead of re-reading Sk.  Replaces _k_errorgate + _k_waterfill
  * (inference/ours_fused.py:122-216).  C <= 256, n_sel <= 512.  Sk and Sk2 16-byte aligned.
  * status (may be NULL): device int32, unused by this entry (kept for a uniform stage signature). */
-int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64_t B, int64_t Lmax, int64_t C,
+int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64_t B, int64_t hkv, int64_t Lmax,
+                           int64_t C,
                            const int32_t* asg, const int32_t* sel, int64_t n_sel, const float* Sk, const float* Sk2,
                            const float* nb, float E, float* score, float* nt, float* quota, float* zdot,
                            int32_t* status, void* stream);
@@ -203,7 +208,7 @@ size_t oa_topq_workspace_bytes(int64_t R, int64_t Lmax, int64_t E);
  * log_n = ln max(n', 1) if n' > 0.5 else -inf (R, C) fp32.  Replaces _k_resid_scatter +
  * _k_resid_norm (inference/ours_fused.py:367-407), without atomics.  Quotas outside [0, E] are clamped
  * to it when the segments are placed.  status: as oa_errorgate_waterfill (value 3). */
-int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, const int32_t* asg,
+int oa_residual(const void* K, const void* V, int64_t B, int64_t hkv, int64_t Lmax, int64_t C, const int32_t* asg,
                 const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E, const float* Sk,
                 const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar, float* log_n,
                 int32_t* status, void* stream);
@@ -221,52 +226,55 @@ int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C
  * Quotas outside [0, E] are clamped to it when the segments are placed; a selected token whose
  * assignment is outside [0, C) counts as in no cluster.
  * status (may be NULL): device int32, unused by this entry. */
-int oa_residual_flash(const void* q, int64_t q_stride, const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C,
+int oa_residual_flash(const void* q, int64_t q_stride, const void* K, const void* V, int64_t B, int64_t hkv,
+                      int64_t Lmax, int64_t C,
                       const int32_t* asg, const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E,
                       const float* Sk, const float* Sv, const float* nt, const float* quota, const float* zdot,
                       void* kbar, void* vbar, float* log_n, void* out, int64_t out_stride, int out_dtype,
                       float sm_scale, int32_t* status, void* stream);
 
 /* ------------------------------------------------------------------------------------------------
- * Per-request build (prefill).  Each call works on ONE request: K, V (8, Lmax, 128) bf16 with the
- * first T positions valid; state pointers address that request's slice ((8, ...) for QGS arrays,
- * (32, ...) for QGC arrays).  Replaces methods_eager.Ours.build (inference/methods_eager.py:519-555)
+ * Per-request build (prefill).  Each call works on ONE request: K, V (hkv, Lmax, 128) bf16 with the
+ * first T positions valid; state pointers address that request's slice ((hkv, ...) for QGS arrays,
+ * (4*hkv, ...) for QGC arrays; hkv = 8 is the whole request).  Replaces methods_eager.Ours.build (inference/methods_eager.py:519-555)
  * and the fast build (inference/ours_fastbuild.py:253-304); the eigen-decomposition and the k-means
  * seeds stay on the host (torch), as in the reference.
  * ----------------------------------------------------------------------------------------------*/
 
 /* QGS codes: z = k.U (8, T, 32), scale = max(amax_t |z| / 127, 1e-12) (8, 32), codes (8, Lmax, 32)
  * = clamp(rint(z / scale), +-127).  amax_ws: 256 uint32 of scratch. */
-int oa_build_codes(const void* K, int64_t Lmax, int64_t T, const float* U, float* scale, int8_t* codes,
+int oa_build_codes(const void* K, int64_t hkv, int64_t Lmax, int64_t T, const float* U, float* scale, int8_t* codes,
                    uint32_t* amax_ws, void* stream);
 
 /* QGC projection: zP (32, T, 16) fp32 = bf16(k . W[h]) - colmean, colmean (32, 16) = column means
  * (double accumulation per 256-token tile, then over tiles).  W (32, 128, 16) bf16. */
 size_t oa_build_project_workspace_bytes(int64_t T);
-int oa_build_project(const void* K, int64_t Lmax, int64_t T, const void* W, float* zP, float* colmean,
+int oa_build_project(const void* K, int64_t hkv, int64_t Lmax, int64_t T, const void* W, float* zP, float* colmean,
                      void* workspace, size_t workspace_bytes, void* stream);
 
 /* One Lloyd assignment for the 32 query heads: asg[h, t] = argmax_c bf16(bf16(bf16(zP).bf16(cent_c))
  * - bf16(|cent_c|^2 / 2)), ties -> lower c (inference/ours_fastbuild.py:52-82). */
-int oa_kmeans_assign(const float* zP, int64_t T, int64_t C, const float* cent, int32_t* asg, int64_t asg_stride,
-                     void* stream);
+int oa_kmeans_assign(const float* zP, int64_t hkv, int64_t T, int64_t C, const float* cent, int32_t* asg,
+                     int64_t asg_stride, void* stream);
 
 /* Stable CSR member lists of an assignment: mem[h, cstart[h,c] + i] = i-th position (ascending) with
  * asg == c; clen = counts (inference/ours_fused.py:436-445).  mem (32, mem_stride) int32. */
 size_t oa_csr_workspace_bytes(int64_t T, int64_t C);
-int oa_csr_build(const int32_t* asg, int64_t asg_stride, int64_t T, int64_t C, int32_t* mem, int64_t mem_stride,
-                 int32_t* cstart, int32_t* clen, void* workspace, size_t workspace_bytes, void* stream);
+int oa_csr_build(const int32_t* asg, int64_t asg_stride, int64_t hkv, int64_t T, int64_t C, int32_t* mem,
+                 int64_t mem_stride, int32_t* cstart, int32_t* clen, void* workspace, size_t workspace_bytes,
+                 void* stream);
 
 /* Lloyd update: cent_c = (sum of member zP, in position order, fp32) / count, an empty cluster takes
  * zP[init_c]; nb = counts (inference/methods_eager.py:543-545). init: (C,) int64 seed positions. */
-int oa_kmeans_update(const float* zP, int64_t T, int64_t C, const int32_t* mem, int64_t mem_stride,
+int oa_kmeans_update(const float* zP, int64_t hkv, int64_t T, int64_t C, const int32_t* mem, int64_t mem_stride,
                      const int32_t* cstart, const int32_t* clen, const int64_t* init, float* cent, float* nb,
                      void* stream);
 
 /* Cluster sums Sk, Sk2, Sv (32, C, 128) fp32 over the members in position order
  * (inference/ours_fastbuild.py:111-139; = the scatter_add sums of methods_eager.py:549-555). */
-int oa_cluster_sums(const void* K, const void* V, int64_t Lmax, int64_t C, const int32_t* mem, int64_t mem_stride,
-                    const int32_t* cstart, const int32_t* clen, float* Sk, float* Sk2, float* Sv, void* stream);
+int oa_cluster_sums(const void* K, const void* V, int64_t hkv, int64_t Lmax, int64_t C, const int32_t* mem,
+                    int64_t mem_stride, const int32_t* cstart, const int32_t* clen, float* Sk, float* Sk2, float* Sv,
+                    void* stream);
 
 #ifdef __cplusplus
 }

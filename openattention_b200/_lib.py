@@ -30,26 +30,27 @@ SIGNATURES = {
                                      I32, I64, I64, I64, I64, F32, I32, P, SZ, P]),
     "oa_flash_qhead_proxies_noalloc": (I32, [P, I64, P, P, I64, I64, P, I64, P, I64, P, P, I64, I64, P, I64, P,
                                              I64, I32, I64, I64, I64, I64, F32, I32, P]),
-    "oa_index_update": (I32, [P, P, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, P, I64, P, P, P]),
-    "oa_append_kv": (I32, [P, P, I64, I64, P, P, P, I32, I32, P, P]),
-    "oa_index_update_append": (I32, [P, P, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, P,
-                                     I64, P, P, P]),
-    "oa_qgs_scan": (I32, [P, P, I64, I64, P, I32, I32, P, I64, P, I64, P, P]),
+    "oa_index_update": (I32, [P, P, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, I32, P, I64, P, P,
+                              P]),
+    "oa_append_kv": (I32, [P, P, I64, I64, I64, P, P, P, I32, I32, P, P]),
+    "oa_index_update_append": (I32, [P, P, I64, I64, I64, I64, P, P, P, P, P, P, P, P, P, P, P, P, P, P, P, I32,
+                                     P, I64, P, P, P]),
+    "oa_qgs_scan": (I32, [P, P, I64, I64, I64, P, I32, I32, P, I64, P, I64, P, P]),
     "oa_qgs_select": (I32, [P, I64, P, I64, I64, I64, P, I32, I32, I32, P, P]),
-    "oa_errorgate_waterfill": (I32, [P, I64, P, I64, I64, I64, P, P, I64, P, P, P, F32, P, P, P, P, P, P]),
+    "oa_errorgate_waterfill": (I32, [P, I64, P, I64, I64, I64, I64, P, P, I64, P, P, P, F32, P, P, P, P, P, P]),
     "oa_topq": (I32, [P, I64, I64, I64, I64, P, P, P, P, P, P, I32, P, I64, P, P, P, P, P, SZ, P]),
     "oa_topq_workspace_bytes": (SZ, [I64, I64, I64]),
-    "oa_residual": (I32, [P, P, I64, I64, I64, P, P, I64, P, I64, P, P, P, P, P, P, P, P, P]),
-    "oa_residual_flash": (I32, [P, I64, P, P, I64, I64, I64, P, P, I64, P, I64, P, P, P, P, P, P, P, P, P, I64,
-                                I32, F32, P, P]),
-    "oa_build_codes": (I32, [P, I64, I64, P, P, P, P, P]),
+    "oa_residual": (I32, [P, P, I64, I64, I64, I64, P, P, I64, P, I64, P, P, P, P, P, P, P, P, P]),
+    "oa_residual_flash": (I32, [P, I64, P, P, I64, I64, I64, I64, P, P, I64, P, I64, P, P, P, P, P, P, P, P, P,
+                                I64, I32, F32, P, P]),
+    "oa_build_codes": (I32, [P, I64, I64, I64, P, P, P, P, P]),
     "oa_build_project_workspace_bytes": (SZ, [I64]),
-    "oa_build_project": (I32, [P, I64, I64, P, P, P, P, SZ, P]),
-    "oa_kmeans_assign": (I32, [P, I64, I64, P, P, I64, P]),
+    "oa_build_project": (I32, [P, I64, I64, I64, P, P, P, P, SZ, P]),
+    "oa_kmeans_assign": (I32, [P, I64, I64, I64, P, P, I64, P]),
     "oa_csr_workspace_bytes": (SZ, [I64, I64]),
-    "oa_csr_build": (I32, [P, I64, I64, I64, P, I64, P, P, P, SZ, P]),
-    "oa_kmeans_update": (I32, [P, I64, I64, P, I64, P, P, P, P, P, P]),
-    "oa_cluster_sums": (I32, [P, P, I64, I64, P, I64, P, P, P, P, P, P]),
+    "oa_csr_build": (I32, [P, I64, I64, I64, I64, P, I64, P, P, P, SZ, P]),
+    "oa_kmeans_update": (I32, [P, I64, I64, I64, P, I64, P, P, P, P, P, P]),
+    "oa_cluster_sums": (I32, [P, P, I64, I64, I64, P, I64, P, P, P, P, P, P]),
 }
 
 _lock = threading.Lock()

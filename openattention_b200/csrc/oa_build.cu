@@ -70,9 +70,9 @@ __global__ void __launch_bounds__(kBT) build_codes_kernel(const __nv_bfloat16* K
   }
 }
 
-__global__ void build_scale_kernel(const uint32_t* amax, float* scale) {
+__global__ void build_scale_kernel(const uint32_t* amax, float* scale, int n) {
   const int i = threadIdx.x + blockIdx.x * blockDim.x;
-  if (i < kHKV * kRQ) scale[i] = fmaxf(__fdiv_rn(__uint_as_float(amax[i]), 127.f), 1e-12f);
+  if (i < n) scale[i] = fmaxf(__fdiv_rn(__uint_as_float(amax[i]), 127.f), 1e-12f);
 }
 
 // ---------------------------------------------------------------- QGC projection
@@ -115,18 +115,18 @@ __global__ void __launch_bounds__(kBT) project_kernel(const __nv_bfloat16* K, in
   }
 }
 
-__global__ void colmean_kernel(const double* part, int ntiles, int T, float* colmean) {
+__global__ void colmean_kernel(const double* part, int ntiles, int T, float* colmean, int nq) {
   const int i = threadIdx.x + blockIdx.x * blockDim.x;  // h * 16 + c
-  if (i >= kHQ * kRC) return;
+  if (i >= nq * kRC) return;
   const int h = i / kRC, c = i % kRC;
   double s = 0.0;
   for (int tl = 0; tl < ntiles; ++tl) s = __dadd_rn(s, part[((int64_t)h * ntiles + tl) * kRC + c]);
   colmean[i] = __double2float_rn(__ddiv_rn(s, (double)T));
 }
 
-__global__ void center_kernel(float* zP, int T, const float* colmean) {
+__global__ void center_kernel(float* zP, int T, const float* colmean, int nq) {
   const int64_t i = threadIdx.x + (int64_t)blockIdx.x * blockDim.x;
-  if (i >= (int64_t)kHQ * T * kRC) return;
+  if (i >= (int64_t)nq * T * kRC) return;
   const int c = (int)(i % kRC);
   const int h = (int)(i / ((int64_t)T * kRC));
   zP[i] = __fsub_rn(zP[i], colmean[h * kRC + c]);
@@ -257,10 +257,10 @@ __global__ void kmeans_update_kernel(const float* zP, int T, int C, const int32_
 __global__ void __launch_bounds__(128) cluster_sums_kernel(const __nv_bfloat16* K, const __nv_bfloat16* V, int Lmax,
                                                            int C, const int32_t* mem, int64_t mem_stride,
                                                            const int32_t* cstart, const int32_t* clen, float* Sk,
-                                                           float* Sk2, float* Sv) {
+                                                           float* Sk2, float* Sv, int nq) {
   const int lane = threadIdx.x & 31;
   const int gw = blockIdx.x * 4 + (threadIdx.x >> 5);  // h * C + i
-  if (gw >= kHQ * C) return;
+  if (gw >= nq * C) return;
   const int h = gw / C, i = gw % C;
   const int st = cstart[h * C + i], len = clen[h * C + i];
   const int32_t* mp = mem + (int64_t)h * mem_stride + st;
@@ -294,18 +294,21 @@ inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
 
 using namespace oa;
 
-extern "C" int oa_build_codes(const void* K, int64_t Lmax, int64_t T, const float* U, float* scale, int8_t* codes,
-                              uint32_t* amax_ws, void* stream) {
+// hkv (1..8): the KV heads of the request this call builds (a shard of its 8 holds a subset; their query
+// heads are the 4 hkv that read them).  Every array argument covers those heads only.
+extern "C" int oa_build_codes(const void* K, int64_t hkv, int64_t Lmax, int64_t T, const float* U, float* scale,
+                              int8_t* codes, uint32_t* amax_ws, void* stream) {
   const char* fn = "oa_build_codes";
+  OA_REQUIRE_HKV(fn, hkv);
   OA_REQUIRE(T > 0 && T <= Lmax && Lmax < (1ll << 30), "%s: need 0 < T <= Lmax", fn);
   OA_REQUIRE(K && U && scale && codes && amax_ws, "%s: null pointer", fn);
   OA_REQUIRE(oa_aligned16(K) && oa_aligned16(codes), "%s: K and codes must be 16-byte aligned", fn);
-  cudaError_t e = cudaMemsetAsync(amax_ws, 0, sizeof(uint32_t) * kHKV * kRQ, S(stream));
+  cudaError_t e = cudaMemsetAsync(amax_ws, 0, sizeof(uint32_t) * hkv * kRQ, S(stream));
   if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: %s", fn, cudaGetErrorString(e));
-  dim3 grid((unsigned)((T + kBT - 1) / kBT), kHKV);
+  dim3 grid((unsigned)((T + kBT - 1) / kBT), (unsigned)hkv);
   const __nv_bfloat16* Kb = static_cast<const __nv_bfloat16*>(K);
   build_codes_kernel<false><<<grid, kBT, 0, S(stream)>>>(Kb, (int)Lmax, (int)T, U, amax_ws, nullptr, nullptr);
-  build_scale_kernel<<<1, kHKV * kRQ, 0, S(stream)>>>(amax_ws, scale);
+  build_scale_kernel<<<1, kHKV * kRQ, 0, S(stream)>>>(amax_ws, scale, (int)(hkv * kRQ));
   build_codes_kernel<true><<<grid, kBT, 0, S(stream)>>>(Kb, (int)Lmax, (int)T, U, nullptr, scale, codes);
   return oa_check_launch(fn);
 }
@@ -314,31 +317,34 @@ extern "C" size_t oa_build_project_workspace_bytes(int64_t T) {
   return sizeof(double) * kHQ * kRC * (size_t)((T + kBT - 1) / kBT);
 }
 
-extern "C" int oa_build_project(const void* K, int64_t Lmax, int64_t T, const void* W, float* zP, float* colmean,
-                                void* workspace, size_t workspace_bytes, void* stream) {
+extern "C" int oa_build_project(const void* K, int64_t hkv, int64_t Lmax, int64_t T, const void* W, float* zP,
+                                float* colmean, void* workspace, size_t workspace_bytes, void* stream) {
   const char* fn = "oa_build_project";
+  OA_REQUIRE_HKV(fn, hkv);
+  const int nq = (int)(kG * hkv);
   OA_REQUIRE(T > 0 && T <= Lmax && Lmax < (1ll << 30), "%s: need 0 < T <= Lmax", fn);
   OA_REQUIRE(K && W && zP && colmean && workspace, "%s: null pointer", fn);
   OA_REQUIRE(oa_aligned16(K) && oa_aligned16(workspace), "%s: K and workspace must be 16-byte aligned", fn);
   const int ntiles = (int)((T + kBT - 1) / kBT);
   OA_REQUIRE(workspace_bytes >= oa_build_project_workspace_bytes(T), "%s: workspace too small", fn);
   double* part = static_cast<double*>(workspace);
-  project_kernel<<<dim3(ntiles, kHQ), kBT, 0, S(stream)>>>(static_cast<const __nv_bfloat16*>(K), (int)Lmax, (int)T,
-                                                          static_cast<const __nv_bfloat16*>(W), zP, part);
-  colmean_kernel<<<1, kHQ * kRC, 0, S(stream)>>>(part, ntiles, (int)T, colmean);
-  const int64_t total = (int64_t)kHQ * T * kRC;
-  center_kernel<<<(unsigned)((total + 255) / 256), 256, 0, S(stream)>>>(zP, (int)T, colmean);
+  project_kernel<<<dim3(ntiles, nq), kBT, 0, S(stream)>>>(static_cast<const __nv_bfloat16*>(K), (int)Lmax, (int)T,
+                                                         static_cast<const __nv_bfloat16*>(W), zP, part);
+  colmean_kernel<<<1, kHQ * kRC, 0, S(stream)>>>(part, ntiles, (int)T, colmean, nq);
+  const int64_t total = (int64_t)nq * T * kRC;
+  center_kernel<<<(unsigned)((total + 255) / 256), 256, 0, S(stream)>>>(zP, (int)T, colmean, nq);
   return oa_check_launch(fn);
 }
 
-extern "C" int oa_kmeans_assign(const float* zP, int64_t T, int64_t C, const float* cent, int32_t* asg,
+extern "C" int oa_kmeans_assign(const float* zP, int64_t hkv, int64_t T, int64_t C, const float* cent, int32_t* asg,
                                 int64_t asg_stride, void* stream) {
   const char* fn = "oa_kmeans_assign";
+  OA_REQUIRE_HKV(fn, hkv);
   OA_REQUIRE(T > 0 && C > 0 && C <= 1024 && asg_stride >= T, "%s: bad sizes", fn);
   OA_REQUIRE(zP && cent && asg && oa_aligned16(zP), "%s: null or misaligned pointer", fn);
   const size_t smem = sizeof(float) * (size_t)C * (kRC + 1);
   if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(kmeans_assign_kernel), smem, fn)) return rc;
-  kmeans_assign_kernel<<<dim3((unsigned)((T + kBT - 1) / kBT), kHQ), kBT, smem, S(stream)>>>(
+  kmeans_assign_kernel<<<dim3((unsigned)((T + kBT - 1) / kBT), (unsigned)(kG * hkv)), kBT, smem, S(stream)>>>(
       zP, (int)T, (int)C, cent, asg, asg_stride);
   return oa_check_launch(fn);
 }
@@ -347,41 +353,46 @@ extern "C" size_t oa_csr_workspace_bytes(int64_t T, int64_t C) {
   return sizeof(int32_t) * kHQ * (size_t)C * (size_t)((T + kBT - 1) / kBT);
 }
 
-extern "C" int oa_csr_build(const int32_t* asg, int64_t asg_stride, int64_t T, int64_t C, int32_t* mem,
+extern "C" int oa_csr_build(const int32_t* asg, int64_t asg_stride, int64_t hkv, int64_t T, int64_t C, int32_t* mem,
                             int64_t mem_stride, int32_t* cstart, int32_t* clen, void* workspace,
                             size_t workspace_bytes, void* stream) {
   const char* fn = "oa_csr_build";
+  OA_REQUIRE_HKV(fn, hkv);
+  const unsigned nq = (unsigned)(kG * hkv);
   OA_REQUIRE(T > 0 && C > 0 && C <= 1024 && asg_stride >= T && mem_stride >= T, "%s: bad sizes", fn);
   OA_REQUIRE(asg && mem && cstart && clen && workspace, "%s: null pointer", fn);
   OA_REQUIRE(workspace_bytes >= oa_csr_workspace_bytes(T, C), "%s: workspace too small", fn);
   const int ntiles = (int)((T + kBT - 1) / kBT);
   int32_t* tilecnt = static_cast<int32_t*>(workspace);
-  csr_count_kernel<<<dim3(ntiles, kHQ), kBT, sizeof(int) * C, S(stream)>>>(asg, asg_stride, (int)T, (int)C, tilecnt);
-  csr_offsets_kernel<<<kHQ, 256, 0, S(stream)>>>(tilecnt, ntiles, (int)C, cstart, clen);
-  csr_place_kernel<<<dim3(ntiles, kHQ), kBT, 0, S(stream)>>>(asg, asg_stride, (int)T, (int)C, tilecnt, cstart, mem,
-                                                            mem_stride);
+  csr_count_kernel<<<dim3(ntiles, nq), kBT, sizeof(int) * C, S(stream)>>>(asg, asg_stride, (int)T, (int)C, tilecnt);
+  csr_offsets_kernel<<<nq, 256, 0, S(stream)>>>(tilecnt, ntiles, (int)C, cstart, clen);
+  csr_place_kernel<<<dim3(ntiles, nq), kBT, 0, S(stream)>>>(asg, asg_stride, (int)T, (int)C, tilecnt, cstart, mem,
+                                                           mem_stride);
   return oa_check_launch(fn);
 }
 
-extern "C" int oa_kmeans_update(const float* zP, int64_t T, int64_t C, const int32_t* mem, int64_t mem_stride,
-                                const int32_t* cstart, const int32_t* clen, const int64_t* init, float* cent,
-                                float* nb, void* stream) {
+extern "C" int oa_kmeans_update(const float* zP, int64_t hkv, int64_t T, int64_t C, const int32_t* mem,
+                                int64_t mem_stride, const int32_t* cstart, const int32_t* clen, const int64_t* init,
+                                float* cent, float* nb, void* stream) {
   const char* fn = "oa_kmeans_update";
+  OA_REQUIRE_HKV(fn, hkv);
   OA_REQUIRE(T > 0 && C > 0 && C <= 1024, "%s: bad sizes", fn);
   OA_REQUIRE(zP && mem && cstart && clen && init && cent && nb, "%s: null pointer", fn);
-  kmeans_update_kernel<<<dim3((unsigned)((C * kRC + 127) / 128), kHQ), 128, 0, S(stream)>>>(
+  kmeans_update_kernel<<<dim3((unsigned)((C * kRC + 127) / 128), (unsigned)(kG * hkv)), 128, 0, S(stream)>>>(
       zP, (int)T, (int)C, mem, mem_stride, cstart, clen, init, cent, nb);
   return oa_check_launch(fn);
 }
 
-extern "C" int oa_cluster_sums(const void* K, const void* V, int64_t Lmax, int64_t C, const int32_t* mem,
+extern "C" int oa_cluster_sums(const void* K, const void* V, int64_t hkv, int64_t Lmax, int64_t C, const int32_t* mem,
                                int64_t mem_stride, const int32_t* cstart, const int32_t* clen, float* Sk, float* Sk2,
                                float* Sv, void* stream) {
   const char* fn = "oa_cluster_sums";
+  OA_REQUIRE_HKV(fn, hkv);
+  const int nq = (int)(kG * hkv);
   OA_REQUIRE(Lmax > 0 && C > 0 && C <= 1024, "%s: bad sizes", fn);
   OA_REQUIRE(K && V && mem && cstart && clen && Sk && Sk2 && Sv, "%s: null pointer", fn);
-  cluster_sums_kernel<<<(unsigned)((kHQ * C + 3) / 4), 128, 0, S(stream)>>>(
+  cluster_sums_kernel<<<(unsigned)((nq * C + 3) / 4), 128, 0, S(stream)>>>(
       static_cast<const __nv_bfloat16*>(K), static_cast<const __nv_bfloat16*>(V), (int)Lmax, (int)C, mem, mem_stride,
-      cstart, clen, Sk, Sk2, Sv);
+      cstart, clen, Sk, Sk2, Sv, nq);
   return oa_check_launch(fn);
 }

@@ -120,3 +120,8 @@ int oa_smem_opt_in(const void* kernel, size_t dyn, const char* what, bool max_ca
   } while (0)
 
 static inline bool oa_aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// hkv: KV heads per request held by this call's arrays (8 = whole requests; fewer = a KV-head shard of
+// each request, whose query heads are the 4 hkv that read those KV heads)
+#define OA_REQUIRE_HKV(fn, hkv) \
+  OA_REQUIRE((hkv) >= 1 && (hkv) <= oa::kHKV, "%s: hkv=%lld outside [1, %d]", fn, (long long)(hkv), oa::kHKV)

@@ -1917,12 +1917,14 @@ size_t proxy_flash_smem(int NT, int C) {
 
 using namespace oa;
 
-extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64_t B, int64_t Lmax,
-                                      int64_t C, const int32_t* asg, const int32_t* sel, int64_t n_sel,
+extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const void* K, int64_t B, int64_t hkv,
+                                      int64_t Lmax, int64_t C, const int32_t* asg, const int32_t* sel, int64_t n_sel,
                                       const float* Sk, const float* Sk2, const float* nb, float E, float* score,
                                       float* nt, float* quota, float* zdot, int32_t* status, void* stream) {
   const char* fn = "oa_errorgate_waterfill";
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= kMaxC, "%s: need 0 < C <= %d (C=%lld)", fn, kMaxC, (long long)C);
+  OA_REQUIRE_HKV(fn, hkv);
+  const int64_t R = B * kG * hkv;
   OA_REQUIRE(n_sel > 0 && n_sel <= 512, "%s: n_sel=%lld outside [1, 512]", fn, (long long)n_sel);
   OA_REQUIRE(q && K && asg && sel && Sk && Sk2 && nb && score && nt && quota, "%s: null pointer", fn);
   OA_REQUIRE(E >= 0.f, "%s: negative budget", fn);
@@ -1935,13 +1937,13 @@ extern "C" int oa_errorgate_waterfill(const void* q, int64_t q_stride, const voi
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  if (B * kHQ <= 2 * sms) {
+  if (R <= 2 * sms) {
     if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(errorgate_waterfill_kernel<256>), smem, fn)) return rc;
-    errorgate_waterfill_kernel<256><<<(unsigned)(B * kHQ), 256, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    errorgate_waterfill_kernel<256><<<(unsigned)R, 256, smem, static_cast<cudaStream_t>(stream)>>>(a);
   } else {
     if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(errorgate_waterfill_kernel<kEgThreads>), smem, fn))
       return rc;
-    errorgate_waterfill_kernel<kEgThreads><<<(unsigned)(B * kHQ), kEgThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    errorgate_waterfill_kernel<kEgThreads><<<(unsigned)R, kEgThreads, smem, static_cast<cudaStream_t>(stream)>>>(a);
   }
   return oa_check_launch(fn);
 }
@@ -2022,12 +2024,14 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
   return oa_check_launch(fn);
 }
 
-extern "C" int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, const int32_t* asg,
+extern "C" int oa_residual(const void* K, const void* V, int64_t B, int64_t hkv, int64_t Lmax, int64_t C,
+                           const int32_t* asg,
                            const int32_t* sel, int64_t n_sel, const int32_t* exp_idx, int64_t E, const float* Sk,
                            const float* Sv, const float* nt, const float* quota, void* kbar, void* vbar, float* logn,
                            int32_t* status, void* stream) {
   const char* fn = "oa_residual";
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
+  OA_REQUIRE_HKV(fn, hkv);
   OA_REQUIRE(n_sel > 0 && n_sel + E <= kMaxRead, "%s: need 0 < n_sel and n_sel + E <= %d", fn, kMaxRead);
   OA_REQUIRE(K && V && asg && sel && exp_idx && Sk && Sv && nt && quota && kbar && vbar && logn, "%s: null pointer",
              fn);
@@ -2035,17 +2039,18 @@ extern "C" int oa_residual(const void* K, const void* V, int64_t B, int64_t Lmax
   ResidArgs a{nullptr, 0, static_cast<const __nv_bfloat16*>(K), static_cast<const __nv_bfloat16*>(V), (int)Lmax,
               (int)C, (int)n_sel, (int)E, asg, sel, exp_idx, Sk, Sv, nt, quota, nullptr, static_cast<__nv_bfloat16*>(kbar),
               static_cast<__nv_bfloat16*>(vbar), logn, nullptr, 0, 0, 0.f, status};
-  residual_kernel<false><<<(unsigned)(B * kHQ), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  residual_kernel<false><<<(unsigned)(B * kG * hkv), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }
 
-extern "C" int oa_residual_flash(const void* q, int64_t q_stride, const void* K, const void* V, int64_t B, int64_t Lmax,
-                                 int64_t C, const int32_t* asg, const int32_t* sel, int64_t n_sel,
+extern "C" int oa_residual_flash(const void* q, int64_t q_stride, const void* K, const void* V, int64_t B, int64_t hkv,
+                                 int64_t Lmax, int64_t C, const int32_t* asg, const int32_t* sel, int64_t n_sel,
                                  const int32_t* exp_idx, int64_t E, const float* Sk, const float* Sv, const float* nt,
                                  const float* quota, const float* zdot, void* kbar, void* vbar, float* logn, void* out,
                                  int64_t out_stride, int out_dtype, float sm_scale, int32_t* status, void* stream) {
   const char* fn = "oa_residual_flash";
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= kMaxC && E > 0, "%s: bad sizes", fn);
+  OA_REQUIRE_HKV(fn, hkv);
   OA_REQUIRE(n_sel > 0 && n_sel + E <= kMaxRead, "%s: need 0 < n_sel and n_sel + E <= %d", fn, kMaxRead);
   OA_REQUIRE(q && K && V && asg && sel && exp_idx && Sk && Sv && nt && quota && out, "%s: null pointer", fn);
   OA_REQUIRE((kbar == nullptr) == (vbar == nullptr), "%s: kbar and vbar are given together", fn);
@@ -2060,9 +2065,9 @@ extern "C" int oa_residual_flash(const void* q, int64_t q_stride, const void* K,
     OA_REQUIRE(oa_aligned16(Sk) && oa_aligned16(Sv), "%s: Sk / Sv must be 16-byte aligned", fn);
     const size_t smem = proxy_flash_smem((int)(n_sel + E), (int)C);
     if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(proxy_flash_kernel), smem, fn)) return rc;
-    proxy_flash_kernel<<<(unsigned)(B * kHQ), kPF, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    proxy_flash_kernel<<<(unsigned)(B * kG * hkv), kPF, smem, static_cast<cudaStream_t>(stream)>>>(a);
   } else {
-    residual_kernel<true><<<(unsigned)(B * kHQ), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+    residual_kernel<true><<<(unsigned)(B * kG * hkv), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
   }
   return oa_check_launch(fn);
 }

@@ -614,13 +614,14 @@ __global__ void __launch_bounds__(kApThreads) append_kv_kernel(__nv_bfloat16* K,
 using namespace oa;
 
 namespace {
-int index_update_entry(const char* fn, void* K, void* V, int64_t B, int64_t Lmax, int64_t C, int8_t* codes,
+int index_update_entry(const char* fn, void* K, void* V, int64_t B, int64_t hkv, int64_t Lmax, int64_t C, int8_t* codes,
                        const float* U, const float* scale, const void* W, const float* colmean, const float* cent,
                        int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv, int32_t* reclist, int32_t* reccnt,
                        int rmax, const void* q, int64_t q_stride, void* zq, const int32_t* n_dev, const void* k_new,
                        const void* v_new, void* stream) {
   OA_REQUIRE(B > 0 && Lmax > 0 && C > 0 && C <= 4096, "%s: bad sizes B=%lld Lmax=%lld C=%lld", fn, (long long)B,
              (long long)Lmax, (long long)C);
+  OA_REQUIRE_HKV(fn, hkv);
   OA_REQUIRE(Lmax < (1ll << 31) / 1, "%s: Lmax too large", fn);
   OA_REQUIRE(K && V && codes && U && scale && W && colmean && cent && asg && nb && Sk && Sk2 && Sv && n_dev,
              "%s: null pointer", fn);
@@ -634,22 +635,24 @@ int index_update_entry(const char* fn, void* K, void* V, int64_t B, int64_t Lmax
   const size_t smem = (size_t)std::min<int64_t>(C, kIuCentCache) * kRC * sizeof(float);
   OA_REQUIRE(oa_aligned16(cent) && oa_aligned16(U) && oa_aligned16(W), "%s: U / W / cent must be 16-byte aligned", fn);
   if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(index_update_kernel), smem, fn, true)) return rc;
-  index_update_kernel<<<(unsigned)(B * kHQ), 128, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  index_update_kernel<<<(unsigned)(B * kG * hkv), 128, smem, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }
 }  // namespace
 
-extern "C" int oa_index_update(const void* K, const void* V, int64_t B, int64_t Lmax, int64_t C, int8_t* codes,
+extern "C" int oa_index_update(const void* K, const void* V, int64_t B, int64_t hkv, int64_t Lmax, int64_t C,
+                               int8_t* codes,
                                const float* U, const float* scale, const void* W, const float* colmean,
                                const float* cent, int32_t* asg, float* nb, float* Sk, float* Sk2, float* Sv,
                                int32_t* reclist, int32_t* reccnt, int rmax, const void* q, int64_t q_stride,
                                void* zq, const int32_t* n_dev, void* stream) {
-  return index_update_entry("oa_index_update", const_cast<void*>(K), const_cast<void*>(V), B, Lmax, C, codes, U,
+  return index_update_entry("oa_index_update", const_cast<void*>(K), const_cast<void*>(V), B, hkv, Lmax, C, codes, U,
                             scale, W, colmean, cent, asg, nb, Sk, Sk2, Sv, reclist, reccnt, rmax, q, q_stride, zq,
                             n_dev, nullptr, nullptr, stream);
 }
 
-extern "C" int oa_index_update_append(void* K, void* V, int64_t B, int64_t Lmax, int64_t C, const void* k_new,
+extern "C" int oa_index_update_append(void* K, void* V, int64_t B, int64_t hkv, int64_t Lmax, int64_t C,
+                                      const void* k_new,
                                       const void* v_new, int8_t* codes, const float* U, const float* scale,
                                       const void* W, const float* colmean, const float* cent, int32_t* asg, float* nb,
                                       float* Sk, float* Sk2, float* Sv, int32_t* reclist, int32_t* reccnt, int rmax,
@@ -657,28 +660,30 @@ extern "C" int oa_index_update_append(void* K, void* V, int64_t B, int64_t Lmax,
                                       void* stream) {
   const char* fn = "oa_index_update_append";
   OA_REQUIRE(k_new && v_new, "%s: null k_new / v_new", fn);
-  return index_update_entry(fn, K, V, B, Lmax, C, codes, U, scale, W, colmean, cent, asg, nb, Sk, Sk2, Sv, reclist,
+  return index_update_entry(fn, K, V, B, hkv, Lmax, C, codes, U, scale, W, colmean, cent, asg, nb, Sk, Sk2, Sv, reclist,
                             reccnt, rmax, q, q_stride, zq, n_dev, k_new, v_new, stream);
 }
 
-extern "C" int oa_append_kv(void* K, void* V, int64_t B, int64_t Lmax, const void* k_new, const void* v_new,
-                            int32_t* n_dev, int offset, int advance, int64_t* kv_idx, void* stream) {
+extern "C" int oa_append_kv(void* K, void* V, int64_t B, int64_t hkv, int64_t Lmax, const void* k_new,
+                            const void* v_new, int32_t* n_dev, int offset, int advance, int64_t* kv_idx, void* stream) {
   const char* fn = "oa_append_kv";
+  OA_REQUIRE_HKV(fn, hkv);
   OA_REQUIRE(B > 0 && Lmax > 0 && Lmax < (1ll << 31) && B * kHKV * kD / 8 * 2 < (1ll << 31), "%s: bad sizes", fn);
   OA_REQUIRE(K && V && k_new && v_new && n_dev, "%s: null pointer", fn);
   OA_REQUIRE(oa_aligned16(K) && oa_aligned16(V) && oa_aligned16(k_new) && oa_aligned16(v_new),
              "%s: K, V, k_new and v_new must be 16-byte aligned", fn);
   append_kv_kernel<<<1, kApThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      static_cast<__nv_bfloat16*>(K), static_cast<__nv_bfloat16*>(V), (int)(B * kHKV), (int)Lmax,
+      static_cast<__nv_bfloat16*>(K), static_cast<__nv_bfloat16*>(V), (int)(B * hkv), (int)Lmax,
       static_cast<const __nv_bfloat16*>(k_new), static_cast<const __nv_bfloat16*>(v_new), n_dev, offset,
       advance ? 1 : 0, kv_idx);
   return oa_check_launch(fn);
 }
 
-extern "C" int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64_t Lmax, const int32_t* n_dev, int ns,
-                           int nl, void* scores, int64_t score_stride, float* tile_max, int64_t tile_max_stride,
-                           int32_t* status, void* stream) {
+extern "C" int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64_t hkv, int64_t Lmax,
+                           const int32_t* n_dev, int ns, int nl, void* scores, int64_t score_stride, float* tile_max,
+                           int64_t tile_max_stride, int32_t* status, void* stream) {
   const char* fn = "oa_qgs_scan";
+  OA_REQUIRE_HKV(fn, hkv);
   OA_REQUIRE(B > 0 && Lmax > 0 && Lmax < (1ll << 30), "%s: bad sizes", fn);
   OA_REQUIRE(codes && zq && n_dev && scores && tile_max, "%s: null pointer", fn);
   OA_REQUIRE(oa_aligned16(codes), "%s: codes must be 16-byte aligned", fn);
@@ -689,7 +694,7 @@ extern "C" int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64
   ScanArgs a{codes, static_cast<const __nv_bfloat16*>(zq), n_dev, ns, nl, (int)Lmax, NT,
              static_cast<uint16_t*>(scores), score_stride, tile_max, tile_max_stride, status};
   const int nsteps = (int)((Lmax + kTile - 1) / kTile);
-  dim3 grid((unsigned)(B * kHKV), (unsigned)((nsteps + kTilesPerCta - 1) / kTilesPerCta));
+  dim3 grid((unsigned)(B * hkv), (unsigned)((nsteps + kTilesPerCta - 1) / kTilesPerCta));
   qgs_scan_kernel<<<grid, kScanThreads, 0, static_cast<cudaStream_t>(stream)>>>(a);
   return oa_check_launch(fn);
 }

@@ -122,8 +122,9 @@ def basis_from_metric(M: torch.Tensor):
 
 
 def basis_from_host_metric(Mh: torch.Tensor):
-    """basis_from_metric on a host copy of M (32, D, D) fp32; returns host tensors."""
-    _, Ukv = torch.linalg.eigh(Mh.view(HKV, G, D, D).mean(1))
+    """basis_from_metric on a host copy of M (4 hkv, D, D) fp32 (32 heads, or a KV-head shard's query heads);
+    returns host tensors U (hkv, D, 32) and W (4 hkv, D, 16)."""
+    _, Ukv = torch.linalg.eigh(Mh.view(-1, G, D, D).mean(1))
     ev, Uq = torch.linalg.eigh(Mh)
     U = Ukv[..., -RQ:].contiguous()
     W = (Uq[..., -RC:] * ev[..., -RC:].clamp(min=0).sqrt().unsqueeze(-2)).to(torch.bfloat16).contiguous()
@@ -197,22 +198,29 @@ class OursB200:
     FUSED = True
     keep_proxies = False
 
-    def __init__(self, a, B, Lmax, dev, layers: int | None = None):
+    def __init__(self, a, B, Lmax, dev, layers: int | None = None, kv_heads: tuple[int, int] | None = None):
+        """kv_heads = (k0, kc): this instance holds KV heads k0 .. k0+kc-1 of every request (a KV-head shard:
+        caches C.K[l] / C.V[l] are (B, kc, Lmax, 128), decode queries (B, 4 kc, 1, 128) for query heads
+        4 k0 .. 4 (k0+kc) - 1); default all 8."""
         self.a, self.B, self.Lmax = a, B, Lmax
         self.dev = torch.device(dev)
         if self.dev.type != "cuda":
             raise RuntimeError("OursB200 runs on CUDA devices only (no CPU fallback)")
         _lib.load()
-        self.R = B * HQ
+        k0, kc = kv_heads if kv_heads is not None else getattr(a, "kv_heads", None) or (0, HKV)
+        if not (0 <= k0 and 1 <= kc and k0 + kc <= HKV):
+            raise RuntimeError(f"kv_heads {(k0, kc)} is not a range of the {HKV} KV heads")
+        self.k0, self.hkv, self.hq = k0, kc, G * kc
+        self.R = B * self.hq
         self.C, self.E = budget(a.rho)
         self.NL = layers or getattr(a, "layers", None) or NL
         Mpre, inv_freq, scaling = load_static_metric(a, self.NL)
         # the metric is evaluated on the host, in the reference's CPU arithmetic (see build_async)
-        self.Mpre = Mpre.cpu()
+        self.Mpre = Mpre.cpu()[:, G * k0:G * (k0 + kc)].contiguous()  # this shard's query heads
         self.inv_freq = inv_freq.cpu()
         self.scaling = scaling
         self._mst = {}  # layer -> (T, static metric rotated to T): shared by the requests of one prefill length
-        self.st = [S.new_state(B, Lmax, self.C, self.dev, RMAX) for _ in range(self.NL)]
+        self.st = [S.new_state(B, Lmax, self.C, self.dev, RMAX, hkv=kc) for _ in range(self.NL)]
         R, Cn, E, dev = self.R, self.C, self.E, self.dev
         self.NT = (Lmax + 31) // 32          # 32-token tiles of the QGS tile maxima
         self.SW = S.padded_len(Lmax)
@@ -243,7 +251,8 @@ class OursB200:
     # ---------------------------------------------------------------- build (prefill)
     def build(self, l, b, q, T):
         """Index of layer l, batch row b after the prefill wrote C.K[l][b, :, :T], C.V[l][b, :, :T];
-        q: (1, 32, T, D) prefill queries (the last C.qlen[b] rows are the question)."""
+        q: (1, 32, T, D) prefill queries (the last C.qlen[b] rows are the question); a KV-head shard takes
+        either all 32 query heads or its own 4 kc."""
         self.build_async(l, b, q, T)()
 
     def build_async(self, l, b, q, T):
@@ -257,6 +266,10 @@ class OursB200:
         evaluation would round its fp32 matmuls differently and perturb the eigenvectors."""
         Qn = C.qlen[b] if C.qlen else 40
         pi = question_rows(Qn)
+        if q.shape[1] == HQ and self.hq != HQ:
+            q = q[:, G * self.k0:G * self.k0 + self.hq]
+        if q.shape[1] != self.hq:
+            raise RuntimeError(f"prefill queries hold {q.shape[1]} heads; this instance builds {self.hq}")
         rows = q[0, :, T - Qn:, :].index_select(1, pi.pin_memory().to(q.device, non_blocking=True))
         rows_h = torch.empty(rows.shape, dtype=rows.dtype, pin_memory=True)
         rows_h.copy_(rows, non_blocking=True)
@@ -284,24 +297,25 @@ class OursB200:
         st["U"][b].copy_(U)
         st["W"][b].copy_(W)
         lib = _lib.load()
-        amax = torch.empty(HKV * RQ, dtype=torch.int32, device=dev)
-        _lib.call("oa_build_codes", p(K1), Lmax, T, p(st["U"][b]), p(st["scale"][b]), p(st["codes"][b]), p(amax),
+        hkv = self.hkv
+        amax = torch.empty(hkv * RQ, dtype=torch.int32, device=dev)
+        _lib.call("oa_build_codes", p(K1), hkv, Lmax, T, p(st["U"][b]), p(st["scale"][b]), p(st["codes"][b]), p(amax),
                   stream)
-        zP = torch.empty(HQ, T, RC, device=dev)
+        zP = torch.empty(self.hq, T, RC, device=dev)
         ws = torch.empty(max(lib.oa_build_project_workspace_bytes(T), lib.oa_csr_workspace_bytes(T, Cn)),
                          dtype=torch.uint8, device=dev)
-        _lib.call("oa_build_project", p(K1), Lmax, T, p(st["W"][b]), p(zP), p(st["colmean"][b]), p(ws), ws.numel(),
-                  stream)
+        _lib.call("oa_build_project", p(K1), hkv, Lmax, T, p(st["W"][b]), p(zP), p(st["colmean"][b]), p(ws),
+                  ws.numel(), stream)
         init = kmeans_seeds(T, Cn, l).to(dev)
         cent = st["cent"][b]
         cent.copy_(zP.index_select(1, init))
         for _ in range(ITERS):
-            _lib.call("oa_kmeans_assign", p(zP), T, Cn, p(cent), p(st["asg"][b]), Lmax, stream)
-            _lib.call("oa_csr_build", p(st["asg"][b]), Lmax, T, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]),
+            _lib.call("oa_kmeans_assign", p(zP), hkv, T, Cn, p(cent), p(st["asg"][b]), Lmax, stream)
+            _lib.call("oa_csr_build", p(st["asg"][b]), Lmax, hkv, T, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]),
                       p(st["clen"][b]), p(ws), ws.numel(), stream)
-            _lib.call("oa_kmeans_update", p(zP), T, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]), p(st["clen"][b]),
-                      p(init), p(cent), p(st["nb"][b]), stream)
-        _lib.call("oa_cluster_sums", p(K1), p(V1), Lmax, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]),
+            _lib.call("oa_kmeans_update", p(zP), hkv, T, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]),
+                      p(st["clen"][b]), p(init), p(cent), p(st["nb"][b]), stream)
+        _lib.call("oa_cluster_sums", p(K1), p(V1), hkv, Lmax, Cn, p(st["mem"][b]), Lmax, p(st["cstart"][b]),
                   p(st["clen"][b]), p(st["Sk"][b]), p(st["Sk2"][b]), p(st["Sv"][b]), stream)
         if "reccnt" in st:
             st["reccnt"][b].zero_()
@@ -353,7 +367,7 @@ class OursB200:
         S.residual_flash(qr, C.K[l], C.V[l], self.st[l], sel, self.exp_idx, self.nt, self.quota, self.out,
                          kbar=self.kbar if keep else None, vbar=self.vbar if keep else None,
                          logn=self.logn if keep else None, status=self.status, zdot=self.zdot)
-        return self.out.view(self.B, HQ, 1, D)
+        return self.out.view(self.B, self.hq, 1, D)
 
     def attend(self, l, qr, sel, exp_idx, kbar_r, vbar_r, logn):
         """OpenAttention.flash with per-query-head proxies, called through the module attribute
@@ -361,7 +375,7 @@ class OursB200:
         Lmax = self.Lmax
         out = flash_mod.ours_flash(qr, C.K[l].view(-1, Lmax, D), C.V[l].view(-1, Lmax, D), sel, exp_idx, kbar_r,
                                    vbar_r, logn, out=self.out, workspace=self.flash_ws)
-        return out.view(self.B, HQ, 1, D)
+        return out.view(self.B, self.hq, 1, D)
 
 
 METHODS = {"ours3": OursB200, "ours": OursB200}

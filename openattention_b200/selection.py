@@ -1,12 +1,16 @@
 """Torch-tensor wrappers over the C-ABI selection stages (one call = one kernel launch on the current
 stream).  Shapes follow the state layout of include/openattention_b200.h; all tensors must be CUDA,
-contiguous and of the stated dtype (checked here, so the C side only sees valid layouts)."""
+contiguous and of the stated dtype (checked here, so the C side only sees valid layouts).
+
+A KV-head shard of the requests (hkv of their 8 KV heads, and the 4 hkv query heads that read them) uses
+the same wrappers: the caches are (B, hkv, Lmax, 128), the per-query-head state (B, 4 hkv, ...), and
+hkv is read from the cache shape."""
 from __future__ import annotations
 
 import torch
 
 from . import _lib
-from .geometry import D, HKV, HQ, RC, RQ
+from .geometry import D, G, HKV, RC, RQ
 
 _ptr = _lib.ptr
 
@@ -45,34 +49,42 @@ def _rows(name, t, dtype, R, cols=None):
                            f"last dim, got {tuple(t.shape)} {t.dtype}")
 
 
+def _heads(K):
+    """(B, hkv, Lmax) of a cache (B, hkv, Lmax, 128): hkv KV heads per request (8, or a shard's subset)."""
+    B, hkv, Lmax, _ = K.shape
+    if not 1 <= hkv <= HKV:
+        raise RuntimeError(f"K holds {hkv} KV heads per request; 1..{HKV} are supported")
+    return B, hkv, Lmax
+
+
 def append_kv(K, V, k_new, v_new, n_dev, offset=0, advance=True, kv_idx=None):
-    """Writes the new token's K/V rows (B, 8, 128) at position n_dev + offset of the caches (B, 8, Lmax,
+    """Writes the new token's K/V rows (B, hkv, 128) at position n_dev + offset of the caches (B, hkv, Lmax,
     128) in one launch; with advance, n_dev += 1 and kv_idx (int64, optional) = the old n_dev."""
-    B, _, Lmax, _ = K.shape
-    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
-    _need("V", V, torch.bfloat16, (B, HKV, Lmax, D))
-    _need("k_new", k_new, torch.bfloat16, (B, HKV, D))
-    _need("v_new", v_new, torch.bfloat16, (B, HKV, D))
+    B, hkv, Lmax = _heads(K)
+    _need("K", K, torch.bfloat16, (B, hkv, Lmax, D))
+    _need("V", V, torch.bfloat16, (B, hkv, Lmax, D))
+    _need("k_new", k_new, torch.bfloat16, (B, hkv, D))
+    _need("v_new", v_new, torch.bfloat16, (B, hkv, D))
     _need("n_dev", n_dev, torch.int32, (1,))
     if kv_idx is not None:
         _need("kv_idx", kv_idx, torch.int64, (1,))
     _on(K.device, ("V", V), ("k_new", k_new), ("v_new", v_new), ("n_dev", n_dev), ("kv_idx", kv_idx))
-    _lib.call("oa_append_kv", _ptr(K), _ptr(V), B, Lmax, _ptr(k_new), _ptr(v_new), _ptr(n_dev), int(offset),
+    _lib.call("oa_append_kv", _ptr(K), _ptr(V), B, hkv, Lmax, _ptr(k_new), _ptr(v_new), _ptr(n_dev), int(offset),
               1 if advance else 0, _ptr(kv_idx), _stream(K))
 
 
 def index_update(K, V, st, n_dev, q=None, zq=None, k_new=None, v_new=None):
-    """New token at n-1 joins the index; with q (B*32, D) also writes zq (B*32, 32) bf16.  With k_new,
-    v_new (B, 8, 128) the token's rows are written into K, V at n-1 by the same launch."""
-    B, _, Lmax, _ = K.shape
+    """New token at n-1 joins the index; with q (B*4*hkv, D) also writes zq (B*4*hkv, 32) bf16.  With
+    k_new, v_new (B, hkv, 128) the token's rows are written into K, V at n-1 by the same launch."""
+    B, hkv, Lmax = _heads(K)
     C = st["nb"].shape[-1]
-    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
-    _need("V", V, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("K", K, torch.bfloat16, (B, hkv, Lmax, D))
+    _need("V", V, torch.bfloat16, (B, hkv, Lmax, D))
     _need("n_dev", n_dev, torch.int32, (1,))
     if q is not None:
-        if q.dtype != torch.bfloat16 or q.stride(-1) != 1 or q.shape != (B * HQ, D):
-            raise RuntimeError("q must be (B*32, 128) bf16 with a contiguous last dim")
-        _need("zq", zq, torch.bfloat16, (B * HQ, RQ))
+        if q.dtype != torch.bfloat16 or q.stride(-1) != 1 or q.shape != (B * G * hkv, D):
+            raise RuntimeError(f"q must be ({B * G * hkv}, 128) bf16 with a contiguous last dim")
+        _need("zq", zq, torch.bfloat16, (B * G * hkv, RQ))
     _on(K.device, ("V", V), ("n_dev", n_dev), ("q", q), ("zq", zq), ("k_new", k_new), ("v_new", v_new))
     _state_on(K.device, st)
     rec = st.get("reclist")
@@ -81,21 +93,21 @@ def index_update(K, V, st, n_dev, q=None, zq=None, k_new=None, v_new=None):
             _ptr(st["asg"]), _ptr(st["nb"]), _ptr(st["Sk"]), _ptr(st["Sk2"]), _ptr(st["Sv"]), _ptr(rec),
             _ptr(st.get("reccnt")), rmax, _ptr(q), 0 if q is None else q.stride(0), _ptr(zq), _ptr(n_dev), _stream(K))
     if k_new is None:
-        _lib.call("oa_index_update", _ptr(K), _ptr(V), B, Lmax, C, *tail)
+        _lib.call("oa_index_update", _ptr(K), _ptr(V), B, hkv, Lmax, C, *tail)
         return
-    _need("k_new", k_new, torch.bfloat16, (B, HKV, D))
-    _need("v_new", v_new, torch.bfloat16, (B, HKV, D))
-    _lib.call("oa_index_update_append", _ptr(K), _ptr(V), B, Lmax, C, _ptr(k_new), _ptr(v_new), *tail)
+    _need("k_new", k_new, torch.bfloat16, (B, hkv, D))
+    _need("v_new", v_new, torch.bfloat16, (B, hkv, D))
+    _lib.call("oa_index_update_append", _ptr(K), _ptr(V), B, hkv, Lmax, C, _ptr(k_new), _ptr(v_new), *tail)
 
 
 def qgs_scan(codes, zq, n_dev, ns, nl, scores, tile_max, status=None):
-    B, _, Lmax, _ = codes.shape
+    B, hkv, Lmax = _heads(codes)
     _need("codes", codes, torch.int8)
-    _need("zq", zq, torch.bfloat16, (B * HQ, RQ))
+    _need("zq", zq, torch.bfloat16, (B * G * hkv, RQ))
     if scores.dtype != torch.bfloat16 or tile_max.dtype != torch.float32 or scores.stride(1) != 1:
         raise RuntimeError("scores must be bf16 (R, >= Lmax) and tile_max fp32 (R, >= NT)")
     _on(codes.device, ("zq", zq), ("n_dev", n_dev), ("scores", scores), ("tile_max", tile_max), ("status", status))
-    _lib.call("oa_qgs_scan", _ptr(codes), _ptr(zq), B, Lmax, _ptr(n_dev), int(ns), int(nl), _ptr(scores),
+    _lib.call("oa_qgs_scan", _ptr(codes), _ptr(zq), B, hkv, Lmax, _ptr(n_dev), int(ns), int(nl), _ptr(scores),
               scores.stride(0), _ptr(tile_max), tile_max.stride(0), _ptr(status), _stream(codes))
 
 
@@ -111,18 +123,18 @@ def qgs_select(scores, tile_max, Lmax, n_dev, ns, nl, k_top, sel):
 
 def errorgate_waterfill(q, K, st, sel, E, score, nt, quota, status=None, zdot=None):
     """zdot (optional, (R, C) fp32): receives q . kbar of each cluster's tail mean, for residual_flash."""
-    B, _, Lmax, _ = K.shape
+    B, hkv, Lmax = _heads(K)
     C = st["nb"].shape[-1]
-    R = B * HQ
+    R = B * G * hkv
     for nm, t in (("score", score), ("nt", nt), ("quota", quota), ("zdot", zdot)):
         _need(nm, t, torch.float32, (R, C))
     _need("sel", sel, torch.int32)
-    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("K", K, torch.bfloat16, (B, hkv, Lmax, D))
     _rows("q", q, torch.bfloat16, R, D)
     _on(K.device, ("q", q), ("sel", sel), ("score", score), ("nt", nt), ("quota", quota), ("zdot", zdot),
         ("status", status))
     _state_on(K.device, st)
-    _lib.call("oa_errorgate_waterfill", _ptr(q), q.stride(0), _ptr(K), B, Lmax, C, _ptr(st["asg"]), _ptr(sel),
+    _lib.call("oa_errorgate_waterfill", _ptr(q), q.stride(0), _ptr(K), B, hkv, Lmax, C, _ptr(st["asg"]), _ptr(sel),
               sel.shape[1], _ptr(st["Sk"]), _ptr(st["Sk2"]), _ptr(st["nb"]), float(E), _ptr(score), _ptr(nt),
               _ptr(quota), _ptr(zdot), _ptr(status), _stream(K))
 
@@ -151,14 +163,14 @@ def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx, status=None, workspace=No
 
 
 def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn, status=None):
-    B, _, Lmax, _ = K.shape
+    B, hkv, Lmax = _heads(K)
     C = st["nb"].shape[-1]
-    R = B * HQ
+    R = B * G * hkv
     _need("kbar", kbar, torch.bfloat16, (R, C, D))
     _need("vbar", vbar, torch.bfloat16, (R, C, D))
     _need("logn", logn, torch.float32, (R, C))
-    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
-    _need("V", V, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("K", K, torch.bfloat16, (B, hkv, Lmax, D))
+    _need("V", V, torch.bfloat16, (B, hkv, Lmax, D))
     _need("sel", sel, torch.int32)
     _need("exp_idx", exp_idx, torch.int32)
     _need("nt", nt, torch.float32, (R, C))
@@ -166,7 +178,7 @@ def residual(K, V, st, sel, exp_idx, nt, quota, kbar, vbar, logn, status=None):
     _on(K.device, ("V", V), ("sel", sel), ("exp_idx", exp_idx), ("nt", nt), ("quota", quota), ("kbar", kbar),
         ("vbar", vbar), ("logn", logn), ("status", status))
     _state_on(K.device, st)
-    _lib.call("oa_residual", _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["asg"]), _ptr(sel), sel.shape[1], _ptr(exp_idx),
+    _lib.call("oa_residual", _ptr(K), _ptr(V), B, hkv, Lmax, C, _ptr(st["asg"]), _ptr(sel), sel.shape[1], _ptr(exp_idx),
               exp_idx.shape[1], _ptr(st["Sk"]), _ptr(st["Sv"]), _ptr(nt), _ptr(quota), _ptr(kbar), _ptr(vbar),
               _ptr(logn), _ptr(status), _stream(K))
 
@@ -175,15 +187,15 @@ def residual_flash(q, K, V, st, sel, exp_idx, nt, quota, out, kbar=None, vbar=No
                    status=None, zdot=None):
     """Residual proxies + OpenAttention.flash in one kernel; out (B*32, D) bf16 or fp32.  zdot: the
     step's errorgate_waterfill zdot output (optional; saves the Sk read)."""
-    B, _, Lmax, _ = K.shape
+    B, hkv, Lmax = _heads(K)
     C = st["nb"].shape[-1]
-    R = B * HQ
+    R = B * G * hkv
     if out.shape != (R, D) or out.stride(1) != 1 or out.dtype not in (torch.bfloat16, torch.float32):
-        raise RuntimeError("out must be (B*32, 128) bf16 or fp32 with a contiguous last dim")
+        raise RuntimeError(f"out must be ({R}, 128) bf16 or fp32 with a contiguous last dim")
     code = _lib.OA_F32 if out.dtype == torch.float32 else _lib.OA_BF16
     _need("zdot", zdot, torch.float32, (R, C))
-    _need("K", K, torch.bfloat16, (B, HKV, Lmax, D))
-    _need("V", V, torch.bfloat16, (B, HKV, Lmax, D))
+    _need("K", K, torch.bfloat16, (B, hkv, Lmax, D))
+    _need("V", V, torch.bfloat16, (B, hkv, Lmax, D))
     _rows("q", q, torch.bfloat16, R, D)
     _need("sel", sel, torch.int32)
     _need("exp_idx", exp_idx, torch.int32)
@@ -192,7 +204,7 @@ def residual_flash(q, K, V, st, sel, exp_idx, nt, quota, out, kbar=None, vbar=No
     _on(K.device, ("q", q), ("V", V), ("sel", sel), ("exp_idx", exp_idx), ("nt", nt), ("quota", quota), ("out", out),
         ("kbar", kbar), ("vbar", vbar), ("logn", logn), ("status", status), ("zdot", zdot))
     _state_on(K.device, st)
-    _lib.call("oa_residual_flash", _ptr(q), q.stride(0), _ptr(K), _ptr(V), B, Lmax, C, _ptr(st["asg"]), _ptr(sel),
+    _lib.call("oa_residual_flash", _ptr(q), q.stride(0), _ptr(K), _ptr(V), B, hkv, Lmax, C, _ptr(st["asg"]), _ptr(sel),
               sel.shape[1], _ptr(exp_idx), exp_idx.shape[1], _ptr(st["Sk"]), _ptr(st["Sv"]), _ptr(nt), _ptr(quota),
               _ptr(zdot), _ptr(kbar), _ptr(vbar), _ptr(logn), _ptr(out), out.stride(0), code, float(sm_scale),
               _ptr(status), _stream(K))
@@ -203,17 +215,19 @@ def padded_len(Lmax: int) -> int:
     return (Lmax + 255) // 256 * 256
 
 
-def new_state(B: int, Lmax: int, C: int, device, rmax: int = 256) -> dict:
+def new_state(B: int, Lmax: int, C: int, device, rmax: int = 256, hkv: int = HKV) -> dict:
     """Per-layer index state: the layout contract of methods_eager.Ours / OursG2 (int8 codes, CSR
     member lists, generated-token lists of rmax entries per cluster; rmax = 0 leaves them out, the
-    top-q stage then finds generated tokens by scanning the assignments)."""
+    top-q stage then finds generated tokens by scanning the assignments).  hkv < 8: the state of a
+    KV-head shard (hkv KV heads and their 4 hkv query heads per request)."""
     z = lambda *s, dt=torch.float32: torch.zeros(*s, device=device, dtype=dt)  # noqa: E731
-    st = dict(codes=z(B, HKV, Lmax, RQ, dt=torch.int8), U=z(B, HKV, D, RQ), scale=z(B, HKV, RQ),
-              W=z(B, HQ, D, RC, dt=torch.bfloat16), colmean=z(B, HQ, RC), cent=z(B, HQ, C, RC),
-              asg=z(B, HQ, Lmax, dt=torch.int32), nb=z(B, HQ, C), Sk=z(B, HQ, C, D), Sk2=z(B, HQ, C, D),
-              Sv=z(B, HQ, C, D), mem=z(B, HQ, Lmax, dt=torch.int32), cstart=z(B, HQ, C, dt=torch.int32),
-              clen=z(B, HQ, C, dt=torch.int32))
+    hq = G * hkv
+    st = dict(codes=z(B, hkv, Lmax, RQ, dt=torch.int8), U=z(B, hkv, D, RQ), scale=z(B, hkv, RQ),
+              W=z(B, hq, D, RC, dt=torch.bfloat16), colmean=z(B, hq, RC), cent=z(B, hq, C, RC),
+              asg=z(B, hq, Lmax, dt=torch.int32), nb=z(B, hq, C), Sk=z(B, hq, C, D), Sk2=z(B, hq, C, D),
+              Sv=z(B, hq, C, D), mem=z(B, hq, Lmax, dt=torch.int32), cstart=z(B, hq, C, dt=torch.int32),
+              clen=z(B, hq, C, dt=torch.int32))
     if rmax > 0:
-        st["reclist"] = z(B, HQ, C, rmax, dt=torch.int32)
-        st["reccnt"] = z(B, HQ, C, dt=torch.int32)
+        st["reclist"] = z(B, hq, C, rmax, dt=torch.int32)
+        st["reccnt"] = z(B, hq, C, dt=torch.int32)
     return st

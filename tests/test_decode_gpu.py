@@ -19,7 +19,7 @@ from openattention_b200 import flash as F
 from openattention_b200 import method as Mth
 from openattention_b200 import selection as S
 from openattention_b200 import synth
-from openattention_b200.geometry import HQ
+from openattention_b200.geometry import G, HQ
 
 pytestmark = pytest.mark.gpu
 D = 128
@@ -566,3 +566,59 @@ def test_proxy_flash_read_list_lengths(C, NS, E, use_zdot):
     assert np.abs(got - est).max() <= 2e-3
     assert np.linalg.norm(got - est) <= 1e-3 * np.linalg.norm(est)
     assert int(status.item()) == 0
+
+
+def test_kvhead_shards_match_whole_requests():
+    """A KV-head shard of the requests (the plan for batches smaller than the GPU count: a rank keeps some
+    KV heads and their query heads) builds and decodes exactly what the whole request does for those
+    heads: three shards of uneven size (1, 3 and 4 KV heads) against the unsharded method, state and every
+    step output bit for bit, the unsharded method itself being checked against the oracle above."""
+    from openattention_b200 import synth
+    dev = torch.device("cuda")
+    B, n0, steps, rho = 2, 2048, 2, 0.01
+    Lmax = n0 + steps + 8
+    K, V, mus = synth.kv_torch(61, B, n0, Lmax, dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(62)
+    qpre = torch.randn(B, 1, HQ, n0, D, generator=g, device=dev).to(torch.bfloat16)
+    qs = [torch.randn(B, HQ, 1, D, generator=g, device=dev).to(torch.bfloat16) for _ in range(steps)]
+    news = [synth.new_tokens_torch(700 + s, mus, n0 + s) for s in range(steps)]
+    metric = synth.static_metric_standin(7, 1)
+
+    def run(kv_heads):
+        k0, kc = kv_heads
+        Ks, Vs = K[:, k0:k0 + kc].clone(), V[:, k0:k0 + kc].clone()
+        Mth.C.K, Mth.C.V, Mth.C.qlen = [Ks], [Vs], [40] * B
+        Mth.C.n_dev = None
+        m = Mth.OursB200(types.SimpleNamespace(rho=rho, static_metric=metric), B, Lmax, dev, layers=1,
+                         kv_heads=kv_heads)
+        for b in range(B):
+            m.build(0, b, qpre[b], n0)  # all 32 query heads: the shard takes its own
+        Mth.C.n0_dev = torch.tensor([n0], dtype=torch.int32, device=dev)
+        st0 = {k: v.clone() for k, v in m.st[0].items()}
+        outs = []
+        for s in range(steps):
+            n = n0 + s + 1
+            nk, nv = news[s]
+            Ks[:, :, n - 1], Vs[:, :, n - 1] = nk[:, k0:k0 + kc], nv[:, k0:k0 + kc]
+            q = qs[s][:, G * k0:G * (k0 + kc)].contiguous()
+            o = m.decode(0, q, n)
+            torch.cuda.synchronize()
+            outs.append(dict(sel=m.last_sel.clone(), exp=m.exp_idx.clone(), quota=m.quota.clone(), out=o.clone()))
+        assert int(m.status.item()) == 0
+        return st0, outs, m
+
+    full_st, full_out, mf = run((0, 8))
+    R_req = HQ
+    for k0, kc in ((0, 1), (1, 3), (4, 4)):
+        st, outs, m = run((k0, kc))
+        for k, v in st.items():
+            per_kv = k in ("codes", "U", "scale")
+            lo, hi = (k0, k0 + kc) if per_kv else (G * k0, G * (k0 + kc))
+            assert torch.equal(v, full_st[k][:, lo:hi]), f"shard {(k0, kc)}: state {k}"
+        rows = torch.cat([torch.arange(b * R_req + G * k0, b * R_req + G * (k0 + kc)) for b in range(B)]).cuda()
+        for s, (a, f) in enumerate(zip(outs, full_out)):
+            assert torch.equal(a["sel"], f["sel"].index_select(0, rows)), f"shard {(k0, kc)} step {s}: sel"
+            assert torch.equal(a["exp"], f["exp"].index_select(0, rows)), f"shard {(k0, kc)} step {s}: exp_idx"
+            assert torch.equal(a["quota"], f["quota"].index_select(0, rows)), f"shard {(k0, kc)} step {s}: quota"
+            assert torch.equal(a["out"], f["out"][:, G * k0:G * (k0 + kc)]), f"shard {(k0, kc)} step {s}: out"
