@@ -289,23 +289,21 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
     return;
   }
   // exact limb sum l0 + l1 2^8 + l2 2^16 + l3 2^24 (|l| < 2^19) -> fp32 (one rounding) -> x 2^-S -> bf16
-  auto finish = [&](int l0, int l1, int l2, int l3, int t, float& hm) {
+  auto finish = [&](int l0, int l1, int l2, int l3) -> uint32_t {
     const long long tot = (long long)(l3 * 256 + l2) * 65536 + (long long)(l1 * 256 + l0);
     const float f0 = __ll2float_rn(tot);
     const float f = one_mul ? __fmul_rn(f0, inv2S) : scale_pow2(f0, -S_h);
-    uint16_t sb = f2bf_bits(f);
-    if (t < a.ns || t >= n - a.nl || t >= n) sb = 0xff80u;
-    if (t < a.Lmax) {
-      srow[t] = sb;
-      hm = fmaxf(hm, __uint_as_float((uint32_t)sb << 16));
-    }
+    return f2bf_bits(f);
   };
+  const int nv = min(n, a.Lmax);  // positions with a score; the rest of a touched tile is written -inf
 #pragma unroll
   for (int ti = 0; ti < kTilesPerCta; ++ti) {
     const int tile = t_begin + ti;
     const int t0 = tile * kTile;
     float hmax = -INFINITY;  // head tig, this warp's 32 tokens
     if (t0 < n && t0 < a.Lmax) {
+      // only the tiles holding sink / local positions or the end of the row test positions one by one
+      const bool edge = t0 < a.ns || t0 + kTile > nv - a.nl;
 #pragma unroll
       for (int grp = 0; grp < 2; ++grp) {
         const int lt0 = ti * kTile + warp * 32 + grp * 16;  // chunk-local first token of the 16
@@ -320,8 +318,24 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
         int d0[4], d1[4];
         mma_s8(d0, af, bf[0][0], bf[0][1]);
         mma_s8(d1, af, bf[1][0], bf[1][1]);
-        finish(d0[0], d0[1], d1[0], d1[1], ta, hmax);
-        finish(d0[2], d0[3], d1[2], d1[3], ta + 8, hmax);
+        uint32_t s0 = finish(d0[0], d0[1], d1[0], d1[1]);  // token ta
+        uint32_t s1 = finish(d0[2], d0[3], d1[2], d1[3]);  // token ta + 8
+        if (edge) {
+          if (ta < a.ns || ta >= n - a.nl || ta >= nv) s0 = 0xff80u;
+          if (ta + 8 < a.ns || ta + 8 >= n - a.nl || ta + 8 >= nv) s1 = 0xff80u;
+          if (ta < a.Lmax) srow[ta] = (uint16_t)s0;
+          if (ta + 8 < a.Lmax) srow[ta + 8] = (uint16_t)s1;
+        } else {
+          // pair tokens with the neighbouring lane (gid ^ 1, same head): even gid stores tokens
+          // (ta, ta + 1), odd gid tokens (ta + 7, ta + 8), each as one 4-byte store
+          const uint32_t mine = s0 | (s1 << 16);
+          const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 4);
+          if ((gid & 1) == 0)
+            *reinterpret_cast<uint32_t*>(srow + ta) = s0 | (other << 16);
+          else
+            *reinterpret_cast<uint32_t*>(srow + ta + 7) = (other >> 16) | (s1 << 16);
+        }
+        hmax = fmaxf(hmax, fmaxf(__uint_as_float(s0 << 16), __uint_as_float(s1 << 16)));
       }
     }
     // maximum of this warp's 32 tokens for head tig (a 32-token tile): reduce over gid
@@ -690,6 +704,7 @@ extern "C" int oa_qgs_scan(const int8_t* codes, const void* zq, int64_t B, int64
   const int NT = (int)((Lmax + kMaxTile - 1) / kMaxTile);
   OA_REQUIRE(score_stride >= Lmax && tile_max_stride >= NT, "%s: score stride %lld < Lmax or tile-max stride < %d",
              fn, (long long)score_stride, NT);
+  OA_REQUIRE(score_stride % 8 == 0 && oa_aligned16(scores), "%s: score rows must be 16-byte aligned", fn);
   OA_REQUIRE(ns >= 0 && nl >= 0, "%s: negative sink/local", fn);
   ScanArgs a{codes, static_cast<const __nv_bfloat16*>(zq), n_dev, ns, nl, (int)Lmax, NT,
              static_cast<uint16_t*>(scores), score_stride, tile_max, tile_max_stride, status};
