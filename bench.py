@@ -350,6 +350,12 @@ def stage_profile(m, Mth, gs, iters):
     quota = m.quota.view(B, m.hq, C)
     members = int((st["clen"].float() * (quota > 0)).sum().item())
     reads = int((m.exp_idx >= 0).sum().item()) + R * NS
+    # GQA-unique rows: the union of the read lists of a KV head's query heads (they share little)
+    G_ = m.hq // m.hkv
+    lists = torch.cat([sel, m.exp_idx], 1).view(B * m.hkv, G_ * (NS + E)).long()
+    lists = torch.where(lists >= 0, lists, torch.full_like(lists, -1)).sort(1).values
+    uniq = (lists[:, 1:] != lists[:, :-1]) & (lists[:, 1:] >= 0)
+    unique_reads = int(uniq.sum().item() + (lists[:, 0] >= 0).sum().item())
     nt_tiles = (n + 31) // 32
     alg = {
         "index_update_kernel": R * (D * 16 * 2 + C * 16 * 4 + 3 * D * 4 * 2 + D * 2) + Rkv * (D * 32 * 4 + 2 * D * 2),
@@ -363,7 +369,8 @@ def stage_profile(m, Mth, gs, iters):
     # per-row arrays, the index-update operands and the chosen clusters' member lists
     step_alg = (Rkv * n * 32 + 3 * R * C * D * 4 + reads * 2 * D * 2 + R * C * 4 + R * (NS + E) * 4 + 2 * R * D * 2
                 + R * (D * 16 * 2 + C * 16 * 4) + Rkv * D * 32 * 4 + members * 6)
-    return ms, alg, step_alg, n
+    unique = {"proxy_flash_kernel": alg["proxy_flash_kernel"] - (reads - unique_reads) * 2 * D * 2}
+    return ms, alg, step_alg, n, unique
 
 
 def cpu_baseline_sample(m, Mth, qs, nks, nvs, budget_s=12.0):
@@ -541,7 +548,7 @@ def run_ours(a):
     reset()
     ig_ms = in_graph_profile(m, Mth, n0, dev, qs, nks, nvs, 20)
     ig_ms = {k: max_over_ranks(v) for k, v in ig_ms.items()}
-    st_ms, st_alg, step_alg, n_now = stage_profile(m, Mth, gs, max(10, min(a.steps, 50)))
+    st_ms, st_alg, step_alg, n_now, st_unique = stage_profile(m, Mth, gs, max(10, min(a.steps, 50)))
     st_ms = {k: max_over_ranks(v) for k, v in st_ms.items()}
     peak, peak_kind = peaks()
     dom = max(ig_ms, key=ig_ms.get)
@@ -549,6 +556,9 @@ def run_ours(a):
     stages = {k: {"us": round(ig_ms[k] * 1e3, 2), "alone_us": round(st_ms[k] * 1e3, 2), "alg_bytes": st_alg[k],
                   "gbs": round(st_alg[k] / (ig_ms[k] * 1e-3) / 1e9, 1),
                   "frac": round(st_alg[k] / (ig_ms[k] * 1e-3) / 1e9 / peak, 4)} for k in st_ms}
+    for k, ub in st_unique.items():  # bytes counting each K/V row once per KV head (GQA-unique)
+        stages[k]["unique_alg_bytes"] = ub
+        stages[k]["unique_frac"] = round(ub / (ig_ms[k] * 1e-3) / 1e9 / peak, 4)
     step_gbs = step_alg / (ms * 1e-3 * 1.0) / 1e9
     res = None
     if rank == 0:

@@ -14,7 +14,8 @@
 #include "oa_common.cuh"
 #include "oa_math.cuh"
 #include "oa_warp.cuh"
-#include "oa_warp.cuh"
+
+#include <cooperative_groups.h>
 #include "../../include/openattention_b200.h"
 
 namespace oa {
@@ -1674,13 +1675,25 @@ __device__ __forceinline__ float block_reduce_pf(float v, bool is_max, float* s_
   return r;
 }
 
+// NCTA > 1 (few rows): a row is spread over a cluster of NCTA CTAs.  CTA k makes the token dots of
+// its share of the read list (and the q.Sk dots of its share of the clusters); the CTAs exchange them
+// through distributed shared memory, each then forms the same proxy logits, normaliser and
+// coefficients, and gathers its share of the V / Sv rows; rank 0 adds the NCTA partial outputs in
+// rank order.  Token dots, proxies and softmax statistics are those of NCTA = 1 bit for bit; the
+// output differs only by the order of that last sum.
+template <int NCTA>
 __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) {
   extern __shared__ __align__(16) unsigned char pf_smem[];
-  const int r = blockIdx.x;
+  namespace cg = cooperative_groups;
+  const int r = blockIdx.x / NCTA;
+  const int rank = NCTA > 1 ? (int)cg::this_cluster().block_rank() : 0;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int hw = tid >> 4, hl = tid & 15;
   const int kv = r / kG;
   const int C = a.C, NS = a.NS, NT = a.NS + a.E;
+  // this CTA's share of the read list and of the clusters
+  const int j_lo = rank * NT / NCTA, j_hi = (rank + 1) * NT / NCTA;
+  const int c_lo = rank * C / NCTA, c_hi = (rank + 1) * C / NCTA;
   __shared__ float s_red[kPF / 32];
   __shared__ __align__(16) float s_acc[kPFHalf][kD];
   PFShared S;
@@ -1766,19 +1779,19 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
   //      half-warp with full-mask shuffles run a CTA-uniform trip count: with the half-warp index in
   //      the loop bound, the two halves of a warp would differ by one trip whenever NT = 2w + 1 (mod
   //      64), and one half would shuffle with lanes that have left the loop.
-  for (int jb = 0; jb < NT; jb += kPFHalf * kPFU) {
+  for (int jb = j_lo; jb < j_hi; jb += kPFHalf * kPFU) {
     uint4 kw[kPFU];
 #pragma unroll
     for (int u = 0; u < kPFU; ++u) {
       const int j = jb + hw + u * kPFHalf;
-      const int t = j < NT ? S.tok[j] : -1;
+      const int t = j < j_hi ? S.tok[j] : -1;
       kw[u] = t >= 0 ? ldg_stream(reinterpret_cast<const uint4*>(Kr + (int64_t)t * kD)) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kPFU; ++u) {
       const int j = jb + hw + u * kPFHalf;
       const float d = hw_sum(dot8(qv, kw[u]));
-      if (hl == 0 && j < NT) S.z[j] = d;
+      if (hl == 0 && j < j_hi) S.z[j] = d;
     }
   }
   const float* Skr = a.Sk + rowC * kD + hl * 8;
@@ -1787,12 +1800,12 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
     for (int c = tid; c < C; c += kPF)
       if (S.inv[c] > 0.f) S.qsk[c] = __fmul_rn(a.zdot[rowC + c], a.nt[rowC + c]);
   }
-  for (int cb = 0; a.zdot == nullptr && cb < C; cb += kPFHalf * 4) {
+  for (int cb = c_lo; a.zdot == nullptr && cb < c_hi; cb += kPFHalf * 4) {
     float4 x[4], y[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int c = cb + hw + u * kPFHalf;
-      const bool live = c < C && S.inv[c] > 0.f;
+      const bool live = c < c_hi && S.inv[c] > 0.f;
       x[u] = live ? __ldg(reinterpret_cast<const float4*>(Skr + (int64_t)c * kD)) : make_float4(0.f, 0.f, 0.f, 0.f);
       y[u] = live ? __ldg(reinterpret_cast<const float4*>(Skr + (int64_t)c * kD + 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
@@ -1800,8 +1813,22 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
     for (int u = 0; u < 4; ++u) {
       const int c = cb + hw + u * kPFHalf;
       const float d = hw_sum(dot8f(qv, x[u], y[u]));
-      if (hl == 0 && c < C) S.qsk[c] = d;
+      if (hl == 0 && c < c_hi) S.qsk[c] = d;
     }
+  }
+  if constexpr (NCTA > 1) {  // every CTA gets the other CTAs' token dots (and q.Sk dots)
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    for (int k = 0; k < NCTA; ++k) {
+      if (k == rank) continue;
+      const float* rz = cluster.map_shared_rank(S.z, k);
+      for (int j = k * NT / NCTA + tid; j < (k + 1) * NT / NCTA; j += kPF) S.z[j] = rz[j];
+      if (a.zdot == nullptr) {
+        const float* rq = cluster.map_shared_rank(S.qsk, k);
+        for (int c = k * C / NCTA + tid; c < (k + 1) * C / NCTA; c += kPF) S.qsk[c] = rq[c];
+      }
+    }
+    cluster.sync();  // no CTA overwrites its dots (with coefficients, below) while a peer still reads them
   }
   __syncthreads();
   // ---- proxy logits: one thread per cluster sums q.dk_c over the cluster's read tokens in a fixed
@@ -1846,18 +1873,18 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
   float acc[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) acc[i] = 0.f;
-  for (int j0 = hw; j0 < NT; j0 += kPFHalf * kPFU) {
+  for (int j0 = j_lo + hw; j0 < j_hi; j0 += kPFHalf * kPFU) {
     uint4 vw[kPFU];
 #pragma unroll
     for (int u = 0; u < kPFU; ++u) {
       const int j = j0 + u * kPFHalf;
-      const int t = j < NT ? S.tok[j] : -1;
+      const int t = j < j_hi ? S.tok[j] : -1;
       vw[u] = t >= 0 ? ldg_stream(reinterpret_cast<const uint4*>(Vr + (int64_t)t * kD)) : make_uint4(0, 0, 0, 0);
     }
 #pragma unroll
     for (int u = 0; u < kPFU; ++u) {
       const int j = j0 + u * kPFHalf;
-      const float cf = j < NT ? S.z[j] : 0.f;
+      const float cf = j < j_hi ? S.z[j] : 0.f;
       acc[0] = fmaf(cf, bf_lo(vw[u].x), acc[0]);
       acc[1] = fmaf(cf, bf_hi(vw[u].x), acc[1]);
       acc[2] = fmaf(cf, bf_lo(vw[u].y), acc[2]);
@@ -1869,19 +1896,19 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
     }
   }
   const float* Svr = a.Sv + rowC * kD + hl * 8;
-  for (int c0 = hw; c0 < C; c0 += kPFHalf * 4) {
+  for (int c0 = c_lo + hw; c0 < c_hi; c0 += kPFHalf * 4) {
     float4 x[4], y[4];
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int c = c0 + u * kPFHalf;
-      const bool use = c < C && S.w[c] != 0.f;
+      const bool use = c < c_hi && S.w[c] != 0.f;
       x[u] = use ? __ldg(reinterpret_cast<const float4*>(Svr + (int64_t)c * kD)) : make_float4(0.f, 0.f, 0.f, 0.f);
       y[u] = use ? __ldg(reinterpret_cast<const float4*>(Svr + (int64_t)c * kD + 4)) : make_float4(0.f, 0.f, 0.f, 0.f);
     }
 #pragma unroll
     for (int u = 0; u < 4; ++u) {
       const int c = c0 + u * kPFHalf;
-      const float wc = c < C ? S.w[c] : 0.f;
+      const float wc = c < c_hi ? S.w[c] : 0.f;
       acc[0] = fmaf(wc, x[u].x, acc[0]);
       acc[1] = fmaf(wc, x[u].y, acc[1]);
       acc[2] = fmaf(wc, x[u].z, acc[2]);
@@ -1895,10 +1922,22 @@ __global__ void __launch_bounds__(kPF, 8) proxy_flash_kernel(const ResidArgs a) 
 #pragma unroll
   for (int i = 0; i < 8; ++i) s_acc[hw][hl * 8 + i] = acc[i];
   __syncthreads();
+  float A = 0.f;
   if (tid < kD) {
-    float A = 0.f;
 #pragma unroll
     for (int h = 0; h < kPFHalf; ++h) A += s_acc[h][tid];
+  }
+  if constexpr (NCTA > 1) {  // rank 0 adds the partial outputs in rank order
+    cg::cluster_group cluster = cg::this_cluster();
+    if (tid < kD) s_acc[0][tid] = A;  // a thread rewrites only the column it has summed
+    cluster.sync();
+    A = 0.f;
+    if (rank == 0 && tid < kD)
+      for (int k = 0; k < NCTA; ++k) A += cluster.map_shared_rank(&s_acc[0][0], k)[tid];
+    cluster.sync();  // every CTA stays until rank 0 has read its partial output
+    if (rank != 0) return;
+  }
+  if (tid < kD) {
     const float o = L > 0.f ? A / L : 0.f;
     if (a.out_f32)
       reinterpret_cast<float*>(a.out)[(int64_t)r * a.out_stride + tid] = o;
@@ -2064,8 +2103,31 @@ extern "C" int oa_residual_flash(const void* q, int64_t q_stride, const void* K,
     OA_REQUIRE(oa_aligned16(q) && q_stride % 8 == 0, "%s: q rows must be 16-byte aligned", fn);
     OA_REQUIRE(oa_aligned16(Sk) && oa_aligned16(Sv), "%s: Sk / Sv must be 16-byte aligned", fn);
     const size_t smem = proxy_flash_smem((int)(n_sel + E), (int)C);
-    if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(proxy_flash_kernel), smem, fn)) return rc;
-    proxy_flash_kernel<<<(unsigned)(B * kG * hkv), kPF, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    const int64_t R = B * kG * hkv;
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (R * 2 <= sms) {  // few rows: each row on a cluster of 4 CTAs (distributed shared memory)
+      constexpr int kN = 4;
+      if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(proxy_flash_kernel<kN>), smem, fn)) return rc;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3((unsigned)(R * kN));
+      cfg.blockDim = dim3(kPF);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = static_cast<cudaStream_t>(stream);
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = kN;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      const cudaError_t e = cudaLaunchKernelEx(&cfg, proxy_flash_kernel<kN>, a);
+      if (e != cudaSuccess) return oa_fail(OA_ERR_CUDA, "%s: cluster launch failed: %s", fn, cudaGetErrorString(e));
+    } else {
+      if (int rc = oa_smem_opt_in(reinterpret_cast<const void*>(proxy_flash_kernel<1>), smem, fn)) return rc;
+      proxy_flash_kernel<1><<<(unsigned)R, kPF, smem, static_cast<cudaStream_t>(stream)>>>(a);
+    }
   } else {
     residual_kernel<true><<<(unsigned)(B * kG * hkv), kRW * 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
   }
