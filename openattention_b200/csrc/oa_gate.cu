@@ -671,10 +671,10 @@ __global__ void __launch_bounds__(kTqThreads, 3) topq_kernel(const TopqArgs a) {
 //            topq_kernel); winners are recorded in shared memory as CSR slots (or positions of
 //            generated tokens) and turned into positions by one parallel pass over the row.
 // While phase 2 runs, the next row's score row is already being copied into the freed buffer.
-constexpr int kTsThreads = 512;
+constexpr int kTsThreads = 1024;
 constexpr int kTsWarps = kTsThreads / 32;
 constexpr int kTsGenCap = 4096;  // generated positions whose keys are staged
-constexpr int kTsU = 16;         // 16-byte member vectors a thread has in flight in phase 1
+constexpr int kTsU = 8;          // 16-byte member vectors a thread has in flight in phase 1
 
 struct TsRow {
   const uint16_t* key;   // member keys of the row, CSR order (key[i] = member i; key - mo is 8-byte aligned)
@@ -756,6 +756,92 @@ __device__ __forceinline__ void topq_keys_regs(const TsRow& w, int cs, int nmem,
   if (lane < q && my_idx != 0x7fffffff && rank < lim) win[rank] = ts_enc(my_idx, cs, nmem, rec);
 }
 
+// The same selection without a register copy of the cluster: each lane streams its keys (four per
+// 8-byte word, words 128 keys apart) from shared memory once to find its best two, and the lane that
+// gives up its second best re-reads its keys below the value just taken.  Only (m1, m2) live in
+// registers, so the kernel runs 32 warps per SM and any cluster size takes this path.  Words whose
+// four keys all lie inside the cluster for every lane (all but the first and the last one or two)
+// skip the bounds tests and build their (key, 0xffff - index) words with byte permutes from a packed
+// pair of index complements.
+template <bool FILTER>
+__device__ __forceinline__ void ts_best2(const uint16_t* kb, int idx0, int nmem, int nj, int j_lo, int j_hi,
+                                         const uint32_t (&g)[2], uint32_t below, uint32_t& m1, uint32_t& m2) {
+  m1 = 0u;
+  m2 = 0u;
+  auto take = [&](uint32_t c) {
+    if (FILTER) c = c < below ? c : 0u;
+    m2 = max(m2, min(m1, c));
+    m1 = max(m1, c);
+  };
+  auto checked = [&](int j) {
+    const uint2 x = *reinterpret_cast<const uint2*>(kb + 128 * j);
+    const uint32_t k4[4] = {x.x << 16, x.x & 0xffff0000u, x.y << 16, x.y & 0xffff0000u};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int idx = idx0 + 128 * j + e;
+      take((uint32_t)idx < (uint32_t)nmem ? k4[e] | (uint32_t)(0xffff - idx) : 0u);
+    }
+  };
+  for (int j = 0; j < min(j_lo, nj); ++j) checked(j);
+  // interior words: index complements of keys 0,1 and 2,3 as packed 16-bit pairs (all >= 0 here, so
+  // the packed subtraction never borrows across the halves)
+  const uint32_t b0 = (uint32_t)(0xffff - (idx0 + 128 * j_lo)), b2 = b0 - 2u;
+  const uint32_t p01 = (b0 & 0xffffu) | ((b0 - 1u) << 16), p23 = (b2 & 0xffffu) | ((b2 - 1u) << 16);
+#pragma unroll 2
+  for (int j = j_lo; j < j_hi; ++j) {
+    const uint2 x = *reinterpret_cast<const uint2*>(kb + 128 * j);
+    const uint32_t dj = (uint32_t)(128 * (j - j_lo)) * 0x10001u;
+    const uint32_t l01 = p01 - dj, l23 = p23 - dj;
+    take(__byte_perm(x.x, l01, 0x1054));  // key 0 over the low complement
+    take(__byte_perm(x.x, l01, 0x3276));  // key 1 over the high complement
+    take(__byte_perm(x.y, l23, 0x1054));
+    take(__byte_perm(x.y, l23, 0x3276));
+  }
+  for (int j = max(j_hi, j_lo); j < nj; ++j) checked(j);
+#pragma unroll
+  for (int h = 0; h < 2; ++h) take(g[h]);
+}
+
+__device__ __forceinline__ void topq_keys_stream(const TsRow& w, int cs, int nmem, const int32_t* rec, int ngen,
+                                                 int q, int* win, int lim, int lane) {
+  const int o = (cs + w.mo) & 3;
+  const uint16_t* kb = w.key + (cs - o) + 4 * lane;  // 8-byte aligned
+  const int nj = (nmem + o + 127) >> 7;              // words a lane reads
+  const int idx0 = 4 * lane - o;                     // list index of the lane's first key
+  const int j_lo = o > 0 ? 1 : 0;                    // first word inside the cluster for every lane
+  const int j_hi = (nmem + o) >> 7;                  // words [j_lo, j_hi) lie inside for every lane
+  uint32_t g[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int gi = lane + 32 * h;
+    g[h] = gi < ngen ? (ts_key_at(w, rec[gi]) << 16) | (uint32_t)(0xffff - (nmem + gi)) : 0u;
+  }
+  uint32_t m1, m2;
+  ts_best2<false>(kb, idx0, nmem, nj, j_lo, j_hi, g, 0u, m1, m2);
+  bool have2 = true;  // m2 is this lane's second best
+  int my_idx = 0x7fffffff;
+  for (int k = 0; k < q; ++k) {
+    const uint32_t wm = __reduce_max_sync(0xffffffffu, m1);
+    if (wm == 0u) break;
+    if (m1 == wm) {  // the unique owner
+      if (have2) {
+        m1 = m2;
+        have2 = false;
+      } else {  // re-read below the value just taken
+        ts_best2<true>(kb, idx0, nmem, nj, j_lo, j_hi, g, wm, m1, m2);
+        have2 = true;
+      }
+    }
+    if (lane == k) my_idx = 0xffff - (int)(wm & 0xffffu);
+  }
+  int rank = 0;
+  for (int j = 0; j < q; ++j) {
+    const int oth = __shfl_sync(0xffffffffu, my_idx, j);
+    rank += (oth < my_idx) ? 1 : 0;
+  }
+  if (lane < q && my_idx != 0x7fffffff && rank < lim) win[rank] = ts_enc(my_idx, cs, nmem, rec);
+}
+
 // parts > 1 (fewer rows than SMs): work item w is row w / parts, clusters [p C / parts, (p+1) C / parts)
 // of it for p = w % parts; each item's CTA stages the whole score row but keys and selects only its
 // clusters' members (their CSR range), so a row's work is spread over `parts` SMs.
@@ -771,7 +857,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
   __shared__ int s_q_[2][kMaxC], s_cs_[2][kMaxC], s_cl_[2][kMaxC], s_rcnt_[2][kMaxC];  // this row runs
   __shared__ int s_ord_[2][kMaxC];  // the order in which warps take the clusters
   __shared__ int s_next;
-  __shared__ int s_hist[kTsWarps][256];
+  __shared__ uint32_t s_hist[kTsWarps][128];  // radix path: 256 16-bit counts per warp, two to a word
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int C = a.C;
   const int n = __ldg(a.n_dev), n0 = __ldg(a.n0_dev);
@@ -914,7 +1000,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
     if (warp == 0 && nr < R) prefix(cur ^ 1);
     // ---- phase 2: clusters with q > 0
     TsRow w{s_key + mo, s_gkey, a.scores + (int64_t)r * a.sw, mrow, n0, nsp, gcount, mo};
-    int* hist = s_hist[warp];
+    uint32_t* hist = s_hist[warp];  // candidates per cluster < 2^16 (rows here are below 2^16 positions)
     const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
     const int* s_ord = s_ord_[cur];
     while (true) {
@@ -933,14 +1019,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
       const bool use_list = a.reclist != nullptr && cnt <= a.rmax;
       const int32_t* rec = use_list ? a.reclist + (rC + c) * a.rmax : nullptr;
       const int ngen = use_list ? cnt : 0;
-      if (use_list && q <= kSmallQ && ngen <= 64 && nmem + 3 <= 1024) {
-        const int span = nmem + 3;
-        if (span <= 256)
-          topq_keys_regs<8>(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
-        else if (span <= 512)
-          topq_keys_regs<16>(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
-        else
-          topq_keys_regs<32>(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
+      if (use_list && q <= kSmallQ && ngen <= 64 && nmem + ngen < 0xffff) {
+        topq_keys_stream(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
         continue;
       }
       // radix path over (list index, key): members from the key array, then generated tokens
@@ -972,16 +1052,20 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
       int above = 0, hi = 0, lo = 0;
       bool all = false;
       for (int pass = 0; pass < 2 && !all; ++pass) {
-        for (int b = lane; b < 256; b += 32) hist[b] = 0;
+        for (int b = lane; b < 128; b += 32) hist[b] = 0u;
         __syncwarp();
         for_each([&](bool v, int, uint32_t k) {
-          if (v && (pass == 0 || (int)(k >> 8) == hi)) atomicAdd(&hist[pass == 0 ? (k >> 8) : (k & 255)], 1);
+          if (v && (pass == 0 || (int)(k >> 8) == hi)) {
+            const uint32_t d = pass == 0 ? (k >> 8) : (k & 255u);
+            atomicAdd(&hist[d >> 1], 1u << (16 * (d & 1u)));
+          }
         });
         __syncwarp();
         int cnt8[8], sum = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          cnt8[i] = hist[255 - 8 * lane - i];
+          const int d = 255 - 8 * lane - i;
+          cnt8[i] = (int)((hist[d >> 1] >> (16 * (d & 1))) & 0xffffu);
           sum += cnt8[i];
         }
         int incl = sum;

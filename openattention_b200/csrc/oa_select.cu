@@ -232,17 +232,21 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
   const int gid = lane >> 2, tig = lane & 3;
   const int n = __ldg(a.n_dev);
   __shared__ __align__(128) int8_t sbuf[kTilesPerCta * kTile * kRQ];  // the CTA's codes chunk (32 KB)
-  __shared__ __align__(8) uint64_t mbar;
+  __shared__ __align__(8) uint64_t mbar[kTilesPerCta];  // one per 256-token tile of the chunk
   __shared__ int8_t limb[kG][4][kRQ];  // [head][limb][j]
   __shared__ int sS[kG];
   const int t_begin = blockIdx.y * kTilesPerCta;
   const int tok0 = t_begin * kTile;
   const int ntok = max(0, min(min(a.Lmax, n), tok0 + kTilesPerCta * kTile) - tok0);  // tokens to fetch
-  const uint32_t bar = smem_u32(&mbar);
-  if (tid == 0) mbar_init(bar);
+  if (tid == 0)
+    for (int ti = 0; ti < kTilesPerCta; ++ti) mbar_init(smem_u32(&mbar[ti]));
   __syncthreads();
-  if (tid == 0 && ntok > 0)  // one bulk copy (TMA, no multicast) of the chunk into shared memory
-    bulk_load(sbuf, a.codes + ((int64_t)kv * a.Lmax + tok0) * kRQ, (uint32_t)ntok * kRQ, bar);
+  // one bulk copy (TMA, no multicast) per 256-token tile, each on its own barrier, so the first tile's
+  // MMAs start while the later tiles are still arriving
+  if (tid == 0)
+    for (int ti = 0; ti < kTilesPerCta && ti * kTile < ntok; ++ti)
+      bulk_load(sbuf + ti * kTile * kRQ, a.codes + ((int64_t)kv * a.Lmax + tok0 + ti * kTile) * kRQ,
+                (uint32_t)min(kTile, ntok - ti * kTile) * kRQ, smem_u32(&mbar[ti]));
   // fixed-point image of each head's zq (one warp per head), overlapping the copy
   if (warp < kG) {
     const float z = __bfloat162float(a.zq[(int64_t)(kv * kG + warp) * kRQ + lane]);
@@ -282,12 +286,7 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
   const bool one_mul = S_h >= -100 && S_h <= 100;  // 2^-S is a normal float: one exact multiply
   const float inv2S = one_mul ? pow2f_exact(-S_h) : 0.f;
   uint16_t* srow = a.scores + (int64_t)(kv * kG + tig) * a.sw;
-  const bool ok = ntok == 0 || mbar_wait(bar, 0);
-  if (!__syncthreads_and(ok)) {  // the copy did not complete in time: report, wait once more, skip
-    if (tid == 0 && a.status != nullptr) atomicExch(a.status, 1);
-    if (!ok) mbar_wait(bar, 0);
-    return;
-  }
+  bool failed = false;  // a tile's copy did not complete in the bounded wait (this warp stops computing)
   // exact limb sum l0 + l1 2^8 + l2 2^16 + l3 2^24 (|l| < 2^19) -> fp32 (one rounding) -> x 2^-S -> bf16
   auto finish = [&](int l0, int l1, int l2, int l3) -> uint32_t {
     const long long tot = (long long)(l3 * 256 + l2) * 65536 + (long long)(l1 * 256 + l0);
@@ -301,7 +300,11 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
     const int tile = t_begin + ti;
     const int t0 = tile * kTile;
     float hmax = -INFINITY;  // head tig, this warp's 32 tokens
-    if (t0 < n && t0 < a.Lmax) {
+    if (!failed && t0 < n && t0 < a.Lmax) {
+      failed = !__all_sync(0xffffffffu, mbar_wait(smem_u32(&mbar[ti]), 0));
+      if (failed && lane == 0 && a.status != nullptr) atomicExch(a.status, 1);
+    }
+    if (!failed && t0 < n && t0 < a.Lmax) {
       // only the tiles holding sink / local positions or the end of the row test positions one by one
       const bool edge = t0 < a.ns || t0 + kTile > nv - a.nl;
 #pragma unroll
@@ -343,8 +346,10 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
     hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, 4));
     hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, 8));
     hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, 16));
-    if (wt < a.NT && gid == 0) a.tmax[(int64_t)(kv * kG + tig) * a.tm_stride + wt] = hmax;
+    if (!failed && wt < a.NT && gid == 0) a.tmax[(int64_t)(kv * kG + tig) * a.tm_stride + wt] = hmax;
   }
+  if (failed && lane == 0)  // leave no copy in flight: each wait is bounded and returns at once if done
+    for (int ti = 0; ti < kTilesPerCta && ti * kTile < ntok; ++ti) mbar_wait(smem_u32(&mbar[ti]), 0);
 }
 
 // ------------------------------------------------------------------------ exact row top-k
