@@ -237,7 +237,7 @@ class StageGraphStep(GraphStep):
     the method's fused decode (OursB200.select + residual_flash) written out stage by stage."""
 
     NAMES = ("index_update_kernel", "qgs_scan_kernel", "qgs_select_kernel", "errorgate_waterfill_kernel",
-             "topq_stream_kernel", "proxy_flash_kernel")
+             "topq_pipe_kernel", "proxy_flash_kernel")
 
     def __init__(self, m, Mth, n0, dev):
         self.ev = [torch.cuda.Event(enable_timing=True, external=True) for _ in range(len(self.NAMES) + 1)]
@@ -341,7 +341,7 @@ def stage_profile(m, Mth, gs, iters):
                                    prep=lambda: m.scores.copy_(scores_snap)),
         "errorgate_waterfill_kernel": timed(lambda: S.errorgate_waterfill(qr, K, st, sel, E, m.score, m.nt, m.quota,
                                                                           m.status, zdot=m.zdot)),
-        "topq_stream_kernel": timed(lambda: S.topq(m.scores, st, m.quota, E, n_dev, n0_dev, m.exp_idx, m.status,
+        "topq_pipe_kernel": timed(lambda: S.topq(m.scores, st, m.quota, E, n_dev, n0_dev, m.exp_idx, m.status,
                                                      workspace=m.topq_ws)),
         "proxy_flash_kernel": timed(lambda: S.residual_flash(qr, K, V, st, sel, m.exp_idx, m.nt, m.quota, m.out,
                                                                 status=m.status, zdot=m.zdot)),
@@ -362,7 +362,7 @@ def stage_profile(m, Mth, gs, iters):
         "qgs_scan_kernel": Rkv * n * 32,
         "qgs_select_kernel": R * (nt_tiles * 4 + NS * 4),
         "errorgate_waterfill_kernel": R * (2 * C * D * 4 + C * 4 + NS * (D * 2 + 4) + D * 2 + 4 * C * 4),
-        "topq_stream_kernel": members * 6 + R * (2 * C * 4 + E * 4),
+        "topq_pipe_kernel": members * 6 + R * (2 * C * 4 + E * 4),
         "proxy_flash_kernel": reads * 2 * D * 2 + R * (C * D * 4 + 3 * C * 4 + (NS + E) * 4 + 2 * D * 2),
     }
     # the whole step's algorithmic bytes: codes, the three fp32 sum arrays once, the read rows, the small

@@ -842,6 +842,223 @@ __device__ __forceinline__ void topq_keys_stream(const TsRow& w, int cs, int nme
   if (lane < q && my_idx != 0x7fffffff && rank < lim) win[rank] = ts_enc(my_idx, cs, nmem, rec);
 }
 
+// Row metadata of one work item in shared memory: quotas, CSR starts and lengths, generated-list
+// counts, the order in which warps take the clusters, and the exclusive prefix of the quotas (C + 1).
+struct TsMeta {
+  int *q, *cs, *cl, *rcnt, *ord, *base;
+};
+
+__device__ __forceinline__ void ts_load_meta(const TopqArgs& a, const TsMeta& m, int row, int tid, int nthreads) {
+  const int64_t rc0 = (int64_t)row * a.C;
+  for (int c = tid; c < a.C; c += nthreads) {
+    m.q[c] = quota_int(a.quota[rc0 + c], a.E);
+    m.cs[c] = a.cstart[rc0 + c];
+    m.cl[c] = a.clen[rc0 + c];
+    m.rcnt[c] = a.reclist ? a.reccnt[rc0 + c] : 0x7fffffff;
+  }
+}
+
+// One warp: the exclusive prefix of the quotas and the order in which warps take the clusters.
+__device__ __forceinline__ void ts_prefix(const TsMeta& m, int C, int lane) {
+  const int per = (C + 31) / 32;
+  const int c0 = lane * per, c1 = min(C, c0 + per);
+  int run = 0;
+  for (int c = c0; c < c1; ++c) run += m.q[c];
+  int incl = run;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int x = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += x;
+  }
+  int ex = incl - run;
+  for (int c = c0; c < c1; ++c) {
+    m.base[c] = ex;
+    ex += m.q[c];
+  }
+  if (lane == 31) m.base[C] = incl;
+  // Largest clusters first (C <= 64), so that the last clusters taken are short ones and the
+  // warps reach the end-of-row barrier together; clusters with q = 0 go last.
+  if (C <= 64) {
+    uint64_t wv[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int c = lane + 32 * h;
+      uint32_t work = 0u;
+      if (c < C && m.q[c] > 0) work = 1u + (uint32_t)m.cl[c] + (uint32_t)min(m.rcnt[c], 4096);
+      wv[h] = c < C ? ((uint64_t)work << 32) | (uint64_t)(0xffffffffu - (uint32_t)c) : 0ull;
+    }
+    bitonic64_desc(wv);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int e = lane + 32 * h;
+      if (e < C) m.ord[e] = (int)(0xffffffffu - (uint32_t)wv[h]);
+    }
+  } else {
+    for (int c = lane; c < C; c += 32) m.ord[c] = c;
+  }
+}
+
+// One lane keys U 16-byte vectors of the member list (vectors vbase, vbase + vstride, ...): the four
+// positions of a vector become four score keys in one 8-byte store at key slot 4 * vector.  All loads
+// are issued before the first gather from the staged score row.
+template <int U>
+__device__ __forceinline__ void ts_key_vecs(const int32_t* m0, const int32_t* mem_end, int vbase, int vstride,
+                                            int nvec, const uint16_t* s_spill, uint32_t lim, uint16_t* s_key) {
+  int4 x[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int vi = vbase + u * vstride;
+    const int32_t* p = m0 + 4 * vi;
+    x[u] = make_int4(0, 0, 0, 0);
+    if (vi < nvec) {
+      if (p + 4 <= mem_end) {
+        x[u] = __ldg(reinterpret_cast<const int4*>(p));
+      } else {
+        x[u].x = p + 0 < mem_end ? p[0] : 0;
+        x[u].y = p + 1 < mem_end ? p[1] : 0;
+        x[u].z = p + 2 < mem_end ? p[2] : 0;
+        x[u].w = p + 3 < mem_end ? p[3] : 0;
+      }
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    const int vi = vbase + u * vstride;
+    if (vi < nvec) {  // list entries are positions; the clamp keeps the reads inside the staged row
+      const uint32_t k0 = s_spill[min((uint32_t)x[u].x, lim)], k1 = s_spill[min((uint32_t)x[u].y, lim)];
+      const uint32_t k2 = s_spill[min((uint32_t)x[u].z, lim)], k3 = s_spill[min((uint32_t)x[u].w, lim)];
+      *reinterpret_cast<uint2*>(s_key + 4 * vi) = make_uint2(ukey16x2(k0 | (k1 << 16)), ukey16x2(k2 | (k3 << 16)));
+    }
+  }
+}
+
+// Selection of one work item: the warps of the CTA take its clusters with q > 0 in [c_lo, c_hi) from
+// the shared counter *next and write each cluster's winners (CSR slots, or -(position + 1) of
+// generated tokens) at its quota offset in s_win.  Small quotas with short generated lists take the
+// streamed register path; the rest the radix path (two 8-bit histogram passes for the threshold key,
+// then an ordered collection).
+__device__ __forceinline__ void ts_select(const TopqArgs& a, const TsRow& w, const TsMeta& m, int r, int c_lo,
+                                          int c_hi, int n, int n0, int* next, int* s_win, uint32_t* hist,
+                                          int lane) {
+  const int C = a.C;
+  const int64_t rC = (int64_t)r * C;
+  const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
+  const unsigned lt = (1u << lane) - 1u;
+  while (true) {
+    int c = C;
+    if (lane == 0) {
+      int i;
+      do {
+        i = atomicAdd(next, 1);
+        c = i < C ? m.ord[i] : C;
+      } while (c < C && (m.q[c] <= 0 || c < c_lo || c >= c_hi));
+    }
+    c = __shfl_sync(0xffffffffu, c, 0);
+    if (c >= C) break;
+    const int q = m.q[c], base = m.base[c], cs = m.cs[c], nmem = m.cl[c];
+    const int cnt = m.rcnt[c];
+    const bool use_list = a.reclist != nullptr && cnt <= a.rmax;
+    const int32_t* rec = use_list ? a.reclist + (rC + c) * a.rmax : nullptr;
+    const int ngen = use_list ? cnt : 0;
+    if (use_list && q <= kSmallQ && ngen <= 64 && nmem + ngen < 0xffff) {
+      topq_keys_stream(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
+      continue;
+    }
+    // radix path over (list index, key): members from the key array, then generated tokens
+    const int ngen_scan = max(0, n - n0);
+    auto enc_of = [&](int idx) -> int {
+      if (idx < nmem) return cs + idx;
+      return -((use_list ? rec[idx - nmem] : n0 + (idx - nmem)) + 1);
+    };
+    auto for_each = [&](auto&& f) {
+      for (int i0 = 0; i0 < nmem; i0 += 32) {
+        const int i = i0 + lane;
+        const bool v = i < nmem;
+        f(v, i, v ? (uint32_t)w.key[cs + i] : 0u);
+      }
+      if (use_list) {
+        for (int i0 = 0; i0 < cnt; i0 += 32) {
+          const int i = i0 + lane;
+          const bool v = i < cnt;
+          f(v, nmem + i, v ? ts_key_at(w, rec[i]) : 0u);
+        }
+      } else {
+        for (int i0 = 0; i0 < ngen_scan; i0 += 32) {
+          const int t = n0 + i0 + lane;
+          const bool v = (i0 + lane < ngen_scan) && asg_r[t] == c;
+          f(v, nmem + i0 + lane, v ? ts_key_at(w, t) : 0u);
+        }
+      }
+    };
+    int above = 0, hi = 0, lo = 0;
+    bool all = false;
+    for (int pass = 0; pass < 2 && !all; ++pass) {
+      for (int b = lane; b < 128; b += 32) hist[b] = 0u;
+      __syncwarp();
+      for_each([&](bool v, int, uint32_t k) {
+        if (v && (pass == 0 || (int)(k >> 8) == hi)) {
+          const uint32_t d = pass == 0 ? (k >> 8) : (k & 255u);
+          atomicAdd(&hist[d >> 1], 1u << (16 * (d & 1u)));
+        }
+      });
+      __syncwarp();
+      int cnt8[8], sum = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int d = 255 - 8 * lane - i;
+        cnt8[i] = (int)((hist[d >> 1] >> (16 * (d & 1))) & 0xffffu);
+        sum += cnt8[i];
+      }
+      int incl = sum;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int x = __shfl_up_sync(0xffffffffu, incl, off);
+        if (lane >= off) incl += x;
+      }
+      const int excl = incl - sum;
+      const int need = q - above;
+      int fb = -1, fa = 0;
+      if (excl < need && incl >= need) {
+        int run = excl;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          if (fb < 0 && run + cnt8[i] >= need) {
+            fb = 255 - 8 * lane - i;
+            fa = run;
+          }
+          run += cnt8[i];
+        }
+      }
+      const unsigned who = __ballot_sync(0xffffffffu, fb >= 0);
+      if (who == 0u) {
+        all = true;
+      } else {
+        const int src = __ffs(who) - 1;
+        const int d = __shfl_sync(0xffffffffu, fb, src);
+        above += __shfl_sync(0xffffffffu, fa, src);
+        if (pass == 0) hi = d;
+        else lo = d;
+      }
+      __syncwarp();
+    }
+    const uint32_t T = all ? 0u : (((uint32_t)hi << 8) | (uint32_t)lo);
+    const int need_eq = all ? 0 : q - above;
+    int taken = 0, ties = 0;
+    for_each([&](bool v, int idx, uint32_t k) {
+      const bool gt = v && k > T;
+      const bool eq = v && k == T;
+      const unsigned beq = __ballot_sync(0xffffffffu, eq);
+      const bool take = gt || (eq && ties + __popc(beq & lt) < need_eq);
+      const unsigned bt = __ballot_sync(0xffffffffu, take);
+      const int slot = taken + __popc(bt & lt);
+      if (take && slot < q && base + slot < a.E) s_win[base + slot] = enc_of(idx);
+      taken += __popc(bt);
+      ties += __popc(beq);
+    });
+    __syncwarp();
+  }
+}
+
 // parts > 1 (fewer rows than SMs): work item w is row w / parts, clusters [p C / parts, (p+1) C / parts)
 // of it for p = w % parts; each item's CTA stages the whole score row but keys and selects only its
 // clusters' members (their CSR range), so a row's work is spread over `parts` SMs.
@@ -866,52 +1083,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
   const int gcount = min(max(0, nsp - n0), kTsGenCap);
   const uint32_t bar = smem_u32(&mbar);
   const int32_t* mem_end = a.mem + (int64_t)R * a.Lmax;
-  auto load_meta = [&](int row, int set) {
-    const int64_t rc0 = (int64_t)row * C;
-    for (int c = tid; c < C; c += kTsThreads) {
-      s_q_[set][c] = quota_int(a.quota[rc0 + c], a.E);
-      s_cs_[set][c] = a.cstart[rc0 + c];
-      s_cl_[set][c] = a.clen[rc0 + c];
-      s_rcnt_[set][c] = a.reclist ? a.reccnt[rc0 + c] : 0x7fffffff;
-    }
-  };
-  auto prefix = [&](int set) {  // one warp: exclusive prefix of the quotas
-    const int per = (C + 31) / 32;
-    const int c0 = lane * per, c1 = min(C, c0 + per);
-    int run = 0;
-    for (int c = c0; c < c1; ++c) run += s_q_[set][c];
-    int incl = run;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const int x = __shfl_up_sync(0xffffffffu, incl, off);
-      if (lane >= off) incl += x;
-    }
-    int ex = incl - run;
-    for (int c = c0; c < c1; ++c) {
-      s_base_[set][c] = ex;
-      ex += s_q_[set][c];
-    }
-    if (lane == 31) s_base_[set][C] = incl;
-    // Largest clusters first (C <= 64), so that the last clusters taken are short ones and the
-    // warps reach the end-of-row barrier together; clusters with q = 0 go last.
-    if (C <= 64) {
-      uint64_t wv[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int c = lane + 32 * h;
-        uint32_t work = 0u;
-        if (c < C && s_q_[set][c] > 0) work = 1u + (uint32_t)s_cl_[set][c] + (uint32_t)min(s_rcnt_[set][c], 4096);
-        wv[h] = c < C ? ((uint64_t)work << 32) | (uint64_t)(0xffffffffu - (uint32_t)c) : 0ull;
-      }
-      bitonic64_desc(wv);
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int e = lane + 32 * h;
-        if (e < C) s_ord_[set][e] = (int)(0xffffffffu - (uint32_t)wv[h]);
-      }
-    } else {
-      for (int c = lane; c < C; c += 32) s_ord_[set][c] = c;
-    }
+  auto meta = [&](int set) {
+    return TsMeta{s_q_[set], s_cs_[set], s_cl_[set], s_rcnt_[set], s_ord_[set], s_base_[set]};
   };
   auto winners_out = [&](int row, int lo, int hi) {  // CSR slots / generated positions -> positions
     int32_t* pout = a.exp + (int64_t)row * a.E;
@@ -926,21 +1099,17 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
     mbar_init(bar);
     if (nbytes) bulk_load(s_spill, a.scores + (int64_t)(blockIdx.x / parts) * a.sw, nbytes, bar);
   }
-  load_meta(blockIdx.x / parts, 0);
+  ts_load_meta(a, meta(0), blockIdx.x / parts, tid, kTsThreads);
   __syncthreads();
-  if (warp == 0) prefix(0);
-  const unsigned lt = (1u << lane) - 1u;
+  if (warp == 0) ts_prefix(meta(0), C, lane);
   int it = 0, cur = 0, prev_r = -1, prev_lo = 0, prev_hi = 0;
   for (int wi = blockIdx.x; wi < W; wi += gridDim.x, ++it, cur ^= 1) {
     const int r = wi / parts, part = wi - r * parts;
     const int nwi = wi + (int)gridDim.x;
     const int nr = nwi < W ? nwi / parts : R;  // the next item's row (R: none)
     const int c_lo = part * C / parts, c_hi = (part + 1) * C / parts;
-    const int64_t rC = (int64_t)r * C;
-    const int* s_q = s_q_[cur];
     const int* s_cs = s_cs_[cur];
     const int* s_cl = s_cl_[cur];
-    const int* s_rcnt = s_rcnt_[cur];
     const int* s_base = s_base_[cur];
     const bool ok = nbytes == 0 || mbar_wait(bar, (uint32_t)(it & 1));
     if (!__syncthreads_and(ok)) {
@@ -950,7 +1119,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
     }
     // overlapping phase 1: the previous row's winner positions, the next row's metadata, this row's pads
     if (prev_r >= 0) winners_out(prev_r, prev_lo, prev_hi);
-    if (nr < R) load_meta(nr, cur ^ 1);
+    if (nr < R) ts_load_meta(a, meta(cur ^ 1), nr, tid, kTsThreads);
     int32_t* out = a.exp + (int64_t)r * a.E;
     if (part == 0)
       for (int i = s_base[C] + tid; i < a.E; i += kTsThreads) out[i] = -1;
@@ -963,165 +1132,164 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
     const int32_t* m0 = mrow - mo;
     const int nvec = (m_hi + mo + 3) >> 2;
     const uint32_t lim = (uint32_t)(spill_cap / 2 - 1);  // list entries are positions; clamp keeps reads inside
-    for (int v0 = ((m_lo + mo) >> 2) + tid; v0 < nvec; v0 += kTsThreads * kTsU) {
-      int4 x[kTsU];
-#pragma unroll
-      for (int u = 0; u < kTsU; ++u) {
-        const int vi = v0 + u * kTsThreads;
-        const int32_t* p = m0 + 4 * vi;
-        x[u] = make_int4(0, 0, 0, 0);
-        if (vi < nvec) {
-          if (p + 4 <= mem_end) {
-            x[u] = __ldg(reinterpret_cast<const int4*>(p));
-          } else {
-            x[u].x = p + 0 < mem_end ? p[0] : 0;
-            x[u].y = p + 1 < mem_end ? p[1] : 0;
-            x[u].z = p + 2 < mem_end ? p[2] : 0;
-            x[u].w = p + 3 < mem_end ? p[3] : 0;
-          }
-        }
-      }
-#pragma unroll
-      for (int u = 0; u < kTsU; ++u) {
-        const int vi = v0 + u * kTsThreads;
-        if (vi < nvec) {
-          const uint32_t k0 = s_spill[min((uint32_t)x[u].x, lim)], k1 = s_spill[min((uint32_t)x[u].y, lim)];
-          const uint32_t k2 = s_spill[min((uint32_t)x[u].z, lim)], k3 = s_spill[min((uint32_t)x[u].w, lim)];
-          *reinterpret_cast<uint2*>(s_key + 4 * vi) = make_uint2(ukey16x2(k0 | (k1 << 16)), ukey16x2(k2 | (k3 << 16)));
-        }
-      }
-    }
+    for (int v0 = ((m_lo + mo) >> 2) + tid; v0 < nvec; v0 += kTsThreads * kTsU)
+      ts_key_vecs<kTsU>(m0, mem_end, v0, kTsThreads, nvec, s_spill, lim, s_key);
     for (int i = tid; i < gcount; i += kTsThreads) s_gkey[i] = (uint16_t)ukey16(s_spill[n0 + i]);
     __syncthreads();
     if (tid == 0 && nr < R && nbytes) {  // the staged row is free: fetch the next one
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       bulk_load(s_spill, a.scores + (int64_t)nr * a.sw, nbytes, bar);
     }
-    if (warp == 0 && nr < R) prefix(cur ^ 1);
+    if (warp == 0 && nr < R) ts_prefix(meta(cur ^ 1), C, lane);
     // ---- phase 2: clusters with q > 0
     TsRow w{s_key + mo, s_gkey, a.scores + (int64_t)r * a.sw, mrow, n0, nsp, gcount, mo};
-    uint32_t* hist = s_hist[warp];  // candidates per cluster < 2^16 (rows here are below 2^16 positions)
-    const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
-    const int* s_ord = s_ord_[cur];
-    while (true) {
-      int c = C;
-      if (lane == 0) {
-        int i;
-        do {
-          i = atomicAdd(&s_next, 1);
-          c = i < C ? s_ord[i] : C;
-        } while (c < C && (s_q[c] <= 0 || c < c_lo || c >= c_hi));
-      }
-      c = __shfl_sync(0xffffffffu, c, 0);
-      if (c >= C) break;
-      const int q = s_q[c], base = s_base[c], cs = s_cs[c], nmem = s_cl[c];
-      const int cnt = s_rcnt[c];
-      const bool use_list = a.reclist != nullptr && cnt <= a.rmax;
-      const int32_t* rec = use_list ? a.reclist + (rC + c) * a.rmax : nullptr;
-      const int ngen = use_list ? cnt : 0;
-      if (use_list && q <= kSmallQ && ngen <= 64 && nmem + ngen < 0xffff) {
-        topq_keys_stream(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
-        continue;
-      }
-      // radix path over (list index, key): members from the key array, then generated tokens
-      const int ngen_scan = max(0, n - n0);
-      auto enc_of = [&](int idx) -> int {
-        if (idx < nmem) return cs + idx;
-        return -((use_list ? rec[idx - nmem] : n0 + (idx - nmem)) + 1);
-      };
-      auto for_each = [&](auto&& f) {
-        for (int i0 = 0; i0 < nmem; i0 += 32) {
-          const int i = i0 + lane;
-          const bool v = i < nmem;
-          f(v, i, v ? (uint32_t)w.key[cs + i] : 0u);
-        }
-        if (use_list) {
-          for (int i0 = 0; i0 < cnt; i0 += 32) {
-            const int i = i0 + lane;
-            const bool v = i < cnt;
-            f(v, nmem + i, v ? ts_key_at(w, rec[i]) : 0u);
-          }
-        } else {
-          for (int i0 = 0; i0 < ngen_scan; i0 += 32) {
-            const int t = n0 + i0 + lane;
-            const bool v = (i0 + lane < ngen_scan) && asg_r[t] == c;
-            f(v, nmem + i0 + lane, v ? ts_key_at(w, t) : 0u);
-          }
-        }
-      };
-      int above = 0, hi = 0, lo = 0;
-      bool all = false;
-      for (int pass = 0; pass < 2 && !all; ++pass) {
-        for (int b = lane; b < 128; b += 32) hist[b] = 0u;
-        __syncwarp();
-        for_each([&](bool v, int, uint32_t k) {
-          if (v && (pass == 0 || (int)(k >> 8) == hi)) {
-            const uint32_t d = pass == 0 ? (k >> 8) : (k & 255u);
-            atomicAdd(&hist[d >> 1], 1u << (16 * (d & 1u)));
-          }
-        });
-        __syncwarp();
-        int cnt8[8], sum = 0;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const int d = 255 - 8 * lane - i;
-          cnt8[i] = (int)((hist[d >> 1] >> (16 * (d & 1))) & 0xffffu);
-          sum += cnt8[i];
-        }
-        int incl = sum;
-#pragma unroll
-        for (int off = 1; off < 32; off <<= 1) {
-          const int x = __shfl_up_sync(0xffffffffu, incl, off);
-          if (lane >= off) incl += x;
-        }
-        const int excl = incl - sum;
-        const int need = q - above;
-        int fb = -1, fa = 0;
-        if (excl < need && incl >= need) {
-          int run = excl;
-#pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            if (fb < 0 && run + cnt8[i] >= need) {
-              fb = 255 - 8 * lane - i;
-              fa = run;
-            }
-            run += cnt8[i];
-          }
-        }
-        const unsigned who = __ballot_sync(0xffffffffu, fb >= 0);
-        if (who == 0u) {
-          all = true;
-        } else {
-          const int src = __ffs(who) - 1;
-          const int d = __shfl_sync(0xffffffffu, fb, src);
-          above += __shfl_sync(0xffffffffu, fa, src);
-          if (pass == 0) hi = d;
-          else lo = d;
-        }
-        __syncwarp();
-      }
-      const uint32_t T = all ? 0u : (((uint32_t)hi << 8) | (uint32_t)lo);
-      const int need_eq = all ? 0 : q - above;
-      int taken = 0, ties = 0;
-      for_each([&](bool v, int idx, uint32_t k) {
-        const bool gt = v && k > T;
-        const bool eq = v && k == T;
-        const unsigned beq = __ballot_sync(0xffffffffu, eq);
-        const bool take = gt || (eq && ties + __popc(beq & lt) < need_eq);
-        const unsigned bt = __ballot_sync(0xffffffffu, take);
-        const int slot = taken + __popc(bt & lt);
-        if (take && slot < q && base + slot < a.E) s_win[base + slot] = enc_of(idx);
-        taken += __popc(bt);
-        ties += __popc(beq);
-      });
-      __syncwarp();
-    }
+    ts_select(a, w, meta(cur), r, c_lo, c_hi, n, n0, &s_next, s_win, s_hist[warp], lane);
     __syncthreads();  // winners complete; keys and the cluster counter are reused by the next row
     prev_r = r;
     prev_lo = min(s_base[c_lo], a.E);
     prev_hi = min(s_base[c_hi], a.E);
   }
   if (prev_r >= 0) winners_out(prev_r, prev_lo, prev_hi);
+}
+
+// ------------------------------------------------------------------------ top-q, pipelined rows
+// The persistent top-q with each work item's keying overlapped with the previous item's selection.
+// Shared memory holds one staged score row, two key buffers, two winner lists and three metadata
+// sets.  In iteration i most warps first take clusters of item i until none is left, then take
+// chunks of item i + 1's member list (32 x kTpU vectors, 1024 members) from a second counter and
+// key them from the staged score row of item i + 1; kTpKeyFirst warps do the same in the other
+// order.  So keying and selection run side by side, and the warps that finish one job early help
+// with the other.  One CTA barrier per item; after it the score row of item i + 2 is
+// fetched into the freed buffer while item i + 1 is selected.  Keys of generated positions are read
+// from the score row in global memory (at most 64 per cluster on the register path).
+constexpr int kTpThreads = 1024;
+constexpr int kTpWarps = kTpThreads / 32;
+constexpr int kTpU = 8;  // 16-byte member vectors per lane in one keying chunk
+// Warps that key the next item before selecting (the rest select first).  Measured at c2 (B = 32,
+// 33K positions) for 0 / 4 / 8 / 12 / 16 / 24 of the 32 warps: 106 / 108 / 105 / 102 / 107 / 115 us.
+constexpr int kTpKeyFirst = 12;
+
+__global__ void __launch_bounds__(kTpThreads, 1) topq_pipe_kernel(const TopqArgs a, int R, int spill_cap,
+                                                                  int key_cap, int parts) {
+  extern __shared__ __align__(128) unsigned char tp_smem[];
+  const int C = a.C, E = a.E;
+  const int W = R * parts;  // work items
+  if ((int)blockIdx.x >= W) return;
+  uint16_t* s_spill = reinterpret_cast<uint16_t*>(tp_smem);
+  uint16_t* s_key0 = reinterpret_cast<uint16_t*>(tp_smem + spill_cap);  // two buffers of key_cap keys
+  int* s_win0 = reinterpret_cast<int*>(s_key0 + 2 * key_cap);            // two lists of E winners
+  int* s_meta = s_win0 + 2 * E;                                          // three sets of 6 C + 1 ints
+  __shared__ __align__(8) uint64_t mbar;
+  __shared__ int s_next[2], s_kc[2];  // cluster counters (selection), chunk counters (keying)
+  __shared__ uint32_t s_hist[kTpWarps][128];  // radix path: 256 16-bit counts per warp, two to a word
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int G = (int)gridDim.x;
+  const int n = __ldg(a.n_dev), n0 = __ldg(a.n0_dev);
+  const int nsp = min(n, a.Lmax);
+  const uint32_t nbytes = (uint32_t)((nsp + 7) & ~7) * 2u;
+  const uint32_t bar = smem_u32(&mbar);
+  const int32_t* mem_end = a.mem + (int64_t)R * a.Lmax;
+  const uint32_t lim = (uint32_t)(spill_cap / 2 - 1);  // list entries are positions; the clamp keeps reads inside
+  auto meta = [&](int set) {
+    int* p = s_meta + set * (6 * C + 1);
+    return TsMeta{p, p + C, p + 2 * C, p + 3 * C, p + 4 * C, p + 5 * C};
+  };
+  auto mrow_of = [&](int r) { return a.mem + (int64_t)r * a.Lmax; };
+  auto mo_of = [&](const int32_t* mrow) { return (int)((reinterpret_cast<uintptr_t>(mrow) & 15u) >> 2); };
+  // keying of work item wi into kbuf (key slot = member index + mo): chunks from the counter *cnt
+  auto key_item = [&](int wi, uint16_t* kbuf, int* cnt, const TsMeta& m) {
+    const int r = wi / parts, part = wi - r * parts;
+    const int c_lo = part * C / parts, c_hi = (part + 1) * C / parts;
+    const int m_lo = m.cs[c_lo], m_hi = m.cs[c_hi - 1] + m.cl[c_hi - 1];
+    const int32_t* mrow = mrow_of(r);
+    const int mo = mo_of(mrow);
+    const int nvec = (m_hi + mo + 3) >> 2;
+    const int vb0 = (m_lo + mo) >> 2;
+    while (true) {
+      int ch = 0;
+      if (lane == 0) ch = atomicAdd(cnt, 1);
+      ch = __shfl_sync(0xffffffffu, ch, 0);
+      const int vb = vb0 + ch * (32 * kTpU);
+      if (vb >= nvec) break;
+      ts_key_vecs<kTpU>(mrow - mo, mem_end, vb + lane, 32, nvec, s_spill, lim, kbuf);
+    }
+  };
+  // winners of an item: CSR slots / generated positions -> positions (the CTA's last warps)
+  auto winners_out = [&](int row, int lo, int hi, const int* s_win) {
+    int32_t* pout = a.exp + (int64_t)row * E;
+    const int32_t* pm = mrow_of(row);
+    for (int i = lo + (kTpThreads - 1 - tid); i < hi; i += kTpThreads) {
+      const int e = s_win[i];
+      pout[i] = e >= 0 ? pm[e] : -e - 1;
+    }
+  };
+  auto bail = [&](int pending_parity) {  // a staged row did not arrive in time: report, let copies land, leave
+    if (tid == 0) {
+      if (a.status != nullptr) atomicExch(a.status, 4);
+      if (pending_parity >= 0) mbar_wait(bar, (uint32_t)pending_parity);
+    }
+  };
+  // ---- prologue: the first item's score row, metadata of the first two items, keys of the first
+  if (tid == 0) {
+    mbar_init(bar);
+    s_next[0] = s_next[1] = 0;
+    s_kc[0] = s_kc[1] = 0;
+    if (nbytes) bulk_load(s_spill, a.scores + (int64_t)(blockIdx.x / parts) * a.sw, nbytes, bar);
+  }
+  ts_load_meta(a, meta(0), blockIdx.x / parts, tid, kTpThreads);
+  if ((int)blockIdx.x + G < W) ts_load_meta(a, meta(1), ((int)blockIdx.x + G) / parts, tid, kTpThreads);
+  __syncthreads();
+  if (warp == 0) ts_prefix(meta(0), C, lane);
+  bool fail = !(nbytes == 0 || mbar_wait(bar, 0u));
+  if (!fail) key_item(blockIdx.x, s_key0, &s_kc[0], meta(0));
+  if (__syncthreads_or(fail)) {
+    bail(nbytes ? 0 : -1);
+    return;
+  }
+  int it = 0, prev_r = -1, prev_lo = 0, prev_hi = 0;
+  for (int wi = blockIdx.x; wi < W; wi += G, ++it) {
+    const int cur = it & 1;
+    const int nwi = wi + G, nnwi = wi + 2 * G;
+    const TsMeta m = meta(it % 3), mn = meta((it + 1) % 3), mnn = meta((it + 2) % 3);
+    const int r = wi / parts, part = wi - r * parts;
+    const int c_lo = part * C / parts, c_hi = (part + 1) * C / parts;
+    if (tid == 0) {
+      if (nwi < W && nbytes) {  // the score row was keyed before the last barrier: fetch the next item's
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        bulk_load(s_spill, a.scores + (int64_t)(nwi / parts) * a.sw, nbytes, bar);
+      }
+      s_next[cur ^ 1] = 0;  // the next item's cluster counter (its last use was the previous item)
+      s_kc[cur] = 0;        // the chunk counter of item i + 2 (its last use keyed this item)
+    }
+    if (warp == 1 && nwi < W) ts_prefix(mn, C, lane);  // the next item's quota offsets and cluster order
+    if (nnwi < W) ts_load_meta(a, mnn, nnwi / parts, tid, kTpThreads);  // that set last served item i - 1
+    if (prev_r >= 0) winners_out(prev_r, prev_lo, prev_hi, s_win0 + (cur ^ 1) * E);
+    int32_t* out = a.exp + (int64_t)r * E;
+    if (part == 0)
+      for (int i = m.base[C] + (kTpThreads - 1 - tid); i < E; i += kTpThreads) out[i] = -1;
+    // ---- this item's clusters
+    const int32_t* mrow = mrow_of(r);
+    const int mo = mo_of(mrow);
+    const TsRow w{s_key0 + cur * key_cap + mo, nullptr, a.scores + (int64_t)r * a.sw, mrow, n0, nsp, 0, mo};
+    auto key_next = [&]() {
+      if (nwi < W) {
+        if (nbytes != 0 && !mbar_wait(bar, (uint32_t)((it + 1) & 1))) fail = true;
+        else key_item(nwi, s_key0 + (cur ^ 1) * key_cap, &s_kc[cur ^ 1], mn);
+      }
+    };
+    const bool keys_first = warp >= kTpWarps - kTpKeyFirst;
+    if (keys_first) key_next();
+    ts_select(a, w, m, r, c_lo, c_hi, n, n0, &s_next[cur], s_win0 + cur * E, s_hist[warp], lane);
+    if (!keys_first) key_next();
+    if (__syncthreads_or(fail)) {
+      bail(nwi < W && nbytes ? (it + 1) & 1 : -1);
+      return;
+    }
+    prev_r = r;
+    prev_lo = min(m.base[c_lo], E);
+    prev_hi = min(m.base[c_hi], E);
+  }
+  if (prev_r >= 0) winners_out(prev_r, prev_lo, prev_hi, s_win0 + ((it - 1) & 1) * E);
 }
 
 // ------------------------------------------------------------------------ top-q, long rows
@@ -2079,6 +2247,11 @@ size_t ts_smem_bytes(int64_t Lmax, int64_t E) {  // shared memory of topq_stream
   return spill_bytes + (size_t)(key_cap + kTsGenCap) * 2 + (size_t)E * 4;
 }
 bool ts_fits(int64_t Lmax, int64_t E) { return ts_smem_bytes(Lmax, E) <= 196 * 1024; }
+int tp_key_cap(int64_t Lmax) { return (int)(((Lmax + 7) & ~7ll) + 136); }  // read slack of the streamed selection
+size_t tp_smem_bytes(int64_t Lmax, int64_t E, int64_t C) {  // topq_pipe_kernel: score row, 2 keys, 2 winners, 3 metas
+  return (size_t)((Lmax + 7) & ~7ll) * 2 + (size_t)tp_key_cap(Lmax) * 2 * 2 + (size_t)E * 4 * 2 + (size_t)(6 * C + 1) * 4 * 3;
+}
+bool tp_fits(int64_t Lmax, int64_t E, int64_t C) { return tp_smem_bytes(Lmax, E, C) <= 208 * 1024; }
 int64_t ck_stride(int64_t Lmax) { return (Lmax + 7) & ~7ll; }
 }  // namespace
 }  // namespace oa
@@ -2102,6 +2275,20 @@ extern "C" int oa_topq(const void* scores, int64_t score_stride, int64_t R, int6
   OA_REQUIRE(reclist == nullptr || (reccnt != nullptr && rmax > 0), "%s: reclist needs reccnt and rmax", fn);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const size_t spill_bytes = (size_t)((Lmax + 7) & ~7ll) * 2;
+  if (tp_fits(Lmax, E, C)) {  // pipelined persistent kernel: the score row and two key buffers fit
+    int dev = 0, sms = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    TopqArgs a{static_cast<const uint16_t*>(scores), score_stride, (int)Lmax, (int)C, (int)E, rmax, 1, mem, cstart,
+               clen, asg, reclist, reccnt, quota, n_dev, n0_dev, exp_idx, status};
+    const size_t smem_tp = tp_smem_bytes(Lmax, E, C);
+    if (int rc0 = oa_smem_opt_in(reinterpret_cast<const void*>(topq_pipe_kernel), smem_tp, fn)) return rc0;
+    // fewer rows than SMs: split each row's clusters over up to 4 CTAs
+    const int parts = (int)std::max<int64_t>(1, std::min<int64_t>({4, sms / R, C}));
+    const int grid = (int)std::min<int64_t>(R * parts, sms);
+    topq_pipe_kernel<<<grid, kTpThreads, smem_tp, st>>>(a, (int)R, (int)spill_bytes, tp_key_cap(Lmax), parts);
+    return oa_check_launch(fn);
+  }
   if (ts_fits(Lmax, E)) {  // persistent streamed-key kernel: score row, member keys and generated keys fit
     const int key_cap = (int)(((Lmax + 7) & ~7ll) + 1040);  // list slack of the register path
     const size_t smem_ts = ts_smem_bytes(Lmax, E);

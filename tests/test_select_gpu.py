@@ -103,15 +103,17 @@ def test_topq_matches_oracle_with_ties(golden_dir, kind):
     assert np.array_equal(exp_idx.cpu().numpy(), exp_ref)
 
 
-@pytest.mark.parametrize("use_ws", [True, False])
-def test_topq_long_rows_matches_oracle(use_ws):
-    """Rows too long for the shared-memory top-q (64K positions): with the workspace (keys permuted into
-    CSR order, then selected from contiguous keys) and without it (keys read from global memory)."""
+@pytest.mark.parametrize("n0,use_ws", [(65536, True), (65536, False), (40000, False), (32768, False)])
+def test_topq_long_rows_matches_oracle(n0, use_ws):
+    """Top-q at each row length's kernel, quotas up to 40 (past the register path's 32): 32K positions
+    (the pipelined kernel, two key buffers), 40K (one key buffer), and rows too long for shared memory
+    (64K) with the workspace (keys permuted into CSR order, then selected from contiguous keys) and
+    without it (keys read from global memory)."""
     import types
     from openattention_b200 import method as Mth
     from openattention_b200 import synth
     dev = torch.device("cuda")
-    B, n0, rho = 1, 65536, 0.01
+    B, rho = 1, 0.01
     Lmax = n0 + 8
     K, V, _ = synth.kv_torch(51, B, n0, Lmax, dev)
     Mth.C.K, Mth.C.V, Mth.C.qlen = [K], [V], [40]
