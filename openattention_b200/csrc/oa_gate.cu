@@ -40,6 +40,12 @@ __device__ __forceinline__ float warp_tree_dot(const float (&a)[4], const float 
 }
 
 // ------------------------------------------------------------------------ ErrorGate + water-filling
+// ascending float -> ascending uint32, both zeros mapped to the key of +0 (they compare equal)
+__device__ __forceinline__ uint32_t fkey_eg(float x) {
+  const uint32_t b = __float_as_uint(x == 0.f ? 0.f : x);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
 struct GateArgs {
   const __nv_bfloat16* q;
   int64_t q_stride;
@@ -73,14 +79,14 @@ constexpr int kEgSelCache = 64;    // selected tokens whose K rows are staged in
 
 struct EgShared {
   float *score, *nt, *lg, *zd, *sd, *w, *cap, *ratio, *qb, *capo, *wo, *rato, *cex, *wsuf, *inv;
-  int *ord, *rank2, *nsel, *selc, *selt;
+  int *ord, *rank2, *ord2, *nsel, *selc, *selt;
   __nv_bfloat16* selk;
 };
 
 size_t eg_smem_bytes(int C, int NS) {
   const size_t c4 = (size_t)((C + 3) & ~3);
   const size_t ns4 = (size_t)((NS + 3) & ~3);
-  return c4 * 4 * 18 + ns4 * 4 * 2 + (size_t)std::min(NS, kEgSelCache) * kD * 2;  // 15 fp32 + 3 int per cluster
+  return c4 * 4 * 19 + ns4 * 4 * 2 + (size_t)std::min(NS, kEgSelCache) * kD * 2;  // 15 fp32 + 4 int per cluster
 }
 
 template <int NT>
@@ -117,6 +123,8 @@ __global__ void __launch_bounds__(NT, NT == 64 ? 8 : 2) errorgate_waterfill_kern
     S.ord = reinterpret_cast<int*>(p);
     p += sizeof(int) * c4;
     S.rank2 = reinterpret_cast<int*>(p);
+    p += sizeof(int) * c4;
+    S.ord2 = reinterpret_cast<int*>(p);
     p += sizeof(int) * c4;
     S.nsel = reinterpret_cast<int*>(p);
     p += sizeof(int) * c4;
@@ -305,18 +313,50 @@ __global__ void __launch_bounds__(NT, NT == 64 ? 8 : 2) errorgate_waterfill_kern
     return t;
   };
   const float tot = block_sum(tot_part);  // its barriers also publish w, cap, ratio, score
-  for (int c = tid; c < C; c += NT) {  // ranks by (ratio asc, cluster asc), (score desc, cluster asc)
-    const float ratio = S.ratio[c];
-    const float sm = S.nt[c] > 1.f ? S.score[c] : -INFINITY;
-    int r1 = 0, r2 = 0;
-    for (int j = 0; j < C; ++j) {
-      const float rj = S.ratio[j];
-      r1 += (rj < ratio || (rj == ratio && j < c)) ? 1 : 0;
-      const float sj = S.nt[j] > 1.f ? S.score[j] : -INFINITY;
-      r2 += (sj > sm || (sj == sm && j < c)) ? 1 : 0;
+  // ranks by (ratio asc, cluster asc) and by (score desc, cluster asc)
+  if (C <= 64) {  // one 64-wide warp sort each: warp 0 the ratio order, warp 1 the score order
+    if (warp < 2) {
+      uint64_t v[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int c = lane + 32 * h;
+        uint32_t key = 0u;
+        if (c < C) {
+          const float x = warp == 0 ? S.ratio[c] : (S.nt[c] > 1.f ? S.score[c] : -INFINITY);
+          key = fkey_eg(x);
+          if (warp == 0) key = ~key;  // ascending ratio
+        }
+        v[h] = c < C ? ((uint64_t)key << 32) | (uint64_t)(0xffffffffu - (uint32_t)c) : 0ull;
+      }
+      bitonic64_desc(v);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int e = lane + 32 * h;
+        if (e < C) {
+          const int c = (int)(0xffffffffu - (uint32_t)v[h]);
+          if (warp == 0) {
+            S.ord[e] = c;
+          } else {
+            S.rank2[c] = e;
+            S.ord2[e] = c;
+          }
+        }
+      }
     }
-    S.ord[r1] = c;
-    S.rank2[c] = r2;
+  } else {
+    for (int c = tid; c < C; c += NT) {
+      const float ratio = S.ratio[c];
+      const float sm = S.nt[c] > 1.f ? S.score[c] : -INFINITY;
+      int r1 = 0, r2 = 0;
+      for (int j = 0; j < C; ++j) {
+        const float rj = S.ratio[j];
+        r1 += (rj < ratio || (rj == ratio && j < c)) ? 1 : 0;
+        const float sj = S.nt[j] > 1.f ? S.score[j] : -INFINITY;
+        r2 += (sj > sm || (sj == sm && j < c)) ? 1 : 0;
+      }
+      S.ord[r1] = c;
+      S.rank2[c] = r2;
+    }
   }
   __syncthreads();
   for (int j = tid; j < C; j += NT) {  // caps, weights and ratios in ratio order
@@ -342,11 +382,21 @@ __global__ void __launch_bounds__(NT, NT == 64 ? 8 : 2) errorgate_waterfill_kern
       S.cex[j] = ex;
       ex = __fadd_rn(ex, S.capo[j]);
     }
-  } else if (warp == 1 && lane == 0) {  // suffix sums of the weights in ratio order, accumulated in double from the end
+  } else if (warp == 1) {  // suffix sums of the weights in ratio order, accumulated in double from the end
+    // every lane runs the same sequential sum over 32 weights held across the warp; lane i keeps the
+    // sum that includes weight j0 + i
     double acc = 0.0;
-    for (int j = C - 1; j >= 0; --j) {
-      acc = __dadd_rn(acc, (double)S.wo[j]);
-      S.wsuf[j] = __double2float_rn(acc);
+    for (int j0 = (C - 1) & ~31; j0 >= 0; j0 -= 32) {
+      const int j = j0 + lane;
+      const float wl = j < C ? S.wo[j] : 0.f;
+      double mine = 0.0;
+#pragma unroll
+      for (int i = 31; i >= 0; --i) {
+        const float wi = __shfl_sync(0xffffffffu, wl, i);
+        if (j0 + i < C) acc = __dadd_rn(acc, (double)wi);
+        if (lane == i) mine = acc;
+      }
+      if (j < C) S.wsuf[j] = __double2float_rn(mine);
     }
   }
   __syncthreads();
@@ -374,10 +424,20 @@ __global__ void __launch_bounds__(NT, NT == 64 ? 8 : 2) errorgate_waterfill_kern
   }
   const float sumq = block_sum(q_part);
   const float rem = fmaxf(__fsub_rn(fminf(tot, a.E), sumq), 0.f);
+  // clusters with room, in score order (C <= 64: one bit per rank in two ballots)
+  unsigned rb0 = 0u, rb1 = 0u;
+  if (C <= 64) {
+    const int o0 = lane < C ? S.ord2[lane] : 0, o1 = lane + 32 < C ? S.ord2[lane + 32] : 0;
+    rb0 = __ballot_sync(0xffffffffu, lane < C && S.qb[o0] < S.cap[o0]);
+    rb1 = __ballot_sync(0xffffffffu, lane + 32 < C && S.qb[o1] < S.cap[o1]);
+  }
   for (int c = tid; c < C; c += NT) {  // leftovers: one each to the best-scoring clusters with room
     const int my = S.rank2[c];
     int before = 0;
-    for (int j = 0; j < C; ++j) before += (S.qb[j] < S.cap[j] && S.rank2[j] < my) ? 1 : 0;
+    if (C <= 64)
+      before = my < 32 ? __popc(rb0 & ((1u << my) - 1u)) : __popc(rb0) + __popc(rb1 & ((1u << (my - 32)) - 1u));
+    else
+      for (int j = 0; j < C; ++j) before += (S.qb[j] < S.cap[j] && S.rank2[j] < my) ? 1 : 0;
     const bool room = S.qb[c] < S.cap[c];
     const float add = (room && (float)before < rem) ? 1.f : 0.f;
     a.quota[rC + c] = __fadd_rn(S.qb[c], add);
@@ -937,13 +997,113 @@ __device__ __forceinline__ void ts_key_vecs(const int32_t* m0, const int32_t* me
 // generated tokens) at its quota offset in s_win.  Small quotas with short generated lists take the
 // streamed register path; the rest the radix path (two 8-bit histogram passes for the threshold key,
 // then an ordered collection).
+// The radix path of the selection (quota above the register path's 32, or a long generated list):
+// two 8-bit histogram passes over the cluster's keys for the threshold key, then an ordered
+// collection.
+__device__ __forceinline__ void ts_radix(const TsRow w, int E, int c, int q, int base, int cs, int nmem,
+                                      const int32_t* rec, bool use_list, int cnt, int n, int n0,
+                                      const int32_t* asg_r, int* s_win, uint32_t* hist, int lane) {
+  const unsigned lt = (1u << lane) - 1u;
+  // radix path over (list index, key): members from the key array, then generated tokens
+  const int ngen_scan = max(0, n - n0);
+  auto enc_of = [&](int idx) -> int {
+    if (idx < nmem) return cs + idx;
+    return -((use_list ? rec[idx - nmem] : n0 + (idx - nmem)) + 1);
+  };
+  auto for_each = [&](auto&& f) {
+    for (int i0 = 0; i0 < nmem; i0 += 32) {
+      const int i = i0 + lane;
+      const bool v = i < nmem;
+      f(v, i, v ? (uint32_t)w.key[cs + i] : 0u);
+    }
+    if (use_list) {
+      for (int i0 = 0; i0 < cnt; i0 += 32) {
+        const int i = i0 + lane;
+        const bool v = i < cnt;
+        f(v, nmem + i, v ? ts_key_at(w, rec[i]) : 0u);
+      }
+    } else {
+      for (int i0 = 0; i0 < ngen_scan; i0 += 32) {
+        const int t = n0 + i0 + lane;
+        const bool v = (i0 + lane < ngen_scan) && asg_r[t] == c;
+        f(v, nmem + i0 + lane, v ? ts_key_at(w, t) : 0u);
+      }
+    }
+  };
+  int above = 0, hi = 0, lo = 0;
+  bool all = false;
+  for (int pass = 0; pass < 2 && !all; ++pass) {
+    for (int b = lane; b < 128; b += 32) hist[b] = 0u;
+    __syncwarp();
+    for_each([&](bool v, int, uint32_t k) {
+      if (v && (pass == 0 || (int)(k >> 8) == hi)) {
+        const uint32_t d = pass == 0 ? (k >> 8) : (k & 255u);
+        atomicAdd(&hist[d >> 1], 1u << (16 * (d & 1u)));
+      }
+    });
+    __syncwarp();
+    int cnt8[8], sum = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int d = 255 - 8 * lane - i;
+      cnt8[i] = (int)((hist[d >> 1] >> (16 * (d & 1))) & 0xffffu);
+      sum += cnt8[i];
+    }
+    int incl = sum;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int x = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += x;
+    }
+    const int excl = incl - sum;
+    const int need = q - above;
+    int fb = -1, fa = 0;
+    if (excl < need && incl >= need) {
+      int run = excl;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        if (fb < 0 && run + cnt8[i] >= need) {
+          fb = 255 - 8 * lane - i;
+          fa = run;
+        }
+        run += cnt8[i];
+      }
+    }
+    const unsigned who = __ballot_sync(0xffffffffu, fb >= 0);
+    if (who == 0u) {
+      all = true;
+    } else {
+      const int src = __ffs(who) - 1;
+      const int d = __shfl_sync(0xffffffffu, fb, src);
+      above += __shfl_sync(0xffffffffu, fa, src);
+      if (pass == 0) hi = d;
+      else lo = d;
+    }
+    __syncwarp();
+  }
+  const uint32_t T = all ? 0u : (((uint32_t)hi << 8) | (uint32_t)lo);
+  const int need_eq = all ? 0 : q - above;
+  int taken = 0, ties = 0;
+  for_each([&](bool v, int idx, uint32_t k) {
+    const bool gt = v && k > T;
+    const bool eq = v && k == T;
+    const unsigned beq = __ballot_sync(0xffffffffu, eq);
+    const bool take = gt || (eq && ties + __popc(beq & lt) < need_eq);
+    const unsigned bt = __ballot_sync(0xffffffffu, take);
+    const int slot = taken + __popc(bt & lt);
+    if (take && slot < q && base + slot < E) s_win[base + slot] = enc_of(idx);
+    taken += __popc(bt);
+    ties += __popc(beq);
+  });
+  __syncwarp();
+}
+
 __device__ __forceinline__ void ts_select(const TopqArgs& a, const TsRow& w, const TsMeta& m, int r, int c_lo,
                                           int c_hi, int n, int n0, int* next, int* s_win, uint32_t* hist,
                                           int lane) {
   const int C = a.C;
   const int64_t rC = (int64_t)r * C;
   const int32_t* asg_r = a.asg + (int64_t)r * a.Lmax;
-  const unsigned lt = (1u << lane) - 1u;
   while (true) {
     int c = C;
     if (lane == 0) {
@@ -964,98 +1124,7 @@ __device__ __forceinline__ void ts_select(const TopqArgs& a, const TsRow& w, con
       topq_keys_stream(w, cs, nmem, rec, ngen, q, s_win + base, a.E - base, lane);
       continue;
     }
-    // radix path over (list index, key): members from the key array, then generated tokens
-    const int ngen_scan = max(0, n - n0);
-    auto enc_of = [&](int idx) -> int {
-      if (idx < nmem) return cs + idx;
-      return -((use_list ? rec[idx - nmem] : n0 + (idx - nmem)) + 1);
-    };
-    auto for_each = [&](auto&& f) {
-      for (int i0 = 0; i0 < nmem; i0 += 32) {
-        const int i = i0 + lane;
-        const bool v = i < nmem;
-        f(v, i, v ? (uint32_t)w.key[cs + i] : 0u);
-      }
-      if (use_list) {
-        for (int i0 = 0; i0 < cnt; i0 += 32) {
-          const int i = i0 + lane;
-          const bool v = i < cnt;
-          f(v, nmem + i, v ? ts_key_at(w, rec[i]) : 0u);
-        }
-      } else {
-        for (int i0 = 0; i0 < ngen_scan; i0 += 32) {
-          const int t = n0 + i0 + lane;
-          const bool v = (i0 + lane < ngen_scan) && asg_r[t] == c;
-          f(v, nmem + i0 + lane, v ? ts_key_at(w, t) : 0u);
-        }
-      }
-    };
-    int above = 0, hi = 0, lo = 0;
-    bool all = false;
-    for (int pass = 0; pass < 2 && !all; ++pass) {
-      for (int b = lane; b < 128; b += 32) hist[b] = 0u;
-      __syncwarp();
-      for_each([&](bool v, int, uint32_t k) {
-        if (v && (pass == 0 || (int)(k >> 8) == hi)) {
-          const uint32_t d = pass == 0 ? (k >> 8) : (k & 255u);
-          atomicAdd(&hist[d >> 1], 1u << (16 * (d & 1u)));
-        }
-      });
-      __syncwarp();
-      int cnt8[8], sum = 0;
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int d = 255 - 8 * lane - i;
-        cnt8[i] = (int)((hist[d >> 1] >> (16 * (d & 1))) & 0xffffu);
-        sum += cnt8[i];
-      }
-      int incl = sum;
-#pragma unroll
-      for (int off = 1; off < 32; off <<= 1) {
-        const int x = __shfl_up_sync(0xffffffffu, incl, off);
-        if (lane >= off) incl += x;
-      }
-      const int excl = incl - sum;
-      const int need = q - above;
-      int fb = -1, fa = 0;
-      if (excl < need && incl >= need) {
-        int run = excl;
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          if (fb < 0 && run + cnt8[i] >= need) {
-            fb = 255 - 8 * lane - i;
-            fa = run;
-          }
-          run += cnt8[i];
-        }
-      }
-      const unsigned who = __ballot_sync(0xffffffffu, fb >= 0);
-      if (who == 0u) {
-        all = true;
-      } else {
-        const int src = __ffs(who) - 1;
-        const int d = __shfl_sync(0xffffffffu, fb, src);
-        above += __shfl_sync(0xffffffffu, fa, src);
-        if (pass == 0) hi = d;
-        else lo = d;
-      }
-      __syncwarp();
-    }
-    const uint32_t T = all ? 0u : (((uint32_t)hi << 8) | (uint32_t)lo);
-    const int need_eq = all ? 0 : q - above;
-    int taken = 0, ties = 0;
-    for_each([&](bool v, int idx, uint32_t k) {
-      const bool gt = v && k > T;
-      const bool eq = v && k == T;
-      const unsigned beq = __ballot_sync(0xffffffffu, eq);
-      const bool take = gt || (eq && ties + __popc(beq & lt) < need_eq);
-      const unsigned bt = __ballot_sync(0xffffffffu, take);
-      const int slot = taken + __popc(bt & lt);
-      if (take && slot < q && base + slot < a.E) s_win[base + slot] = enc_of(idx);
-      taken += __popc(bt);
-      ties += __popc(beq);
-    });
-    __syncwarp();
+    ts_radix(w, a.E, c, q, base, cs, nmem, rec, use_list, cnt, n, n0, asg_r, s_win, hist, lane);
   }
 }
 
@@ -1162,12 +1231,11 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
 // with the other.  One CTA barrier per item; after it the score row of item i + 2 is
 // fetched into the freed buffer while item i + 1 is selected.  Keys of generated positions are read
 // from the score row in global memory (at most 64 per cluster on the register path).
-constexpr int kTpThreads = 1024;
+constexpr int kTpThreads = 768;
 constexpr int kTpWarps = kTpThreads / 32;
 constexpr int kTpU = 8;  // 16-byte member vectors per lane in one keying chunk
-// Warps that key the next item before selecting (the rest select first).  Measured at c2 (B = 32,
-// 33K positions) for 0 / 4 / 8 / 12 / 16 / 24 of the 32 warps: 106 / 108 / 105 / 102 / 107 / 115 us.
-constexpr int kTpKeyFirst = 12;
+// Warps that key the next item before selecting (the rest select first).
+constexpr int kTpKeyFirst = 9;
 
 __global__ void __launch_bounds__(kTpThreads, 1) topq_pipe_kernel(const TopqArgs a, int R, int spill_cap,
                                                                   int key_cap, int parts) {
