@@ -287,19 +287,19 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
   const float inv2S = one_mul ? pow2f_exact(-S_h) : 0.f;
   uint16_t* srow = a.scores + (int64_t)(kv * kG + tig) * a.sw;
   bool failed = false;  // a tile's copy did not complete in the bounded wait (this warp stops computing)
-  // exact limb sum l0 + l1 2^8 + l2 2^16 + l3 2^24 (|l| < 2^19) -> fp32 (one rounding) -> x 2^-S -> bf16
-  auto finish = [&](int l0, int l1, int l2, int l3) -> uint32_t {
+  // exact limb sum l0 + l1 2^8 + l2 2^16 + l3 2^24 (|l| < 2^19) -> fp32 (one rounding) -> x 2^-S; the
+  // caller rounds two of them to bf16 with one packed conversion
+  auto finish = [&](int l0, int l1, int l2, int l3) -> float {
     const long long tot = (long long)(l3 * 256 + l2) * 65536 + (long long)(l1 * 256 + l0);
     const float f0 = __ll2float_rn(tot);
-    const float f = one_mul ? __fmul_rn(f0, inv2S) : scale_pow2(f0, -S_h);
-    return f2bf_bits(f);
+    return one_mul ? __fmul_rn(f0, inv2S) : scale_pow2(f0, -S_h);
   };
   const int nv = min(n, a.Lmax);  // positions with a score; the rest of a touched tile is written -inf
 #pragma unroll
   for (int ti = 0; ti < kTilesPerCta; ++ti) {
     const int tile = t_begin + ti;
     const int t0 = tile * kTile;
-    float hmax = -INFINITY;  // head tig, this warp's 32 tokens
+    __nv_bfloat162 hmax2 = __floats2bfloat162_rn(-INFINITY, -INFINITY);  // head tig, this warp's 32 tokens
     if (!failed && t0 < n && t0 < a.Lmax) {
       failed = !__all_sync(0xffffffffu, mbar_wait(smem_u32(&mbar[ti]), 0));
       if (failed && lane == 0 && a.status != nullptr) atomicExch(a.status, 1);
@@ -321,28 +321,32 @@ __global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a
         int d0[4], d1[4];
         mma_s8(d0, af, bf[0][0], bf[0][1]);
         mma_s8(d1, af, bf[1][0], bf[1][1]);
-        uint32_t s0 = finish(d0[0], d0[1], d1[0], d1[1]);  // token ta
-        uint32_t s1 = finish(d0[2], d0[3], d1[2], d1[3]);  // token ta + 8
+        // tokens ta (low half) and ta + 8 (high half) as one bf16 pair
+        __nv_bfloat162 pk2 = __floats2bfloat162_rn(finish(d0[0], d0[1], d1[0], d1[1]), finish(d0[2], d0[3], d1[2], d1[3]));
+        uint32_t pk = *reinterpret_cast<uint32_t*>(&pk2);
         if (edge) {
+          uint32_t s0 = pk & 0xffffu, s1 = pk >> 16;
           if (ta < a.ns || ta >= n - a.nl || ta >= nv) s0 = 0xff80u;
           if (ta + 8 < a.ns || ta + 8 >= n - a.nl || ta + 8 >= nv) s1 = 0xff80u;
           if (ta < a.Lmax) srow[ta] = (uint16_t)s0;
           if (ta + 8 < a.Lmax) srow[ta + 8] = (uint16_t)s1;
+          pk = s0 | (s1 << 16);
+          pk2 = *reinterpret_cast<__nv_bfloat162*>(&pk);
         } else {
           // pair tokens with the neighbouring lane (gid ^ 1, same head): even gid stores tokens
           // (ta, ta + 1), odd gid tokens (ta + 7, ta + 8), each as one 4-byte store
-          const uint32_t mine = s0 | (s1 << 16);
-          const uint32_t other = __shfl_xor_sync(0xffffffffu, mine, 4);
+          const uint32_t other = __shfl_xor_sync(0xffffffffu, pk, 4);
           if ((gid & 1) == 0)
-            *reinterpret_cast<uint32_t*>(srow + ta) = s0 | (other << 16);
+            *reinterpret_cast<uint32_t*>(srow + ta) = (pk & 0xffffu) | (other << 16);
           else
-            *reinterpret_cast<uint32_t*>(srow + ta + 7) = (other >> 16) | (s1 << 16);
+            *reinterpret_cast<uint32_t*>(srow + ta + 7) = (other >> 16) | (pk & 0xffff0000u);
         }
-        hmax = fmaxf(hmax, fmaxf(__uint_as_float(s0 << 16), __uint_as_float(s1 << 16)));
+        hmax2 = __hmax2(hmax2, pk2);  // exact: the maximum of bf16 values
       }
     }
     // maximum of this warp's 32 tokens for head tig (a 32-token tile): reduce over gid
     const int wt = tile * (kTile / kMaxTile) + warp;  // 32-token tile index
+    float hmax = fmaxf(__low2float(hmax2), __high2float(hmax2));
     hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, 4));
     hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, 8));
     hmax = fmaxf(hmax, __shfl_xor_sync(0xffffffffu, hmax, 16));
