@@ -59,7 +59,7 @@ __global__ void __launch_bounds__(128, 8) index_update_kernel(const IndexArgs a)
   const int kv = r / kG, g = r % kG;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int pos = __ldg(a.n_dev) - 1;
-  __shared__ float kf[kD], vf[kD], qf[kD], zp[kRC];
+  __shared__ __align__(16) float kf[kD], vf[kD], qf[kD], zp[kRC];
   __shared__ __align__(16) float sU[kD * kRQ];              // this KV head's QGS basis
   __shared__ __align__(16) __nv_bfloat16 sW[kD * kRC];      // this query head's QGC projection
   __shared__ float s_bv[4];
@@ -82,8 +82,11 @@ __global__ void __launch_bounds__(128, 8) index_update_kernel(const IndexArgs a)
   for (int u = 0; u < kWV; ++u)
     cp_async16(reinterpret_cast<uint4*>(sW) + tid + 128 * u,
                reinterpret_cast<const uint4*>(a.W + (int64_t)r * kD * kRC) + tid + 128 * u);
+  // centroid row i's four 16-byte chunks k land at chunk k ^ ((i >> 1) & 3): the scoring's 16-byte
+  // reads (one row per lane) then meet no bank conflicts
   for (int i = tid; i < ncv; i += 128)
-    cp_async16(reinterpret_cast<float4*>(iu_cent) + i, reinterpret_cast<const float4*>(ce) + i);
+    cp_async16(reinterpret_cast<float4*>(iu_cent) + (i & ~3) + ((i & 3) ^ ((i >> 3) & 3)),
+               reinterpret_cast<const float4*>(ce) + i);
   __nv_bfloat16 kb = __float2bfloat16_rn(0.f), vb = kb, qb = kb;
   if (have_tok) {
     if (a.k_new != nullptr) {
@@ -108,16 +111,28 @@ __global__ void __launch_bounds__(128, 8) index_update_kernel(const IndexArgs a)
     if (a.q != nullptr) {
       const int j = lane;
       float acc = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < kD; ++d) acc = __fmaf_rn(qf[d], sU[d * kRQ + j], acc);
+#pragma unroll 2
+      for (int d = 0; d < kD; d += 4) {  // q four at a time (one broadcast 16-byte read), d ascending
+        const float4 q4 = *reinterpret_cast<const float4*>(&qf[d]);
+        acc = __fmaf_rn(q4.x, sU[d * kRQ + j], acc);
+        acc = __fmaf_rn(q4.y, sU[(d + 1) * kRQ + j], acc);
+        acc = __fmaf_rn(q4.z, sU[(d + 2) * kRQ + j], acc);
+        acc = __fmaf_rn(q4.w, sU[(d + 3) * kRQ + j], acc);
+      }
       a.zq[(int64_t)r * kRQ + j] = __float2bfloat16_rn(__fmul_rn(acc, __ldg(&a.scale[kv * kRQ + j])));
     }
   } else if (warp == 1) {  // QGS code of the new key (per KV head: query head 0 of the group writes it)
     if (have_tok && g == 0) {
       const int j = lane;
       float acc = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < kD; ++d) acc = __fmaf_rn(kf[d], sU[d * kRQ + j], acc);
+#pragma unroll 2
+      for (int d = 0; d < kD; d += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(&kf[d]);
+        acc = __fmaf_rn(k4.x, sU[d * kRQ + j], acc);
+        acc = __fmaf_rn(k4.y, sU[(d + 1) * kRQ + j], acc);
+        acc = __fmaf_rn(k4.z, sU[(d + 2) * kRQ + j], acc);
+        acc = __fmaf_rn(k4.w, sU[(d + 3) * kRQ + j], acc);
+      }
       float c = rintf(__fdiv_rn(acc, __ldg(&a.scale[kv * kRQ + j])));
       c = fminf(fmaxf(c, -127.f), 127.f);
       a.codes[((int64_t)kv * a.Lmax + pos) * kRQ + j] = (int8_t)c;
@@ -126,8 +141,14 @@ __global__ void __launch_bounds__(128, 8) index_update_kernel(const IndexArgs a)
     if (have_tok && lane < kRC) {
       const int c = lane;
       float acc = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < kD; ++d) acc = __fmaf_rn(kf[d], __bfloat162float(sW[d * kRC + c]), acc);
+#pragma unroll 2
+      for (int d = 0; d < kD; d += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(&kf[d]);
+        acc = __fmaf_rn(k4.x, __bfloat162float(sW[d * kRC + c]), acc);
+        acc = __fmaf_rn(k4.y, __bfloat162float(sW[(d + 1) * kRC + c]), acc);
+        acc = __fmaf_rn(k4.z, __bfloat162float(sW[(d + 2) * kRC + c]), acc);
+        acc = __fmaf_rn(k4.w, __bfloat162float(sW[(d + 3) * kRC + c]), acc);
+      }
       zp[c] = __fsub_rn(bf_round(acc), __ldg(&a.colmean[r * kRC + c]));
     }
   }
@@ -139,10 +160,15 @@ __global__ void __launch_bounds__(128, 8) index_update_kernel(const IndexArgs a)
   for (int i = tid; i < C; i += 128) {
     float dot = 0.f, nrm = 0.f;
 #pragma unroll
-    for (int c = 0; c < kRC; ++c) {
-      const float x = i < cstage ? iu_cent[i * kRC + c] : __ldg(&ce[i * kRC + c]);
-      dot = __fmaf_rn(zp[c], x, dot);
-      nrm = __fmaf_rn(x, x, nrm);
+    for (int k = 0; k < kRC / 4; ++k) {  // chunk k of row i, c = 4k .. 4k + 3 ascending
+      const float4 x4 = i < cstage ? reinterpret_cast<const float4*>(iu_cent)[i * 4 + (k ^ ((i >> 1) & 3))]
+                                   : __ldg(reinterpret_cast<const float4*>(ce) + i * 4 + k);
+      const float xs[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        dot = __fmaf_rn(zp[4 * k + e], xs[e], dot);
+        nrm = __fmaf_rn(xs[e], xs[e], nrm);
+      }
     }
     const float dist = __fsub_rn(dot, __fmul_rn(0.5f, nrm));
     if (dist > bestv) {
