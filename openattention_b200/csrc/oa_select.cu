@@ -490,7 +490,33 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   const int kt2 = min(2 * a.k_top, ntv);
   const float* tm = a.tmax + (int64_t)r * a.tm_stride;
   uint16_t* srw = a.scores + (int64_t)r * a.sw;
-  for (int i = lane; i < ntv; i += 32) tkey[i] = fkey(tm[i]);
+  {  // tile keys: the row's maxima with 16-byte loads, all of a lane's loads issued before its stores
+    const int h = min(ntv, (int)((4u - ((uint32_t)(reinterpret_cast<uintptr_t>(tm) >> 2) & 3u)) & 3u));
+    if (lane < h) tkey[lane] = fkey(tm[lane]);
+    const int nv4 = (ntv - h) >> 2;
+    const float4* tm4 = reinterpret_cast<const float4*>(tm + h);  // 16-byte aligned
+    constexpr int kU = 8;
+    for (int v0 = lane; v0 < nv4; v0 += 32 * kU) {
+      float4 x[kU];
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int vi = v0 + 32 * u;
+        x[u] = vi < nv4 ? __ldg(tm4 + vi) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int u = 0; u < kU; ++u) {
+        const int vi = v0 + 32 * u;
+        if (vi < nv4) {
+          uint32_t* t4 = tkey + h + 4 * vi;
+          t4[0] = fkey(x[u].x);
+          t4[1] = fkey(x[u].y);
+          t4[2] = fkey(x[u].z);
+          t4[3] = fkey(x[u].w);
+        }
+      }
+    }
+    for (int i = h + 4 * nv4 + lane; i < ntv; i += 32) tkey[i] = fkey(tm[i]);
+  }
   __syncwarp();
   // (1) tiles: threshold + sort when it applies, else the radix select
   uint64_t srt[2], kth;
@@ -528,14 +554,26 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   // (2) candidate keys of the chosen tiles (ascending tile order) staged with 16-byte loads;
   //     positions >= n get key 0 (below every real key, which is >= 0x7f)
   const int m = kt2 * kMaxTile;
-  for (int i = lane * 8; i < m; i += 32 * 8) {
-    const int pos = tiles[i >> 5] * kMaxTile + (i & (kMaxTile - 1));
-    const uint4 w = *reinterpret_cast<const uint4*>(srw + pos);
-    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+  for (int i0 = lane * 8; i0 < m; i0 += 32 * 8 * 4) {  // four 16-byte loads in flight per lane
+    uint4 w[4];
+    int pos[4];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      const uint32_t b = (wv[u >> 1] >> (16 * (u & 1))) & 0xffffu;
-      ckey[i + u] = (pos + u < n) ? (uint16_t)ukey16(b) : (uint16_t)0;
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + 32 * 8 * u;
+      pos[u] = i < m ? tiles[i >> 5] * kMaxTile + (i & (kMaxTile - 1)) : 0;
+      w[u] = i < m ? *reinterpret_cast<const uint4*>(srw + pos[u]) : make_uint4(0u, 0u, 0u, 0u);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int i = i0 + 32 * 8 * u;
+      if (i < m) {
+        const uint32_t wv[4] = {w[u].x, w[u].y, w[u].z, w[u].w};
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const uint32_t b = (wv[e >> 1] >> (16 * (e & 1))) & 0xffffu;
+          ckey[i + e] = (pos[u] + e < n) ? (uint16_t)ukey16(b) : (uint16_t)0;
+        }
+      }
     }
   }
   __syncwarp();
