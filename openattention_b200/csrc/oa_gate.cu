@@ -944,7 +944,8 @@ __device__ __forceinline__ void ts_prefix(const TsMeta& m, int C, int lane) {
     for (int h = 0; h < 2; ++h) {
       const int c = lane + 32 * h;
       uint32_t work = 0u;
-      if (c < C && m.q[c] > 0) work = 1u + (uint32_t)m.cl[c] + (uint32_t)min(m.rcnt[c], 4096);
+      if (c < C && m.q[c] > 0)  // clusters for the radix path (quota above 32) cost the most per key: first
+        work = (m.q[c] > kSmallQ ? 0x100000u : 0u) + 1u + (uint32_t)m.cl[c] + (uint32_t)min(m.rcnt[c], 4096);
       wv[h] = c < C ? ((uint64_t)work << 32) | (uint64_t)(0xffffffffu - (uint32_t)c) : 0ull;
     }
     bitonic64_desc(wv);
