@@ -222,7 +222,7 @@ __global__ void __launch_bounds__(128, 8) index_update_kernel(const IndexArgs a)
 constexpr int kTile = 256;         // tokens per CTA step (8 warps x 32 tokens)
 constexpr int kMaxTile = 32;       // tokens per tile maximum (one warp's share of a step)
 constexpr int kScanThreads = 256;
-constexpr int kTilesPerCta = 4;
+constexpr int kTilesPerCta = 3;  // 24 KB of codes: 8 CTAs (64 warps) per SM at 30 registers
 
 struct ScanArgs {
   const int8_t* codes;
@@ -252,12 +252,12 @@ __device__ __forceinline__ void mma_s8(int (&d)[4], const uint32_t (&a)[4], uint
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(0));
 }
 
-__global__ void __launch_bounds__(kScanThreads) qgs_scan_kernel(const ScanArgs a) {
+__global__ void __launch_bounds__(kScanThreads, 8) qgs_scan_kernel(const ScanArgs a) {
   const int kv = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int gid = lane >> 2, tig = lane & 3;
   const int n = __ldg(a.n_dev);
-  __shared__ __align__(128) int8_t sbuf[kTilesPerCta * kTile * kRQ];  // the CTA's codes chunk (32 KB)
+  __shared__ __align__(128) int8_t sbuf[kTilesPerCta * kTile * kRQ];  // the CTA's codes chunk (24 KB)
   __shared__ __align__(8) uint64_t mbar[kTilesPerCta];  // one per 256-token tile of the chunk
   __shared__ int8_t limb[kG][4][kRQ];  // [head][limb][j]
   __shared__ int sS[kG];
