@@ -825,7 +825,8 @@ __device__ __forceinline__ void topq_keys_regs(const TsRow& w, int cs, int nmem,
 // pair of index complements.
 template <bool FILTER>
 __device__ __forceinline__ void ts_best2(const uint16_t* kb, int idx0, int nmem, int nj, int j_lo, int j_hi,
-                                         const uint32_t (&g)[2], uint32_t below, uint32_t& m1, uint32_t& m2) {
+                                         uint32_t (&g)[2], const TsRow& w, const int (&gt)[2], int lane,
+                                         uint32_t below, uint32_t& m1, uint32_t& m2) {
   m1 = 0u;
   m2 = 0u;
   auto take = [&](uint32_t c) {
@@ -858,6 +859,11 @@ __device__ __forceinline__ void ts_best2(const uint16_t* kb, int idx0, int nmem,
     take(__byte_perm(x.y, l23, 0x3276));
   }
   for (int j = max(j_hi, j_lo); j < nj; ++j) checked(j);
+  if (!FILTER) {  // the generated candidates' words, from list entries loaded before the member pass
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      g[h] = gt[h] >= 0 ? (ts_key_at(w, gt[h]) << 16) | (uint32_t)(0xffff - (nmem + lane + 32 * h)) : 0u;
+  }
 #pragma unroll
   for (int h = 0; h < 2; ++h) take(g[h]);
 }
@@ -871,13 +877,14 @@ __device__ __forceinline__ void topq_keys_stream(const TsRow& w, int cs, int nme
   const int j_lo = o > 0 ? 1 : 0;                    // first word inside the cluster for every lane
   const int j_hi = (nmem + o) >> 7;                  // words [j_lo, j_hi) lie inside for every lane
   uint32_t g[2];
+  int gt[2];  // generated positions of this lane's candidates, loaded now, used after the member pass
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     const int gi = lane + 32 * h;
-    g[h] = gi < ngen ? (ts_key_at(w, rec[gi]) << 16) | (uint32_t)(0xffff - (nmem + gi)) : 0u;
+    gt[h] = gi < ngen ? rec[gi] : -1;
   }
   uint32_t m1, m2;
-  ts_best2<false>(kb, idx0, nmem, nj, j_lo, j_hi, g, 0u, m1, m2);
+  ts_best2<false>(kb, idx0, nmem, nj, j_lo, j_hi, g, w, gt, lane, 0u, m1, m2);
   bool have2 = true;  // m2 is this lane's second best
   int my_idx = 0x7fffffff;
   for (int k = 0; k < q; ++k) {
@@ -888,7 +895,7 @@ __device__ __forceinline__ void topq_keys_stream(const TsRow& w, int cs, int nme
         m1 = m2;
         have2 = false;
       } else {  // re-read below the value just taken
-        ts_best2<true>(kb, idx0, nmem, nj, j_lo, j_hi, g, wm, m1, m2);
+        ts_best2<true>(kb, idx0, nmem, nj, j_lo, j_hi, g, w, gt, lane, wm, m1, m2);
         have2 = true;
       }
     }
@@ -1230,8 +1237,8 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
 // key them from the staged score row of item i + 1; kTpKeyFirst warps do the same in the other
 // order.  So keying and selection run side by side, and the warps that finish one job early help
 // with the other.  One CTA barrier per item; after it the score row of item i + 2 is
-// fetched into the freed buffer while item i + 1 is selected.  Keys of generated positions are read
-// from the score row in global memory (at most 64 per cluster on the register path).
+// fetched into the freed buffer while item i + 1 is selected.  Keys of generated positions [n0, n)
+// are keyed too, into the key buffer's slots past the members.
 constexpr int kTpThreads = 768;
 constexpr int kTpWarps = kTpThreads / 32;
 constexpr int kTpU = 8;  // 16-byte member vectors per lane in one keying chunk
@@ -1282,6 +1289,11 @@ __global__ void __launch_bounds__(kTpThreads, 1) topq_pipe_kernel(const TopqArgs
       if (vb >= nvec) break;
       ts_key_vecs<kTpU>(mrow - mo, mem_end, vb + lane, 32, nvec, s_spill, lim, kbuf);
     }
+    // keys of the generated positions [n0, n) in the slots past the members' last 4-key vector (every
+    // warp keys its share)
+    const int gbase = (mo + max(n0, m_hi) + 3) & ~3;
+    const int gcnt = max(0, min(nsp - n0, key_cap - gbase));
+    for (int g = warp * 32 + lane; g < gcnt; g += kTpThreads) kbuf[gbase + g] = (uint16_t)ukey16(s_spill[n0 + g]);
   };
   // winners of an item: CSR slots / generated positions -> positions (the CTA's last warps)
   auto winners_out = [&](int row, int lo, int hi, const int* s_win) {
@@ -1339,7 +1351,10 @@ __global__ void __launch_bounds__(kTpThreads, 1) topq_pipe_kernel(const TopqArgs
     // ---- this item's clusters
     const int32_t* mrow = mrow_of(r);
     const int mo = mo_of(mrow);
-    const TsRow w{s_key0 + cur * key_cap + mo, nullptr, a.scores + (int64_t)r * a.sw, mrow, n0, nsp, 0, mo};
+    const int gbase = (mo + max(n0, m.cs[c_hi - 1] + m.cl[c_hi - 1]) + 3) & ~3;  // generated keys, as keyed
+    const int gcnt = max(0, min(nsp - n0, key_cap - gbase));
+    uint16_t* kcur = s_key0 + cur * key_cap;
+    const TsRow w{kcur + mo, kcur + gbase, a.scores + (int64_t)r * a.sw, mrow, n0, nsp, gcnt, mo};
     auto key_next = [&]() {
       if (nwi < W) {
         if (nbytes != 0 && !mbar_wait(bar, (uint32_t)((it + 1) & 1))) fail = true;
