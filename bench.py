@@ -270,13 +270,15 @@ class StageGraphStep(GraphStep):
 
 
 def in_graph_profile(m, Mth, n0, dev, qs, nks, nvs, reps):
-    """Per-kernel milliseconds inside the step graph (mean over `reps` replays, after 3 untimed)."""
+    """Per-kernel milliseconds inside the step graph (mean over `reps` replays, after 3 untimed).  Each
+    replay decodes the next of the workload's steps (its own query and new token), as the timed steps do:
+    one token appended over and over would pile up in one cluster and change the quotas."""
     sg = StageGraphStep(m, Mth, n0, dev)
-    sg.q_in.copy_(qs[0])
-    sg.k_in.copy_(nks[0])
-    sg.v_in.copy_(nvs[0])
     tot = [0.0] * len(sg.NAMES)
     for i in range(reps + 3):
+        sg.q_in.copy_(qs[i % qs.shape[0]])
+        sg.k_in.copy_(nks[i % nks.shape[0]])
+        sg.v_in.copy_(nvs[i % nvs.shape[0]])
         sg.replay()
         torch.cuda.synchronize()
         if i >= 3:
