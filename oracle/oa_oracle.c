@@ -241,7 +241,9 @@ float oro_expf(float x) {
   if (x == -INFINITY) return 0.0f;
   return (float)oro_exp_d((double)x);
 }
-float oro_erff(float x) { return (float)oro_erf_d((double)x); }
+/* From x = 4 on the series rounds to 1 in fp32 (erf(x) > 1 - 1.6e-8, the series is accurate to about
+ * 1e-14, and the fp32 midpoint below 1 is 1 - 3e-8): both implementations skip it there. */
+float oro_erff(float x) { return x >= 4.0f ? 1.0f : (float)oro_erf_d((double)x); }
 
 /* ------------------------------------------------------------------ decode: index update */
 /* New token at position pos of every request: QGS code (per KV head), nearest QGC centroid (per

@@ -276,3 +276,20 @@ def test_index_update_against_float64():
         if cnt < rmax:
             assert st["reclist"][0, h, cid, cnt] == pos
         np.testing.assert_array_equal(st["reclist"][0, h, others], snap["reclist"][0, h, others])
+
+
+def test_erf_series_rounds_to_one_from_four():
+    """The fp32 erf skips its double series from x = 4 on: the series rounded to fp32 is 1 there.
+    Checked on every fp32 value in [4, 4.01] and on a grid up to the series' own cutoff at 6."""
+    import ctypes
+    lib = O.lib()
+    lib.oro_erf_d.restype = ctypes.c_double
+    lib.oro_erf_d.argtypes = [ctypes.c_double]
+    lo = np.float32(4.0)
+    dense = lo + np.arange(0, 40000, dtype=np.float32) * np.spacing(lo)  # every float from 4 upward
+    grid = np.linspace(4.0, 6.0, 20001, dtype=np.float32)
+    for x in np.concatenate([dense, grid]):
+        assert np.float32(lib.oro_erf_d(float(x))) == np.float32(1.0), float(x)
+        assert lib.oro_erff(float(x)) == 1.0
+    # and the series is still used just below 4
+    assert lib.oro_erff(3.5) < 1.0
