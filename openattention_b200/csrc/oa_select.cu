@@ -490,9 +490,14 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
   const int kt2 = min(2 * a.k_top, ntv);
   const float* tm = a.tmax + (int64_t)r * a.tm_stride;
   uint16_t* srw = a.scores + (int64_t)r * a.sw;
+  uint32_t low16 = 0u;  // the OR of the maxima's low 16 bits
   {  // tile keys: the row's maxima with 16-byte loads, all of a lane's loads issued before its stores
     const int h = min(ntv, (int)((4u - ((uint32_t)(reinterpret_cast<uintptr_t>(tm) >> 2) & 3u)) & 3u));
-    if (lane < h) tkey[lane] = fkey(tm[lane]);
+    if (lane < h) {
+      const float x = tm[lane];
+      low16 |= __float_as_uint(x);
+      tkey[lane] = fkey(x);
+    }
     const int nv4 = (ntv - h) >> 2;
     const float4* tm4 = reinterpret_cast<const float4*>(tm + h);  // 16-byte aligned
     constexpr int kU = 8;
@@ -508,6 +513,7 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
         const int vi = v0 + 32 * u;
         if (vi < nv4) {
           uint32_t* t4 = tkey + h + 4 * vi;
+          low16 |= __float_as_uint(x[u].x) | __float_as_uint(x[u].y) | __float_as_uint(x[u].z) | __float_as_uint(x[u].w);
           t4[0] = fkey(x[u].x);
           t4[1] = fkey(x[u].y);
           t4[2] = fkey(x[u].z);
@@ -515,13 +521,32 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
         }
       }
     }
-    for (int i = h + 4 * nv4 + lane; i < ntv; i += 32) tkey[i] = fkey(tm[i]);
+    for (int i = h + 4 * nv4 + lane; i < ntv; i += 32) {
+      const float x = tm[i];
+      low16 |= __float_as_uint(x);
+      tkey[i] = fkey(x);
+    }
   }
   __syncwarp();
-  // (1) tiles: threshold + sort when it applies, else the radix select
+  // every tile maximum a bf16 value (the scan's are): the keys' low halves are then 0 (positive) or
+  // 0xffff (negative) and carry no order, so the tiles can be picked on 32-bit words
+  const bool tiles16 = __all_sync(0xffffffffu, (low16 & 0xffffu) == 0u) && ntv <= 0xffff;
+  // (1) tiles: threshold + sort when it applies (on 32-bit words when the keys allow), else the radix select
   uint64_t srt[2], kth;
+  uint32_t srt32[2], kth32;
+  uint32_t* s_w32 = reinterpret_cast<uint32_t*>(s_w64[warp]);
   auto tword = [&](int i) -> uint64_t { return ((uint64_t)tkey[i] << 32) | (uint64_t)(0xffffffffu - (uint32_t)i); };
-  if (warp_topk_sorted(ntv, kt2, tword, s_w64[warp], srt, kth)) {
+  auto tword32 = [&](int i) -> uint32_t { return (tkey[i] & 0xffff0000u) | (uint32_t)(0xffff - i); };
+  if (tiles16 && warp_topk_sorted32(ntv, kt2, tword32, s_w32, srt32, kth32)) {
+    int taken = 0;
+    for (int i0 = 0; i0 < ntv; i0 += 32) {  // the kt2 tiles with word >= kth, in ascending tile order
+      const int i = i0 + lane;
+      const bool take = i < ntv && tword32(i) >= kth32;
+      const unsigned bt = __ballot_sync(0xffffffffu, take);
+      if (take) tiles[taken + __popc(bt & ((1u << lane) - 1u))] = i;
+      taken += __popc(bt);
+    }
+  } else if (warp_topk_sorted(ntv, kt2, tword, s_w64[warp], srt, kth)) {
     int taken = 0;
     for (int i0 = 0; i0 < ntv; i0 += 32) {  // the kt2 tiles with word >= kth, in ascending tile order
       const int i = i0 + lane;
@@ -581,19 +606,20 @@ __global__ void __launch_bounds__(kSelWarps * 32) qgs_select_kernel(const Select
     k = ckey[i];
     v = k != 0u;
   };
-  // candidate i is tile tiles[i >> 5], offset i & 31: ascending i is ascending position
-  auto cword = [&](int i) -> uint64_t {
+  // candidate i is tile tiles[i >> 5], offset i & 31: ascending i is ascending position; 16-bit keys
+  // and i < 4096, so (key << 16) | (0xffff - i) orders them as the reference does
+  auto cword = [&](int i) -> uint32_t {
     const uint32_t k = ckey[i];
-    return k ? ((uint64_t)k << 32) | (uint64_t)(0xffffffffu - (uint32_t)i) : 0ull;
+    return k ? (k << 16) | (uint32_t)(0xffff - i) : 0u;
   };
   int32_t* outp = a.sel + (int64_t)r * (a.ns + a.nl + a.k_top);
-  if (warp_topk_sorted(m, a.k_top, cword, s_w64[warp], srt, kth)) {
+  if (warp_topk_sorted32(m, a.k_top, cword, s_w32, srt32, kth32)) {
     // the k winners, already in rank order (score desc, position asc)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int e = lane + 32 * h;
       if (e < a.k_top) {
-        const int i = (int)(0xffffffffu - (uint32_t)srt[h]);
+        const int i = 0xffff - (int)(srt32[h] & 0xffffu);
         s_pos[warp][e] = tiles[i >> 5] * kMaxTile + (i & (kMaxTile - 1));
       }
     }

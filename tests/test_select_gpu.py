@@ -43,6 +43,14 @@ def test_select_matches_oracle(kind, k_top):
     _check_select(kind, k_top, 64, 4101, 4160)
 
 
+@pytest.mark.parametrize("kind", ["random", "equal", "skewed"])
+@pytest.mark.parametrize("k_top", [9, 40])
+def test_select_tile_maxima_not_bf16(kind, k_top):
+    """Tile maxima that are not bf16 values (a caller's own) take the 64-bit tile words; the scan's
+    are bf16 values and take the 32-bit ones.  Both pick the same tiles."""
+    _check_select(kind, k_top, 64, 4101, 4160, nudge_tile_max=True)
+
+
 @pytest.mark.parametrize("n,Lmax,k_top", [(65536, 65600, 20), (131072, 131104, 40)])
 def test_select_long_rows_matches_oracle(n, Lmax, k_top):
     """Rows of 64K and 128K positions: the per-warp tile keys then take tens of KB of shared memory,
@@ -50,7 +58,7 @@ def test_select_long_rows_matches_oracle(n, Lmax, k_top):
     _check_select("random", k_top, 8, n, Lmax)
 
 
-def _check_select(kind, k_top, R, n, Lmax):
+def _check_select(kind, k_top, R, n, Lmax, nudge_tile_max=False):
     ns, nl = 3, 3
     SW = S.padded_len(Lmax)
     NT = (Lmax + 31) // 32
@@ -59,6 +67,8 @@ def _check_select(kind, k_top, R, n, Lmax):
     s[:, :ns] = NEG
     s[:, n - nl:n] = NEG
     tmax = O.bf16_to_f32(s[:, :NT * 32].reshape(R, NT, 32)).max(axis=2).astype(np.float32)
+    if nudge_tile_max:  # one ulp up: the same order, but no longer bf16 values (the 64-bit tile words)
+        tmax = np.nextafter(tmax, np.float32(np.inf)).astype(np.float32)
     ref = s.copy()
     sel_ref = O.select(ref, n, ns, nl, k_top)
     scores = O.from_bits(s).cuda()
