@@ -848,7 +848,7 @@ __device__ __forceinline__ void ts_best2(const uint16_t* kb, int idx0, int nmem,
   // the packed subtraction never borrows across the halves)
   const uint32_t b0 = (uint32_t)(0xffff - (idx0 + 128 * j_lo)), b2 = b0 - 2u;
   const uint32_t p01 = (b0 & 0xffffu) | ((b0 - 1u) << 16), p23 = (b2 & 0xffffu) | ((b2 - 1u) << 16);
-#pragma unroll 2
+#pragma unroll 1
   for (int j = j_lo; j < j_hi; ++j) {
     const uint2 x = *reinterpret_cast<const uint2*>(kb + 128 * j);
     const uint32_t dj = (uint32_t)(128 * (j - j_lo)) * 0x10001u;
