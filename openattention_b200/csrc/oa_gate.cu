@@ -720,15 +720,16 @@ __global__ void __launch_bounds__(kTqThreads, 3) topq_kernel(const TopqArgs a) {
 }
 
 // ------------------------------------------------------------------------ top-q, streamed member keys
-// Persistent variant of top-q for rows that fit in shared memory (about 49K positions): one CTA of
-// 16 warps per SM walks rows r = blockIdx.x, + gridDim.x, ...  Per row:
+// Persistent variant of top-q with one key buffer, for rows of about 34K to 47K positions (shorter
+// rows take topq_pipe_kernel): one CTA of 32 warps per SM walks rows r = blockIdx.x, + gridDim.x, ...
+// Per row:
 //   phase 1: the whole CSR member list of the row is streamed with 16-byte loads (every thread has
 //            several in flight) and turned into a contiguous array of 16-bit score keys in CSR order
 //            (the score row itself was staged by a bulk copy); keys of generated positions [n0, n)
 //            are staged too;
 //   phase 2: warps take the clusters with q > 0 and select from contiguous shared-memory keys
-//            (register path: (key, list index) words, q rounds of warp maximum; radix path as in
-//            topq_kernel); winners are recorded in shared memory as CSR slots (or positions of
+//            (streamed path: (key, list index) words, q rounds of warp maximum; radix path for
+//            larger quotas); winners are recorded in shared memory as CSR slots (or positions of
 //            generated tokens) and turned into positions by one parallel pass over the row.
 // While phase 2 runs, the next row's score row is already being copied into the freed buffer.
 constexpr int kTsThreads = 1024;
@@ -819,7 +820,7 @@ __device__ __forceinline__ void topq_keys_regs(const TsRow& w, int cs, int nmem,
 // The same selection without a register copy of the cluster: each lane streams its keys (four per
 // 8-byte word, words 128 keys apart) from shared memory once to find its best two, and the lane that
 // gives up its second best re-reads its keys below the value just taken.  Only (m1, m2) live in
-// registers, so the kernel runs 32 warps per SM and any cluster size takes this path.  Words whose
+// registers, so the kernels run 24 or 32 warps per SM and any cluster size takes this path.  Words whose
 // four keys all lie inside the cluster for every lane (all but the first and the last one or two)
 // skip the bounds tests and build their (key, 0xffff - index) words with byte permutes from a packed
 // pair of index complements.
