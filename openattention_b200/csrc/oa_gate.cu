@@ -1234,7 +1234,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
 // The persistent top-q with each work item's keying overlapped with the previous item's selection.
 // Shared memory holds one staged score row, two key buffers, two winner lists and three metadata
 // sets.  In iteration i most warps first take clusters of item i until none is left, then take
-// chunks of item i + 1's member list (32 x kTpU vectors, 1024 members) from a second counter and
+// chunks of item i + 1's member list (32 x kTpU vectors, 512 members) from a second counter and
 // key them from the staged score row of item i + 1; kTpKeyFirst warps do the same in the other
 // order.  So keying and selection run side by side, and the warps that finish one job early help
 // with the other.  One CTA barrier per item; after it the score row of item i + 2 is
@@ -1242,7 +1242,7 @@ __global__ void __launch_bounds__(kTsThreads, 1) topq_stream_kernel(const TopqAr
 // are keyed too, into the key buffer's slots past the members.
 constexpr int kTpThreads = 768;
 constexpr int kTpWarps = kTpThreads / 32;
-constexpr int kTpU = 8;  // 16-byte member vectors per lane in one keying chunk
+constexpr int kTpU = 4;  // 16-byte member vectors per lane in one keying chunk (512 members)
 // Warps that key the next item before selecting (the rest select first).
 constexpr int kTpKeyFirst = 9;
 
