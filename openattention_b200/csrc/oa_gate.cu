@@ -1378,7 +1378,7 @@ __global__ void __launch_bounds__(kTpThreads, 1) topq_pipe_kernel(const TopqArgs
 }
 
 // ------------------------------------------------------------------------ top-q, long rows
-// For rows whose score row does not fit shared memory (beyond about 49K positions) top-q runs in two
+// For rows whose score row does not fit shared memory (beyond about 47K positions) top-q runs in two
 // kernels over a caller workspace of R x ckw 16-bit keys:
 //   topq_permute_kernel: one CTA per row stages the score row in chunks of kPmChunk positions (bulk
 //     copies; 64 KB chunks let two CTAs share an SM, one staging while the other walks); for each chunk, warps take clusters and key the run of the cluster's members whose
