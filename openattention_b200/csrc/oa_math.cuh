@@ -141,7 +141,7 @@ __device__ __noinline__ double ln_d(double x) {  // x > 0 and normal
   const double s = __ddiv_rn(__dsub_rn(m, 1.0), __dadd_rn(m, 1.0));
   const double s2 = __dmul_rn(s, s);
   double term = s, sum = s;
-#pragma unroll 1
+#pragma unroll
   for (int k = 1; k <= 13; ++k) {
     term = __dmul_rn(term, s2);
     sum = __dadd_rn(sum, __dmul_rn(term, kInvOdd[k]));
@@ -157,7 +157,7 @@ __device__ __noinline__ double exp_d(double x) {
   const double t2 = __dmul_rn(k, 1.90821492927058770002e-10);
   const double r = __dsub_rn(__dsub_rn(x, t1), t2);
   double p = 1.0, term = 1.0;
-#pragma unroll 1
+#pragma unroll
   for (int i = 1; i <= 17; ++i) {
     term = __dmul_rn(term, r);
     term = __dmul_rn(term, kInvInt[i]);
@@ -173,7 +173,7 @@ __device__ __noinline__ double erf_d(double x) {  // x >= 0
   const double x2 = __dmul_rn(x, x);
   const double tx2 = __dmul_rn(2.0, x2);
   double term = x, sum = x;
-#pragma unroll 1
+#pragma unroll 4
   for (int n = 1; n < 400; ++n) {
     term = __dmul_rn(term, tx2);
     term = __dmul_rn(term, kInvOdd[n]);
