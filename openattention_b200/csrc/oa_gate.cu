@@ -720,7 +720,7 @@ __global__ void __launch_bounds__(kTqThreads, 3) topq_kernel(const TopqArgs a) {
 }
 
 // ------------------------------------------------------------------------ top-q, streamed member keys
-// Persistent variant of top-q with one key buffer, for rows of about 34K to 47K positions (shorter
+// Persistent variant of top-q with one key buffer, for rows of about 35K to 47K positions (shorter
 // rows take topq_pipe_kernel): one CTA of 32 warps per SM walks rows r = blockIdx.x, + gridDim.x, ...
 // Per row:
 //   phase 1: the whole CSR member list of the row is streamed with 16-byte loads (every thread has
@@ -2336,7 +2336,9 @@ int tp_key_cap(int64_t Lmax) { return (int)(((Lmax + 7) & ~7ll) + 136); }  // re
 size_t tp_smem_bytes(int64_t Lmax, int64_t E, int64_t C) {  // topq_pipe_kernel: score row, 2 keys, 2 winners, 3 metas
   return (size_t)((Lmax + 7) & ~7ll) * 2 + (size_t)tp_key_cap(Lmax) * 2 * 2 + (size_t)E * 4 * 2 + (size_t)(6 * C + 1) * 4 * 3;
 }
-bool tp_fits(int64_t Lmax, int64_t E, int64_t C) { return tp_smem_bytes(Lmax, E, C) <= 208 * 1024; }
+// 214 KB of dynamic shared memory with the kernel's 12.4 KB of static arrays stays under the 227 KB a
+// CTA can have (rows up to about 35.3K positions at C = 64, E = 216)
+bool tp_fits(int64_t Lmax, int64_t E, int64_t C) { return tp_smem_bytes(Lmax, E, C) <= 214 * 1024; }
 int64_t ck_stride(int64_t Lmax) { return (Lmax + 7) & ~7ll; }
 }  // namespace
 }  // namespace oa

@@ -113,10 +113,12 @@ def test_topq_matches_oracle_with_ties(golden_dir, kind):
     assert np.array_equal(exp_idx.cpu().numpy(), exp_ref)
 
 
-@pytest.mark.parametrize("n0,use_ws", [(65536, True), (65536, False), (40000, False), (32768, False)])
+@pytest.mark.parametrize("n0,use_ws", [(65536, True), (65536, False), (40000, False), (35300, False),
+                                       (32768, False)])
 def test_topq_long_rows_matches_oracle(n0, use_ws):
-    """Top-q at each row length's kernel, quotas up to 40 (past the register path's 32): 32K positions
-    (the pipelined kernel, two key buffers), 40K (one key buffer), and rows too long for shared memory
+    """Top-q at each row length's kernel, quotas up to 40 (past the register path's 32): 32K and 35.3K
+    positions (the pipelined kernel, two key buffers; 35.3K is near the most its shared memory holds),
+    40K (one key buffer), and rows too long for shared memory
     (64K) with the workspace (keys permuted into CSR order, then selected from contiguous keys) and
     without it (keys read from global memory)."""
     import types
