@@ -203,6 +203,12 @@ int oa_topq(const void* scores, int64_t score_stride, int64_t R, int64_t Lmax, i
 /* Bytes of workspace oa_topq uses for these sizes (0 when its rows fit the shared-memory kernel). */
 size_t oa_topq_workspace_bytes(int64_t R, int64_t Lmax, int64_t E);
 
+/* Which oa_topq kernel rows of Lmax positions take: 0 the pipelined one (two key buffers in shared
+ * memory, the next row keyed while the current one is selected; up to about 35K positions at C = 64,
+ * E = 216), 1 the one-buffer one (up to about 47K), 2 the long-row kernels (workspace, or keys read
+ * from global memory). */
+int oa_topq_variant(int64_t Lmax, int64_t E, int64_t C);
+
 /* Residual proxies: per (row, cluster) the pooled sums minus every token read (sel in order, then
  * the cluster's exp segment), n' = nt - quota, kbar' / vbar' = bf16(sums / max(n', 1)) (R, C, 128),
  * log_n = ln max(n', 1) if n' > 0.5 else -inf (R, C) fp32.  Replaces _k_resid_scatter +

@@ -40,6 +40,7 @@ SIGNATURES = {
     "oa_errorgate_waterfill": (I32, [P, I64, P, I64, I64, I64, I64, P, P, I64, P, P, P, F32, P, P, P, P, P, P]),
     "oa_topq": (I32, [P, I64, I64, I64, I64, P, P, P, P, P, P, I32, P, I64, P, P, P, P, P, SZ, P]),
     "oa_topq_workspace_bytes": (SZ, [I64, I64, I64]),
+    "oa_topq_variant": (I32, [I64, I64, I64]),
     "oa_residual": (I32, [P, P, I64, I64, I64, I64, P, P, I64, P, I64, P, P, P, P, P, P, P, P, P]),
     "oa_residual_flash": (I32, [P, I64, P, P, I64, I64, I64, I64, P, P, I64, P, I64, P, P, P, P, P, P, P, P, P,
                                 I64, I32, F32, P, P]),

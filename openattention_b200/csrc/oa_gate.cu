@@ -2343,6 +2343,11 @@ int64_t ck_stride(int64_t Lmax) { return (Lmax + 7) & ~7ll; }
 }  // namespace
 }  // namespace oa
 
+extern "C" int oa_topq_variant(int64_t Lmax, int64_t E, int64_t C) {
+  if (oa::tp_fits(Lmax, E, C)) return 0;
+  return oa::ts_fits(Lmax, E) ? 1 : 2;
+}
+
 extern "C" size_t oa_topq_workspace_bytes(int64_t R, int64_t Lmax, int64_t E) {
   if (R <= 0 || Lmax <= 0 || oa::ts_fits(Lmax, E)) return 0;
   return (size_t)(R * oa::ck_stride(Lmax) + 1024) * sizeof(uint16_t);

@@ -145,6 +145,12 @@ def topq_workspace(R: int, Lmax: int, E: int, device) -> torch.Tensor | None:
     return torch.empty(nbytes, dtype=torch.uint8, device=device) if nbytes else None
 
 
+def topq_variant(Lmax: int, E: int, C: int) -> int:
+    """The top-q kernel rows of Lmax positions take: 0 pipelined (two key buffers), 1 one key buffer,
+    2 the long-row kernels."""
+    return int(_lib.load().oa_topq_variant(Lmax, E, C))
+
+
 def topq(scores, st, quota, E, n_dev, n0_dev, exp_idx, status=None, workspace=None):
     R = scores.shape[0]
     B, _, Lmax = st["asg"].shape

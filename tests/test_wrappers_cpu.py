@@ -75,3 +75,21 @@ def test_flash_entries_reject_host_and_foreign_tensors():
         F._same_device(cuda0, sel_idx=sel)
     with pytest.raises(RuntimeError, match="exp_idx must be a tensor on cuda:0 .*list"):
         F._same_device(cuda0, exp_idx=[1, 2])
+
+
+def test_topq_variant_by_row_length():
+    """oa_topq_variant names the kernel rows of a length take, and the benchmark's default c2 workload
+    (its KV buffer with the warm-up, twice the timed steps and the clock soak's positions) stays on
+    the pipelined one: a longer buffer would measure the one-buffer kernel instead."""
+    import bench
+    from openattention_b200 import selection as S
+    from openattention_b200.geometry import budget
+    C, E = budget(bench.RHO)
+    assert (C, E) == (64, 216)
+    assert S.topq_variant(32768, E, C) == 0
+    assert S.topq_variant(35308, E, C) == 0
+    assert S.topq_variant(40000, E, C) == 1
+    assert S.topq_variant(65536, E, C) == 2
+    steps, warmup = 500, 20  # bench.py's defaults
+    Lmax = bench.N_CTX + (warmup + 2 * steps + 8) + bench.CLOCK_SOAK_RUN + 16
+    assert S.topq_variant(Lmax, E, C) == 0, Lmax
